@@ -1,0 +1,481 @@
+/*
+ * CPU oracle for the int4 decode hot path — TEST INFRASTRUCTURE ONLY.
+ *
+ * This file restates, in plain C, the arithmetic that the reference execution
+ * provider (justinchuby/onnxruntime-mlx) maps onto ONNX Runtime's CPU EP
+ * semantics for three operators:
+ *
+ *   - com.microsoft MatMulNBits         (rust/src/ops/quant.rs:986-1130)
+ *   - com.microsoft GroupQueryAttention  (rust/src/ops/attention.rs:556-952)
+ *   - SimplifiedLayerNormalization / RMSNormalization /
+ *     SkipSimplifiedLayerNormalization    (rust/src/ops/norm.rs:163-246)
+ *
+ * It is the checker for the CUDA kernels (tests, smoke(), and the timed CPU
+ * baseline of bench.py).  The product library never links or calls it.
+ *
+ * Numeric conventions (chosen to model ORT CPU, the reference's parity target):
+ *   - Dequantised weight = (float)(q - zp) * (float)scale, one fp32 multiply.
+ *     This is the bit-exact target for every dequantising kernel.
+ *   - Dot products / reductions accumulate in double; the result is rounded
+ *     once to the I/O dtype.
+ *   - fp16 / bf16 conversions use IEEE round-to-nearest-even.
+ * The reference has no stored golden vectors for this path; the oracle is
+ * pinned against fixtures generated from the reference's own test builders and
+ * numpy references (tests/golden/gen_golden.py).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ONNX TensorProto element types (same values as ONNXTensorElementDataType). */
+enum { OR_F32 = 1, OR_U8 = 2, OR_I32 = 6, OR_F16 = 10, OR_BF16 = 16 };
+
+enum {
+  OR_OK = 0,
+  OR_EINVAL = 1,   /* bad argument / unsupported form */
+  OR_ERANGE = 2    /* position or size outside the caches */
+};
+
+/* ---- fp16 / bf16 <-> fp32 (round to nearest even) ------------------------ */
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+float oracle_half_to_float(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  if (exp == 0) {
+    if (man == 0) return u2f(sign);
+    /* subnormal: value = man * 2^-24 */
+    float v = (float)man * 5.9604644775390625e-08f;
+    return sign ? -v : v;
+  }
+  if (exp == 31) return u2f(sign | 0x7f800000u | (man << 13));
+  return u2f(sign | ((exp + 112u) << 23) | (man << 13));
+}
+
+uint16_t oracle_float_to_half(float f) {
+  uint32_t u = f2u(f);
+  uint32_t sign = (u >> 16) & 0x8000u;
+  uint32_t a = u & 0x7fffffffu;
+  if (a >= 0x7f800000u) /* inf or nan */
+    return (uint16_t)(sign | 0x7c00u | (a > 0x7f800000u ? 0x200u : 0u));
+  if (a >= 0x477ff000u) /* rounds to >= 65520 -> inf */
+    return (uint16_t)(sign | 0x7c00u);
+  if (a < 0x38800000u) { /* result is subnormal or zero in fp16 */
+    /* value / 2^-24, rounded to nearest even integer */
+    float v = u2f(a) * 16777216.0f;
+    float r = nearbyintf(v); /* default rounding mode is RNE */
+    return (uint16_t)(sign | (uint32_t)r);
+  }
+  /* normal: rebias exponent, round mantissa from 23 to 10 bits */
+  uint32_t mant_odd = (a >> 13) & 1u;
+  a += 0xfffu + mant_odd;
+  a -= (112u << 23);
+  return (uint16_t)(sign | (a >> 13));
+}
+
+float oracle_bf16_to_float(uint16_t b) { return u2f((uint32_t)b << 16); }
+
+uint16_t oracle_float_to_bf16(float f) {
+  uint32_t u = f2u(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+  uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7fffu + lsb;
+  return (uint16_t)(u >> 16);
+}
+
+static inline float load_f(const void* p, int64_t i, int dt) {
+  switch (dt) {
+    case OR_F32: return ((const float*)p)[i];
+    case OR_F16: return oracle_half_to_float(((const uint16_t*)p)[i]);
+    case OR_BF16: return oracle_bf16_to_float(((const uint16_t*)p)[i]);
+  }
+  return NAN;
+}
+
+static inline void store_f(void* p, int64_t i, int dt, double v) {
+  float f = (float)v;
+  switch (dt) {
+    case OR_F32: ((float*)p)[i] = f; break;
+    case OR_F16: ((uint16_t*)p)[i] = oracle_float_to_half(f); break;
+    case OR_BF16: ((uint16_t*)p)[i] = oracle_float_to_bf16(f); break;
+  }
+}
+
+/* Round a float through the I/O dtype (identity for fp32). */
+static inline float round_to(float v, int dt) {
+  switch (dt) {
+    case OR_F16: return oracle_half_to_float(oracle_float_to_half(v));
+    case OR_BF16: return oracle_bf16_to_float(oracle_float_to_bf16(v));
+  }
+  return v;
+}
+
+static int is_float_dt(int dt) { return dt == OR_F32 || dt == OR_F16 || dt == OR_BF16; }
+
+static void set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ---- MatMulNBits ----------------------------------------------------------
+ * Layout (ORT contrib op; the reference's accepted forms, quant.rs:1655-1711):
+ *   B       uint8 [N, nblocks, block*bits/8], values packed low-to-high along K
+ *           (int4: low nibble = even k; quant.rs:675-698)
+ *   scales  [N * nblocks], same float dtype as A
+ *   zp      optional uint8; int4: [N, ceil(nblocks/2)] packed, low nibble =
+ *           even block (quant.rs:906-919); int8: [N, nblocks].
+ *           Absent -> 2^(bits-1) (quant.rs:821, 1107).
+ *   K not a multiple of block: the tail of the last block is padding and the
+ *   activation is zero-padded (quant.rs:1034-1039, 1074).
+ */
+
+static inline int mnb_q(const uint8_t* B, int64_t n, int64_t k, int64_t nblocks,
+                        int bits, int block) {
+  int64_t blob = (int64_t)block * bits / 8;
+  int64_t blk = k / block, within = k % block;
+  if (bits == 4) {
+    uint8_t byte = B[(n * nblocks + blk) * blob + within / 2];
+    return (within & 1) ? (byte >> 4) : (byte & 0x0f);
+  }
+  return B[(n * nblocks + blk) * blob + within];
+}
+
+static inline int mnb_zp(const uint8_t* zp, int64_t n, int64_t blk, int64_t nblocks,
+                         int bits) {
+  if (!zp) return 1 << (bits - 1);
+  if (bits == 4) {
+    int64_t cols = (nblocks + 1) / 2;
+    uint8_t byte = zp[n * cols + blk / 2];
+    return (blk & 1) ? (byte >> 4) : (byte & 0x0f);
+  }
+  return zp[n * nblocks + blk];
+}
+
+int oracle_matmulnbits_dequant(const uint8_t* B, const void* scales, int scale_dt,
+                               const uint8_t* zp, int64_t N, int64_t K, int bits,
+                               int block, float* W) {
+  if (!B || !scales || !W || N <= 0 || K <= 0) return OR_EINVAL;
+  if (bits != 4 && bits != 8) return OR_EINVAL;
+  if (block < 16 || (block & (block - 1))) return OR_EINVAL;
+  if (!is_float_dt(scale_dt)) return OR_EINVAL;
+  int64_t nblocks = (K + block - 1) / block;
+  for (int64_t n = 0; n < N; ++n)
+    for (int64_t k = 0; k < K; ++k) {
+      int64_t blk = k / block;
+      float s = load_f(scales, n * nblocks + blk, scale_dt);
+      int d = mnb_q(B, n, k, nblocks, bits, block) - mnb_zp(zp, n, blk, nblocks, bits);
+      W[n * K + k] = (float)d * s;
+    }
+  return OR_OK;
+}
+
+int oracle_matmulnbits(const void* A, const uint8_t* B, const void* scales,
+                       const uint8_t* zp, void* Y, int dt, int64_t M, int64_t N,
+                       int64_t K, int bits, int block, int nthreads) {
+  if (!A || !B || !scales || !Y || M < 0 || N <= 0 || K <= 0) return OR_EINVAL;
+  if (!is_float_dt(dt)) return OR_EINVAL;
+  if (M == 0) return OR_OK;
+  float* W = (float*)malloc((size_t)N * (size_t)K * sizeof(float));
+  float* Af = (float*)malloc((size_t)M * (size_t)K * sizeof(float));
+  if (!W || !Af) { free(W); free(Af); return OR_EINVAL; }
+  int rc = oracle_matmulnbits_dequant(B, scales, dt, zp, N, K, bits, block, W);
+  if (rc) { free(W); free(Af); return rc; }
+  for (int64_t i = 0; i < M * K; ++i) Af[i] = load_f(A, i, dt);
+  set_threads(nthreads);
+#pragma omp parallel for schedule(static) collapse(2)
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t n = 0; n < N; ++n) {
+      const float* a = Af + m * K;
+      const float* w = W + n * K;
+      double acc = 0.0;
+      for (int64_t k = 0; k < K; ++k) acc += (double)a[k] * (double)w[k];
+      store_f(Y, m * N + n, dt, acc);
+    }
+  free(W);
+  free(Af);
+  return OR_OK;
+}
+
+/* ---- RMS norms ------------------------------------------------------------
+ * y = x / sqrt(mean(x^2) + eps) * gamma over the last axis (norm.rs:163-183).
+ * Skip form: r = x + skip; y = rms_norm(r) * gamma; residual output = r
+ * (norm.rs:229-246).  The sum is kept in fp32 for the normalisation and
+ * rounded to the I/O dtype only where it is written out.
+ */
+
+static void rms_row(const float* r, const void* gamma, void* Y, int64_t row,
+                    int64_t hidden, float eps, int dt) {
+  double ss = 0.0;
+  for (int64_t j = 0; j < hidden; ++j) ss += (double)r[j] * (double)r[j];
+  double inv = 1.0 / sqrt(ss / (double)hidden + (double)eps);
+  for (int64_t j = 0; j < hidden; ++j)
+    store_f(Y, row * hidden + j, dt, (double)r[j] * inv * (double)load_f(gamma, j, dt));
+}
+
+int oracle_rms_norm(const void* X, const void* gamma, void* Y, int dt, int64_t rows,
+                    int64_t hidden, float eps, int nthreads) {
+  if (!X || !gamma || !Y || rows < 0 || hidden <= 0 || !is_float_dt(dt)) return OR_EINVAL;
+  set_threads(nthreads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    float* r = (float*)malloc((size_t)hidden * sizeof(float));
+    for (int64_t j = 0; j < hidden; ++j) r[j] = load_f(X, i * hidden + j, dt);
+    rms_row(r, gamma, Y, i, hidden, eps, dt);
+    free(r);
+  }
+  return OR_OK;
+}
+
+int oracle_skip_rms_norm(const void* X, const void* skip, const void* gamma, void* Y,
+                         void* residual_out, int dt, int64_t rows, int64_t hidden,
+                         float eps, int nthreads) {
+  if (!X || !skip || !gamma || !Y || rows < 0 || hidden <= 0 || !is_float_dt(dt))
+    return OR_EINVAL;
+  set_threads(nthreads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    float* r = (float*)malloc((size_t)hidden * sizeof(float));
+    for (int64_t j = 0; j < hidden; ++j) {
+      r[j] = load_f(X, i * hidden + j, dt) + load_f(skip, i * hidden + j, dt);
+      if (residual_out) store_f(residual_out, i * hidden + j, dt, r[j]);
+    }
+    rms_row(r, gamma, Y, i, hidden, eps, dt);
+    free(r);
+  }
+  return OR_OK;
+}
+
+/* ---- GroupQueryAttention --------------------------------------------------
+ * Follows the reference handler (attention.rs:556-952) with ORT CPU's per-batch
+ * sequence lengths:
+ *   past_len_b = seqlens_k[b] + 1 - S          (the reference uses the uniform
+ *                                               total_sequence_length - S,
+ *                                               attention.rs:624-642; equal for
+ *                                               uniform batches)
+ *   query s sits at position past_len_b + s; it attends keys
+ *   j <= past_len_b + s (lower-right causal, attention.rs:537-543) and, with a
+ *   local window w > 0, keys j > past_len_b + s - w.
+ *   RoPE from the cos/sin caches at those positions (attention.rs:417-461):
+ *     non-interleaved: o1 = x1 c - x2 s, o2 = x2 c + x1 s on halves of the
+ *     rotary dims; interleaved: the same on (even, odd) pairs; dims beyond
+ *     2*half pass through.
+ *   Optional per-head RMS norm of q/k (inputs 14/15) before RoPE
+ *   (attention.rs:663-669).
+ *   New K/V rows are written to present at [past_len_b, past_len_b + S)
+ *   (shared buffer in place, attention.rs:893-902; growing concat 903-907).
+ *   softmax(scale * q.k^T + bias) . V, scale = attr or 1/sqrt(D).
+ * Rotated q / k are rounded to the I/O dtype before use, as ORT stores them.
+ */
+
+typedef struct {
+  int64_t batch, seq, num_heads, kv_heads, head_size;
+  int64_t past_cap;    /* axis-2 length of past_key/value (0 = no past) */
+  int64_t present_cap; /* axis-2 length of present_key/value */
+  int64_t max_seq;     /* rows of the cos/sin caches */
+  int64_t rotary_half; /* cos_cache.shape[1] */
+  int32_t do_rotary, interleaved, packed_qkv, shared_buffer;
+  int32_t local_window;   /* <= 0: none */
+  int32_t has_qk_norm;
+  float scale;            /* 0 -> 1/sqrt(D) */
+  float qk_norm_eps;
+  int64_t bias_batch;     /* attention_bias batch dim (0 = absent, 1 = broadcast) */
+  int64_t bias_total;     /* attention_bias last dim */
+} oracle_gqa_params;
+
+static void qk_norm_vec(float* x, int64_t d, const void* w, int dt, float eps) {
+  double ss = 0.0;
+  for (int64_t i = 0; i < d; ++i) ss += (double)x[i] * x[i];
+  double inv = 1.0 / sqrt(ss / (double)d + (double)eps);
+  for (int64_t i = 0; i < d; ++i) x[i] = (float)((double)x[i] * inv * load_f(w, i, dt));
+}
+
+static void rope_vec(float* x, int64_t d, int64_t half, int64_t pos, const void* cos_c,
+                     const void* sin_c, int dt, int interleaved) {
+  float tmp[1024];
+  for (int64_t i = 0; i < d; ++i) tmp[i] = x[i];
+  for (int64_t i = 0; i < half; ++i) {
+    float c = load_f(cos_c, pos * half + i, dt);
+    float s = load_f(sin_c, pos * half + i, dt);
+    if (!interleaved) {
+      float a = tmp[i], b = tmp[i + half];
+      x[i] = a * c - b * s;
+      x[i + half] = b * c + a * s;
+    } else {
+      float a = tmp[2 * i], b = tmp[2 * i + 1];
+      x[2 * i] = a * c - b * s;
+      x[2 * i + 1] = b * c + a * s;
+    }
+  }
+}
+
+int oracle_gqa(const oracle_gqa_params* p, const void* q, const void* k, const void* v,
+               const void* past_k, const void* past_v, const int32_t* seqlens_k,
+               const void* cos_c, const void* sin_c, const void* q_norm_w,
+               const void* k_norm_w, const void* attn_bias, void* out, void* present_k,
+               void* present_v, int dt, int nthreads) {
+  if (!p || !q || !seqlens_k || !out || !present_k || !present_v || !is_float_dt(dt))
+    return OR_EINVAL;
+  const int64_t B = p->batch, S = p->seq, H = p->num_heads, HK = p->kv_heads,
+                D = p->head_size;
+  if (B <= 0 || S <= 0 || H <= 0 || HK <= 0 || D <= 0 || D > 1024 || H % HK) return OR_EINVAL;
+  if (!p->packed_qkv && (!k || !v)) return OR_EINVAL;
+  if (p->do_rotary && (!cos_c || !sin_c || 2 * p->rotary_half > D || p->rotary_half <= 0))
+    return OR_EINVAL;
+  if (p->has_qk_norm && (!q_norm_w || !k_norm_w)) return OR_EINVAL;
+  const int64_t G = H / HK;
+  const int64_t cap = p->present_cap;
+  const int64_t qstride = p->packed_qkv ? (H + 2 * HK) * D : H * D;
+  const int64_t kstride = p->packed_qkv ? qstride : HK * D;
+  const float scale = p->scale != 0.0f ? p->scale : (float)(1.0 / sqrt((double)D));
+
+  for (int64_t b = 0; b < B; ++b) {
+    int64_t past_len = (int64_t)seqlens_k[b] + 1 - S;
+    if (past_len < 0) return OR_ERANGE;
+    if (past_len + S > cap) return OR_ERANGE;
+    if (!p->shared_buffer && past_len > p->past_cap) return OR_ERANGE;
+    if (p->do_rotary && past_len + S > p->max_seq) return OR_ERANGE;
+  }
+
+  /* 1. present = past (when not aliased), then append the new rows. */
+  const int64_t esz = dt == OR_F32 ? 4 : 2;
+  if (!p->shared_buffer) {
+    memset(present_k, 0, (size_t)(B * HK * cap * D * esz));
+    memset(present_v, 0, (size_t)(B * HK * cap * D * esz));
+    if (p->past_cap > 0 && past_k && past_v) {
+      int64_t rows = p->past_cap < cap ? p->past_cap : cap;
+      for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < HK; ++h) {
+          size_t dst = (size_t)(((b * HK + h) * cap) * D * esz);
+          size_t src = (size_t)(((b * HK + h) * p->past_cap) * D * esz);
+          memcpy((char*)present_k + dst, (const char*)past_k + src, (size_t)(rows * D * esz));
+          memcpy((char*)present_v + dst, (const char*)past_v + src, (size_t)(rows * D * esz));
+        }
+    }
+  }
+
+  /* 2. rotate + append new K and V; rotate Q into a scratch buffer. */
+  float* qr = (float*)malloc((size_t)(B * S * H * D) * sizeof(float));
+  if (!qr) return OR_EINVAL;
+  for (int64_t b = 0; b < B; ++b) {
+    int64_t past_len = (int64_t)seqlens_k[b] + 1 - S;
+    for (int64_t s = 0; s < S; ++s) {
+      int64_t pos = past_len + s;
+      float vec[1024];
+      for (int64_t h = 0; h < H; ++h) {
+        for (int64_t i = 0; i < D; ++i) vec[i] = load_f(q, (b * S + s) * qstride + h * D + i, dt);
+        if (p->has_qk_norm) qk_norm_vec(vec, D, q_norm_w, dt, p->qk_norm_eps);
+        if (p->do_rotary)
+          rope_vec(vec, D, p->rotary_half, pos, cos_c, sin_c, dt, p->interleaved);
+        for (int64_t i = 0; i < D; ++i)
+          qr[((b * S + s) * H + h) * D + i] = round_to(vec[i], dt);
+      }
+      for (int64_t h = 0; h < HK; ++h) {
+        const void* ksrc = p->packed_qkv ? q : k;
+        const void* vsrc = p->packed_qkv ? q : v;
+        int64_t koff = p->packed_qkv ? H * D : 0;
+        int64_t voff = p->packed_qkv ? (H + HK) * D : 0;
+        for (int64_t i = 0; i < D; ++i)
+          vec[i] = load_f(ksrc, (b * S + s) * kstride + koff + h * D + i, dt);
+        if (p->has_qk_norm) qk_norm_vec(vec, D, k_norm_w, dt, p->qk_norm_eps);
+        if (p->do_rotary)
+          rope_vec(vec, D, p->rotary_half, pos, cos_c, sin_c, dt, p->interleaved);
+        int64_t row = ((b * HK + h) * cap + pos) * D;
+        for (int64_t i = 0; i < D; ++i) {
+          store_f(present_k, row + i, dt, vec[i]);
+          store_f(present_v, row + i, dt,
+                  load_f(vsrc, (b * S + s) * kstride + voff + h * D + i, dt));
+        }
+      }
+    }
+  }
+
+  /* 3. attention over the valid keys of present. */
+  set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic) collapse(3)
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t h = 0; h < H; ++h)
+      for (int64_t s = 0; s < S; ++s) {
+        int64_t past_len = (int64_t)seqlens_k[b] + 1 - S;
+        int64_t qpos = past_len + s;
+        int64_t hk = h / G;
+        int64_t lo = 0;
+        if (p->local_window > 0 && qpos - p->local_window + 1 > 0)
+          lo = qpos - p->local_window + 1;
+        int64_t n = qpos + 1 - lo;
+        double* sc = (double*)malloc((size_t)n * sizeof(double));
+        const float* qv = qr + ((b * S + s) * H + h) * D;
+        double mx = -INFINITY;
+        for (int64_t j = lo; j <= qpos; ++j) {
+          int64_t row = ((b * HK + hk) * cap + j) * D;
+          double dot = 0.0;
+          for (int64_t i = 0; i < D; ++i) dot += (double)qv[i] * load_f(present_k, row + i, dt);
+          double x = dot * (double)scale;
+          if (p->bias_batch > 0) {
+            int64_t bb = p->bias_batch == 1 ? 0 : b;
+            x += load_f(attn_bias, (bb * S + s) * p->bias_total + j, dt);
+          }
+          sc[j - lo] = x;
+          if (x > mx) mx = x;
+        }
+        double den = 0.0;
+        for (int64_t t = 0; t < n; ++t) {
+          sc[t] = (mx == -INFINITY) ? 0.0 : exp(sc[t] - mx);
+          den += sc[t];
+        }
+        for (int64_t i = 0; i < D; ++i) {
+          double acc = 0.0;
+          for (int64_t j = lo; j <= qpos; ++j)
+            acc += sc[j - lo] * load_f(present_v, ((b * HK + hk) * cap + j) * D + i, dt);
+          store_f(out, ((b * S + s) * H + h) * D + i, dt, den > 0 ? acc / den : 0.0);
+        }
+        free(sc);
+      }
+  free(qr);
+  return OR_OK;
+}
+
+/* ---- GatherBlockQuantized (int4, gather_axis 0, quantize_axis last) -------
+ * Row gather then (q - zp) * scale, zp default 8 (quant.rs:1134-1200). */
+int oracle_gather_block_quantized(const uint8_t* data, const void* scales, int scale_dt,
+                                  const uint8_t* zp, const int64_t* indices,
+                                  int64_t n_indices, int64_t vocab, int64_t dim,
+                                  int block, void* out, int out_dt) {
+  if (!data || !scales || !indices || !out || dim % block || dim % 2) return OR_EINVAL;
+  int64_t nblocks = dim / block;
+  for (int64_t i = 0; i < n_indices; ++i) {
+    int64_t r = indices[i];
+    if (r < 0) r += vocab;
+    if (r < 0 || r >= vocab) return OR_ERANGE;
+    for (int64_t j = 0; j < dim; ++j) {
+      uint8_t byte = data[r * (dim / 2) + j / 2];
+      int qv = (j & 1) ? (byte >> 4) : (byte & 0x0f);
+      int64_t blk = j / block;
+      int z = 8;
+      if (zp) {
+        uint8_t zb = zp[r * ((nblocks + 1) / 2) + blk / 2];
+        z = (blk & 1) ? (zb >> 4) : (zb & 0x0f);
+      }
+      float s = load_f(scales, r * nblocks + blk, scale_dt);
+      store_f(out, i * dim + j, out_dt, (double)((float)(qv - z) * s));
+    }
+  }
+  return OR_OK;
+}
