@@ -1,0 +1,767 @@
+// GroupQueryAttention for sm_100a (reference: group_query_attention_op,
+// rust/src/ops/attention.rs:556-952, which composes mlx_fast_rope, mlx_slice_update and
+// mlx_fast_scaled_dot_product_attention).
+//
+// gqa_decode_kernel — split-K flash-decode over the shared KV buffer.
+//   grid (splits, kv_heads, batch); 4 consumer warps + 1 producer warp.
+//   * Every CTA rotates (RoPE, optional per-head RMS norm) the R = S * (H / HK) query rows of its
+//     kv-head group into shared memory, rounded through the I/O dtype as ORT stores them.
+//   * The CTA whose key range holds the new positions [past_b, past_b + S) rotates the new k rows
+//     and writes k and v in place into the KV buffer (the fused KV append), then fences the
+//     generic-proxy writes against the TMA reads that follow.
+//   * The producer warp streams 32-key K/V tiles with 1-D bulk copies (cp.async.bulk, the TMA
+//     engine) into a ring of shared-memory stages guarded by mbarriers; all waits are bounded.
+//   * Consumers: each lane owns head_size/32 contiguous dims of a key; q.k partials for
+//     (keys x rows) are reduce-scattered across the warp so each lane ends with one score, then
+//     an fp32 online softmax (base 2) and the P.V accumulation run per warp.
+//   * Warp states merge in shared memory; with splits > 1 each CTA writes (m, l, o) partials and
+//     the last CTA of its (batch, kv-head) — found with an arrival counter that it resets —
+//     merges them into the output.
+// past_b = seqlens_k[b] + 1 - S is read on the device, so a launch configuration (and a CUDA
+// graph holding it) serves every decode step.
+//
+// gqa_append_kernel + gqa_generic_kernel — the same semantics for shapes the decode kernel
+// does not cover (head_size not a multiple of 32, more than 32 query rows per group, unaligned
+// rows): one CTA per query row, keys in shared memory.
+#include <algorithm>
+
+#include "../common.cuh"
+#include "kernels.h"
+
+namespace b200ep {
+
+DeviceErrorSlot* device_error_slot();
+
+enum GqaErr { kErrGqaRange = 101, kErrGqaTimeout = 102 };
+
+struct GqaKP {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* kv_k;
+  void* kv_v;
+  const int32_t* seqlens;
+  const void* cos_c;
+  const void* sin_c;
+  const void* qn;
+  const void* kn;
+  const void* bias;
+  void* out;
+  float* partial;
+  int* counters;
+  float* qrot;  // generic path only
+  DeviceErrorSlot* err;
+  int B, S, H, HK, D, G, R, cap, max_seq, half, splits;
+  int do_rotary, interleaved, local_window;
+  int64_t qstride, kstride, koff, voff;  // element strides of the new-row inputs
+  int bias_batch, bias_total;
+  float scale_log2;  // scale * log2(e)
+  float qk_eps;
+  int has_qk_norm;
+};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kNW = 4;        // consumer warps
+constexpr int kKT = 32;       // keys per stage
+constexpr int kKPW = kKT / kNW;  // keys per warp per stage
+
+// ---- shared prologue pieces -----------------------------------------------------------------
+// Rotates (and optionally RMS-normalises) one head row held in `row` (fp32, D values) in place.
+// Executed by one warp; `row` lives in shared memory.
+template <typename T>
+__device__ void rotate_row_warp(float* row, int D, int pos, const GqaKP& kp, const void* normw) {
+  const int lane = threadIdx.x & 31;
+  if (kp.has_qk_norm) {
+    float ss = 0.f;
+    for (int i = lane; i < D; i += 32) ss = fmaf(row[i], row[i], ss);
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)D + kp.qk_eps);
+    const T* w = static_cast<const T*>(normw);
+    for (int i = lane; i < D; i += 32) row[i] = row[i] * inv * to_f<T>(w[i]);
+    __syncwarp();
+  }
+  if (kp.do_rotary) {
+    const T* cc = static_cast<const T*>(kp.cos_c) + (int64_t)pos * kp.half;
+    const T* sc = static_cast<const T*>(kp.sin_c) + (int64_t)pos * kp.half;
+    float o0[4], o1[4];  // rotary_half <= 128 -> at most 4 pairs per lane
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = lane + 32 * c;
+      if (i < kp.half) {
+        const float cs = to_f<T>(cc[i]), sn = to_f<T>(sc[i]);
+        const int i0 = kp.interleaved ? 2 * i : i;
+        const int i1 = kp.interleaved ? 2 * i + 1 : i + kp.half;
+        const float a = row[i0], b = row[i1];
+        o0[c] = a * cs - b * sn;
+        o1[c] = b * cs + a * sn;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = lane + 32 * c;
+      if (i < kp.half) {
+        row[kp.interleaved ? 2 * i : i] = o0[c];
+        row[kp.interleaved ? 2 * i + 1 : i + kp.half] = o1[c];
+      }
+    }
+    __syncwarp();
+  }
+  for (int i = lane; i < D; i += 32) row[i] = round_through<T>(row[i]);
+  __syncwarp();
+}
+
+__device__ __forceinline__ int past_len(const GqaKP& kp, int b) { return kp.seqlens[b] + 1 - kp.S; }
+
+__device__ __forceinline__ bool range_ok(const GqaKP& kp, int past) {
+  return past >= 0 && past + kp.S <= kp.cap && (!kp.do_rotary || past + kp.S <= kp.max_seq);
+}
+
+// ---- decode kernel --------------------------------------------------------------------------
+struct DecodeSmem {
+  // byte offsets inside dynamic shared memory
+  int bars, kbuf, vbuf, qs, pbuf, wst, scratch, flags, total;
+  int stages;
+};
+
+__host__ __device__ inline DecodeSmem decode_smem_layout(int D, int esz, int RP, int stages) {
+  DecodeSmem L;
+  L.stages = stages;
+  int off = 0;
+  L.bars = off;
+  off += 2 * stages * 8;
+  off = (off + 127) & ~127;
+  const int tile = kKT * D * esz;
+  L.kbuf = off;
+  off += stages * tile;
+  L.vbuf = off;
+  off += stages * tile;
+  L.qs = off;
+  off += RP * D * 4;
+  L.pbuf = off;
+  off += kNW * 32 * 4;
+  L.wst = off;
+  off += kNW * RP * (D + 2) * 4;
+  L.scratch = off;
+  off += kNW * D * 4;
+  L.flags = off;
+  off += 16;
+  L.total = off;
+  return L;
+}
+
+template <typename T, int EPL, int RP>
+__global__ void __launch_bounds__((kNW + 1) * 32)
+gqa_decode_kernel(GqaKP kp, int stages) {
+  constexpr int D = EPL * 32;
+  constexpr int KWW = (32 / RP) < kKPW ? (32 / RP) : kKPW;  // keys per warp step
+  constexpr int NV = KWW * RP;                                // values per lane before the reduce
+  static_assert(NV <= 32 && (NV & (NV - 1)) == 0, "NV must be a power of two <= 32");
+  constexpr int LOGNV = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
+  constexpr int SHIFT = 5 - LOGNV;
+  constexpr bool QREG = RP * EPL <= 32;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const DecodeSmem L = decode_smem_layout(D, (int)sizeof(T), RP, stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + stages;
+  T* kbuf = reinterpret_cast<T*>(smem + L.kbuf);
+  T* vbuf = reinterpret_cast<T*>(smem + L.vbuf);
+  float* qs = reinterpret_cast<float*>(smem + L.qs);
+  float* pbuf = reinterpret_cast<float*>(smem + L.pbuf);
+  float* wst = reinterpret_cast<float*>(smem + L.wst);
+  float* scratch = reinterpret_cast<float*>(smem + L.scratch);
+  int* flags = reinterpret_cast<int*>(smem + L.flags);
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int past = past_len(kp, b);
+  const int total = past + kp.S;
+  const bool ok = range_ok(kp, past);
+  const int64_t head_base = ((int64_t)b * kp.HK + kvh) * kp.cap;  // row index of key 0
+  T* kvk = static_cast<T*>(kp.kv_k) + head_base * D;
+  T* kvv = static_cast<T*>(kp.kv_v) + head_base * D;
+
+  // key range of this split
+  int lo = 0;
+  if (kp.local_window > 0) lo = max(0, past - kp.local_window + 1);
+  const int span = max(total - lo, 0);
+  int chunk = (span + kp.splits - 1) / kp.splits;
+  chunk = ((chunk + kKT - 1) / kKT) * kKT;
+  const int kbeg = ok ? min(lo + split * chunk, total) : 0;
+  const int kend = ok ? min(kbeg + chunk, total) : 0;
+  const int ntiles = (kend - kbeg + kKT - 1) / kKT;
+
+  if (threadIdx.x == 0) {
+    flags[0] = 0;       // error flag
+    flags[2] = 0;       // tiles issued by the producer
+    flags[3] = ntiles;  // tiles every consumer warp finished (min)
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kNW);
+    }
+    fence_mbarrier_init();
+    if (!ok && split == 0 && kvh == 0) report_device_error(kp.err, kErrGqaRange, b);
+  }
+
+  // --- prologue: rotated q rows, fused append of the new k / v rows --------------------------
+  for (int i = threadIdx.x; i < (RP - kp.R) * D; i += (kNW + 1) * 32) qs[kp.R * D + i] = 0.f;
+  if (warp < kNW && ok) {
+    const T* qin = static_cast<const T*>(kp.q);
+    for (int r = warp; r < kp.R; r += kNW) {
+      const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
+      float* row = qs + r * D;
+      const T* src = qin + ((int64_t)b * kp.S + s) * kp.qstride + (int64_t)h * D;
+      for (int i = lane; i < D; i += 32) row[i] = to_f<T>(src[i]);
+      __syncwarp();
+      rotate_row_warp<T>(row, D, past + s, kp, kp.qn);
+    }
+    const T* kin = static_cast<const T*>(kp.k);
+    const T* vin = static_cast<const T*>(kp.v);
+    for (int s = warp; s < kp.S; s += kNW) {
+      const int pos = past + s;
+      if (pos < kbeg || pos >= kend) continue;  // another split owns this row
+      float* row = scratch + warp * D;
+      const int64_t in_off = ((int64_t)b * kp.S + s) * kp.kstride + (int64_t)kvh * D;
+      for (int i = lane; i < D; i += 32) row[i] = to_f<T>(kin[in_off + kp.koff + i]);
+      __syncwarp();
+      rotate_row_warp<T>(row, D, pos, kp, kp.kn);
+      for (int i = lane; i < D; i += 32) {
+        kvk[(int64_t)pos * D + i] = from_f<T>(row[i]);
+        kvv[(int64_t)pos * D + i] = vin[in_off + kp.voff + i];
+      }
+    }
+    fence_proxy_async_global();
+  }
+  __syncthreads();
+
+  // --- producer warp -------------------------------------------------------------------------
+  if (warp == kNW) {
+    if (lane == 0 && ok) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % stages;
+        if (t >= stages) {
+          if (!mbar_wait(&empty[s], ((t / stages) - 1) & 1)) {
+            atomicExch(&flags[0], 1);
+            break;
+          }
+        }
+        const int j0 = kbeg + t * kKT;
+        const int nk = min(kKT, kend - j0);
+        const uint32_t bytes = (uint32_t)(nk * D * sizeof(T));
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(kbuf + (size_t)s * kKT * D, kvk + (int64_t)j0 * D, bytes, &full[s]);
+        bulk_g2s(vbuf + (size_t)s * kKT * D, kvv + (int64_t)j0 * D, bytes, &full[s]);
+        flags[2] = t + 1;
+      }
+    }
+  } else {
+    // --- consumer warps ----------------------------------------------------------------------
+    float qreg[QREG ? RP : 1][EPL];
+    if (QREG) {
+#pragma unroll
+      for (int r = 0; r < (QREG ? RP : 1); ++r)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) qreg[r][e] = r < kp.R ? qs[r * D + lane * EPL + e] : 0.f;
+    }
+    float m_run[RP], l_run[RP], o[RP][EPL];
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+      m_run[r] = -INFINITY;
+      l_run[r] = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[r][e] = 0.f;
+    }
+    // row handled by this lane's score after the reduce-scatter
+    const int my_idx = lane >> SHIFT;
+    const int my_r = my_idx % RP;
+    const int my_kk = my_idx / RP;
+    const int my_s = my_r / kp.G;
+    const int qpos = past + my_s;
+    const T* bias = static_cast<const T*>(kp.bias);
+    const int64_t bias_row =
+        kp.bias_batch > 0 ? ((int64_t)(kp.bias_batch == 1 ? 0 : b) * kp.S + my_s) * kp.bias_total : 0;
+
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % stages;
+      if (!mbar_wait(&full[s], (t / stages) & 1)) {
+        atomicExch(&flags[0], 1);
+        if (lane == 0) atomicMin(&flags[3], t);
+        break;
+      }
+      const int j0 = kbeg + t * kKT;
+      const T* kt = kbuf + (size_t)s * kKT * D;
+      const T* vt = vbuf + (size_t)s * kKT * D;
+#pragma unroll
+      for (int step = 0; step < kKPW / KWW; ++step) {
+        const int kl0 = warp * kKPW + step * KWW;  // first key (tile-local) of this step
+        float v[NV];
+#pragma unroll
+        for (int kk = 0; kk < KWW; ++kk) {
+          const int kl = kl0 + kk;
+          float kf[EPL];
+          const T* kr = kt + (size_t)kl * D + lane * EPL;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) kf[e] = (j0 + kl < kend) ? to_f<T>(kr[e]) : 0.f;
+#pragma unroll
+          for (int r = 0; r < RP; ++r) {
+            float acc = 0.f;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              const float qv = QREG ? qreg[QREG ? r : 0][e] : qs[r * D + lane * EPL + e];
+              acc = fmaf(qv, kf[e], acc);
+            }
+            v[kk * RP + r] = acc;
+          }
+        }
+        // reduce-scatter: lane ends with the full dot product of value index (lane >> SHIFT)
+        int cur = NV;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          if (cur > 1) {
+            const int halfn = cur >> 1;
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int i = 0; i < NV / 2; ++i) {
+              if (i < halfn) {
+                const float send = upper ? v[i] : v[i + halfn];
+                const float keep = upper ? v[i + halfn] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+              }
+            }
+            cur = halfn;
+          } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+          }
+        }
+        // score in log2 units with masks
+        const int j = j0 + kl0 + my_kk;
+        float sc = v[0] * kp.scale_log2;
+        bool valid = (j < kend) && (my_r < kp.R) && (j <= qpos) &&
+                     (kp.local_window <= 0 || j > qpos - kp.local_window);
+        if (valid && bias) {
+          if (j < kp.bias_total) sc += to_f<T>(bias[bias_row + j]) * kLog2e;
+        }
+        if (!valid) sc = -INFINITY;
+        // per-row max / sum over the KWW keys: lanes sharing my_r differ in idx bits >= log2(RP)
+        float mx = sc;
+#pragma unroll
+        for (int off = RP << SHIFT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float m_new[RP];
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+          const float step_max = __shfl_sync(0xffffffffu, mx, r << SHIFT);
+          m_new[r] = fmaxf(m_run[r], step_max);
+        }
+        float mrow = m_new[0];
+#pragma unroll
+        for (int r = 1; r < RP; ++r)
+          if (r == my_r) mrow = m_new[r];
+        const float p = (sc == -INFINITY) ? 0.f : exp2f(sc - mrow);
+        float ps = p;
+#pragma unroll
+        for (int off = RP << SHIFT; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+        if ((lane & ((1 << SHIFT) - 1)) == 0) pbuf[warp * 32 + my_idx] = p;
+#pragma unroll
+        for (int r = 0; r < RP; ++r) {
+          const float step_sum = __shfl_sync(0xffffffffu, ps, r << SHIFT);
+          const float corr = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new[r]);
+          l_run[r] = l_run[r] * corr + step_sum;
+          m_run[r] = m_new[r];
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) o[r][e] *= corr;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int kk = 0; kk < KWW; ++kk) {
+          const int kl = kl0 + kk;
+          const T* vr = vt + (size_t)kl * D + lane * EPL;
+          float vf[EPL];
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) vf[e] = (j0 + kl < kend) ? to_f<T>(vr[e]) : 0.f;
+#pragma unroll
+          for (int r = 0; r < RP; ++r) {
+            const float pr = pbuf[warp * 32 + kk * RP + r];
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) o[r][e] = fmaf(pr, vf[e], o[r][e]);
+          }
+        }
+        __syncwarp();
+      }
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // publish this warp's state
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+      float* w = wst + ((size_t)warp * RP + r) * (D + 2);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) w[lane * EPL + e] = o[r][e];
+      if (lane == 0) {
+        w[D] = m_run[r];
+        w[D + 1] = l_run[r];
+      }
+    }
+  }
+  __syncthreads();
+  if (flags[0] && threadIdx.x == 0) {
+    report_device_error(kp.err, kErrGqaTimeout, blockIdx.x);
+    // let the copies still in flight land before this CTA's shared memory is released
+    for (int t = flags[3]; t < flags[2]; ++t) mbar_wait(&full[t % stages], (t / stages) & 1, 1u << 20);
+  }
+  __syncthreads();
+
+  // --- merge the warps; write the output or this split's partial -----------------------------
+  const int nthreads = (kNW + 1) * 32;
+  float* part = kp.partial + ((((int64_t)b * kp.HK + kvh) * kp.splits + split) * RP) * (D + 2);
+  for (int idx = threadIdx.x; idx < kp.R * (D + 2); idx += nthreads) {
+    const int r = idx / (D + 2), d = idx - r * (D + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) M = fmaxf(M, wst[((size_t)w * RP + r) * (D + 2) + D]);
+    float acc = 0.f, lsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) {
+      const float* ws = wst + ((size_t)w * RP + r) * (D + 2);
+      const float f = (ws[D] == -INFINITY) ? 0.f : exp2f(ws[D] - M);
+      if (d < D) acc = fmaf(ws[d], f, acc);
+      lsum = fmaf(ws[D + 1], f, lsum);
+    }
+    if (kp.splits == 1) {
+      if (d < D) {
+        const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
+        T* out = static_cast<T*>(kp.out) + (((int64_t)b * kp.S + s) * kp.H + h) * D;
+        out[d] = from_f<T>(lsum > 0.f ? acc / lsum : 0.f);
+      }
+    } else {
+      part[idx] = d < D ? acc : (d == D ? M : lsum);
+    }
+  }
+  if (kp.splits == 1) return;
+
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&kp.counters[b * kp.HK + kvh], 1);
+    flags[1] = (ticket == kp.splits - 1);
+  }
+  __syncthreads();
+  if (!flags[1]) return;
+  __threadfence();
+  const float* base = kp.partial + (((int64_t)b * kp.HK + kvh) * kp.splits) * RP * (D + 2);
+  for (int idx = threadIdx.x; idx < kp.R * D; idx += nthreads) {
+    const int r = idx / D, d = idx - r * D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < kp.splits; ++sp)
+      M = fmaxf(M, __ldcg(base + ((size_t)sp * RP + r) * (D + 2) + D));
+    float acc = 0.f, lsum = 0.f;
+    for (int sp = 0; sp < kp.splits; ++sp) {
+      const float* ps = base + ((size_t)sp * RP + r) * (D + 2);
+      const float m = __ldcg(ps + D);
+      const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
+      acc = fmaf(__ldcg(ps + d), f, acc);
+      lsum = fmaf(__ldcg(ps + D + 1), f, lsum);
+    }
+    const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
+    T* out = static_cast<T*>(kp.out) + (((int64_t)b * kp.S + s) * kp.H + h) * D;
+    out[d] = from_f<T>(lsum > 0.f ? acc / lsum : 0.f);
+  }
+  if (threadIdx.x == 0) kp.counters[b * kp.HK + kvh] = 0;
+}
+
+// ---- generic path ---------------------------------------------------------------------------
+// One warp per new row: q rows (H per token) go to kp.qrot (fp32, rounded through T); k rows are
+// rotated and written with v into the KV buffer.
+template <typename T>
+__global__ void gqa_append_kernel(GqaKP kp) {
+  extern __shared__ float rowbuf[];  // [warps][D]
+  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_tok = kp.H + kp.HK;
+  const int item = blockIdx.x * warps + warp;
+  if (item >= kp.B * kp.S * per_tok) return;
+  const int b = item / (kp.S * per_tok);
+  const int rem = item - b * kp.S * per_tok;
+  const int s = rem / per_tok, hh = rem - s * per_tok;
+  const int past = past_len(kp, b);
+  if (!range_ok(kp, past)) {
+    if (lane == 0) report_device_error(kp.err, kErrGqaRange, b);
+    return;
+  }
+  const int pos = past + s;
+  const int D = kp.D;
+  float* row = rowbuf + warp * D;
+  if (hh < kp.H) {
+    const T* src = static_cast<const T*>(kp.q) + ((int64_t)b * kp.S + s) * kp.qstride + (int64_t)hh * D;
+    for (int i = lane; i < D; i += 32) row[i] = to_f<T>(src[i]);
+    __syncwarp();
+    rotate_row_warp<T>(row, D, pos, kp, kp.qn);
+    float* dst = kp.qrot + (((int64_t)b * kp.S + s) * kp.H + hh) * D;
+    for (int i = lane; i < D; i += 32) dst[i] = row[i];
+  } else {
+    const int kvh = hh - kp.H;
+    const int64_t in_off = ((int64_t)b * kp.S + s) * kp.kstride + (int64_t)kvh * D;
+    const T* kin = static_cast<const T*>(kp.k);
+    const T* vin = static_cast<const T*>(kp.v);
+    for (int i = lane; i < D; i += 32) row[i] = to_f<T>(kin[in_off + kp.koff + i]);
+    __syncwarp();
+    rotate_row_warp<T>(row, D, pos, kp, kp.kn);
+    const int64_t dst = (((int64_t)b * kp.HK + kvh) * kp.cap + pos) * D;
+    T* kvk = static_cast<T*>(kp.kv_k);
+    T* kvv = static_cast<T*>(kp.kv_v);
+    for (int i = lane; i < D; i += 32) {
+      kvk[dst + i] = from_f<T>(row[i]);
+      kvv[dst + i] = vin[in_off + kp.voff + i];
+    }
+  }
+}
+
+// One CTA (128 threads) per (b, s, h) query row; scores for all keys staged in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(128) gqa_generic_kernel(GqaKP kp) {
+  extern __shared__ float sh[];  // [D] q, [cap] scores, [4] reduction
+  const int row = blockIdx.x;
+  const int h = row % kp.H, s = (row / kp.H) % kp.S, b = row / (kp.H * kp.S);
+  const int past = past_len(kp, b);
+  if (!range_ok(kp, past)) return;
+  const int D = kp.D, kvh = h / kp.G;
+  const int qpos = past + s;
+  const int lo = kp.local_window > 0 ? max(0, qpos - kp.local_window + 1) : 0;
+  const int n = qpos + 1 - lo;
+  float* qv = sh;
+  float* sc = sh + D;
+  float* red = sc + kp.cap;
+  const float* qsrc = kp.qrot + (((int64_t)b * kp.S + s) * kp.H + h) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) qv[i] = qsrc[i];
+  __syncthreads();
+  const T* kc = static_cast<const T*>(kp.kv_k) + ((int64_t)b * kp.HK + kvh) * kp.cap * D;
+  const T* vc = static_cast<const T*>(kp.kv_v) + ((int64_t)b * kp.HK + kvh) * kp.cap * D;
+  const T* bias = static_cast<const T*>(kp.bias);
+  float mx = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const int j = lo + t;
+    float acc = 0.f;
+    for (int i = 0; i < D; ++i) acc = fmaf(qv[i], to_f<T>(kc[(int64_t)j * D + i]), acc);
+    float x = acc * kp.scale_log2;
+    if (bias && j < kp.bias_total)
+      x += to_f<T>(bias[((int64_t)(kp.bias_batch == 1 ? 0 : b) * kp.S + s) * kp.bias_total + j]) * kLog2e;
+    sc[t] = x;
+    mx = fmaxf(mx, x);
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float p = exp2f(sc[t] - mx);
+    sc[t] = p;
+    sum += p;
+  }
+  sum = warp_sum(sum);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  sum = red[0] + red[1] + red[2] + red[3];
+  T* out = static_cast<T*>(kp.out) + (((int64_t)b * kp.S + s) * kp.H + h) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < n; ++t) acc = fmaf(sc[t], to_f<T>(vc[(int64_t)(lo + t) * D + i]), acc);
+    out[i] = from_f<T>(sum > 0.f ? acc / sum : 0.f);
+  }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+namespace {
+
+int pow2_at_least(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+bool decode_path(const b200ep_gqa_params& p, int esz) {
+  const int G = (int)(p.num_heads / p.kv_heads);
+  const int R = (int)(p.seq * G);
+  return p.head_size % 32 == 0 && p.head_size <= 256 && R <= 32 &&
+         pow2_at_least(R) * (p.head_size / 32) <= 64 && (p.head_size * esz) % 16 == 0;
+}
+
+int choose_splits(const b200ep_gqa_params& p) {
+  const int64_t pairs = p.batch * p.kv_heads;
+  int64_t want = (2 * 148 + pairs - 1) / pairs;
+  int64_t max_by_len = std::max<int64_t>(1, p.cap / kKT);
+  return (int)std::max<int64_t>(1, std::min<int64_t>({want, max_by_len, 64}));
+}
+
+struct WsLayout {
+  size_t counters, partial, qrot, total;
+};
+
+WsLayout ws_layout(const b200ep_gqa_params& p) {
+  const int G = (int)(p.num_heads / p.kv_heads);
+  const int RP = pow2_at_least((int)(p.seq * G));
+  WsLayout w;
+  size_t off = 0;
+  w.counters = off;
+  off += ((size_t)p.batch * p.kv_heads * sizeof(int) + 255) & ~(size_t)255;
+  w.partial = off;
+  off += ((size_t)p.batch * p.kv_heads * choose_splits(p) * RP * (p.head_size + 2) * 4 + 255) &
+         ~(size_t)255;
+  w.qrot = off;
+  off += ((size_t)p.batch * p.seq * p.num_heads * p.head_size * 4 + 255) & ~(size_t)255;
+  w.total = off;
+  return w;
+}
+
+template <typename T, int EPL, int RP>
+cudaError_t launch_decode_t(const GqaKP& kp, cudaStream_t st) {
+  if constexpr (RP * EPL > 64) {
+    return cudaErrorInvalidValue;  // never selected: decode_path() sends these to the generic path
+  } else {
+  const int D = EPL * 32;
+  const int tile = kKT * D * (int)sizeof(T);
+  int stages = tile <= 8192 ? 6 : tile <= 16384 ? 4 : 2;
+  DecodeSmem L = decode_smem_layout(D, (int)sizeof(T), RP, stages);
+  auto kern = gqa_decode_kernel<T, EPL, RP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+  if (e != cudaSuccess) return e;
+  dim3 grid(kp.splits, kp.HK, kp.B);
+  kern<<<grid, (kNW + 1) * 32, L.total, st>>>(kp, stages);
+  return cudaGetLastError();
+  }
+}
+
+template <typename T, int EPL>
+cudaError_t launch_decode_rp(const GqaKP& kp, cudaStream_t st) {
+  switch (pow2_at_least(kp.R)) {
+    case 1: return launch_decode_t<T, EPL, 1>(kp, st);
+    case 2: return launch_decode_t<T, EPL, 2>(kp, st);
+    case 4: return launch_decode_t<T, EPL, 4>(kp, st);
+    case 8: return launch_decode_t<T, EPL, 8>(kp, st);
+    case 16: return launch_decode_t<T, EPL, 16>(kp, st);
+    case 32: return launch_decode_t<T, EPL, 32>(kp, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+cudaError_t launch_decode(const GqaKP& kp, cudaStream_t st) {
+  switch (kp.D) {
+    case 32: return launch_decode_rp<T, 1>(kp, st);
+    case 64: return launch_decode_rp<T, 2>(kp, st);
+    case 96: return launch_decode_rp<T, 3>(kp, st);
+    case 128: return launch_decode_rp<T, 4>(kp, st);
+    case 256: return launch_decode_rp<T, 8>(kp, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+cudaError_t launch_generic(const GqaKP& kp, cudaStream_t st) {
+  const int warps = 4;
+  const int items = kp.B * kp.S * (kp.H + kp.HK);
+  gqa_append_kernel<T><<<div_up(items, warps), warps * 32, warps * kp.D * sizeof(float), st>>>(kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t smem = (size_t)(kp.D + kp.cap + 4) * sizeof(float);
+  auto kern = gqa_generic_kernel<T>;
+  if (smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  kern<<<kp.B * kp.S * kp.H, 128, smem, st>>>(kp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
+
+int launch_gqa(const GqaArgs& a, cudaStream_t st) {
+  const b200ep_gqa_params& p = a.p;
+  B200EP_CHECK_ARG(p.batch > 0 && p.seq > 0 && p.num_heads > 0 && p.kv_heads > 0 && p.head_size > 0,
+                   "GroupQueryAttention: batch, seq, num_heads, kv_heads and head_size must be > 0");
+  B200EP_CHECK_ARG(p.num_heads % p.kv_heads == 0, "GroupQueryAttention: num_heads % kv_num_heads != 0");
+  B200EP_CHECK_ARG(p.head_size <= 256, "GroupQueryAttention: head_size > 256 is not supported");
+  B200EP_CHECK_ARG(p.cap > 0, "GroupQueryAttention: KV buffer capacity must be > 0");
+  B200EP_CHECK_ARG(is_float_dtype(a.dtype), "GroupQueryAttention: dtype must be float32/float16/bfloat16");
+  B200EP_CHECK_ARG(a.query && a.kv_key && a.kv_value && a.seqlens_k && a.out,
+                   "GroupQueryAttention: null tensor pointer");
+  B200EP_CHECK_ARG(p.packed_qkv || (a.key && a.value), "GroupQueryAttention: key/value missing");
+  if (p.do_rotary) {
+    B200EP_CHECK_ARG(a.cos_cache && a.sin_cache && p.rotary_half > 0 && 2 * p.rotary_half <= p.head_size &&
+                         p.max_seq > 0,
+                     "GroupQueryAttention: do_rotary needs cos/sin caches with 2*rotary_half <= head_size");
+    B200EP_CHECK_ARG(p.rotary_half <= 128, "GroupQueryAttention: rotary_half > 128 is not supported");
+  }
+  B200EP_CHECK_ARG((a.q_norm == nullptr) == (a.k_norm == nullptr),
+                   "GroupQueryAttention: q_norm and k_norm must be given together");
+  B200EP_CHECK_ARG(p.bias_batch == 0 || a.bias, "GroupQueryAttention: attention_bias pointer missing");
+  const int esz = dtype_size(a.dtype);
+  const WsLayout wl = ws_layout(p);
+  B200EP_CHECK_ARG(a.workspace && a.workspace_bytes >= wl.total, "GroupQueryAttention: workspace too small");
+
+  GqaKP kp{};
+  kp.q = a.query;
+  kp.k = p.packed_qkv ? a.query : a.key;
+  kp.v = p.packed_qkv ? a.query : a.value;
+  kp.kv_k = a.kv_key;
+  kp.kv_v = a.kv_value;
+  kp.seqlens = a.seqlens_k;
+  kp.cos_c = a.cos_cache;
+  kp.sin_c = a.sin_cache;
+  kp.qn = a.q_norm;
+  kp.kn = a.k_norm;
+  kp.bias = p.bias_batch > 0 ? a.bias : nullptr;
+  kp.out = a.out;
+  char* ws = static_cast<char*>(a.workspace);
+  kp.counters = reinterpret_cast<int*>(ws + wl.counters);
+  kp.partial = reinterpret_cast<float*>(ws + wl.partial);
+  kp.qrot = reinterpret_cast<float*>(ws + wl.qrot);
+  kp.err = device_error_slot();
+  kp.B = (int)p.batch;
+  kp.S = (int)p.seq;
+  kp.H = (int)p.num_heads;
+  kp.HK = (int)p.kv_heads;
+  kp.D = (int)p.head_size;
+  kp.G = kp.H / kp.HK;
+  kp.R = kp.S * kp.G;
+  kp.cap = (int)p.cap;
+  kp.max_seq = (int)p.max_seq;
+  kp.half = (int)p.rotary_half;
+  kp.splits = choose_splits(p);
+  kp.do_rotary = p.do_rotary ? 1 : 0;
+  kp.interleaved = p.interleaved ? 1 : 0;
+  kp.local_window = p.local_window;
+  const int64_t D = p.head_size;
+  kp.qstride = p.packed_qkv ? (p.num_heads + 2 * p.kv_heads) * D : p.num_heads * D;
+  kp.kstride = p.packed_qkv ? kp.qstride : p.kv_heads * D;
+  kp.koff = p.packed_qkv ? p.num_heads * D : 0;
+  kp.voff = p.packed_qkv ? (p.num_heads + p.kv_heads) * D : 0;
+  kp.bias_batch = (int)p.bias_batch;
+  kp.bias_total = (int)p.bias_total;
+  const float scale = p.scale != 0.f ? p.scale : 1.0f / sqrtf((float)D);
+  kp.scale_log2 = scale * kLog2e;
+  kp.qk_eps = p.qk_norm_eps;
+  kp.has_qk_norm = a.q_norm ? 1 : 0;
+
+  const bool aligned = (reinterpret_cast<uintptr_t>(a.kv_key) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(a.kv_value) % 16 == 0);
+  cudaError_t e;
+  if (decode_path(p, esz) && aligned) {
+    switch (a.dtype) {
+      case kF32: e = launch_decode<float>(kp, st); break;
+      case kF16: e = launch_decode<__half>(kp, st); break;
+      default: e = launch_decode<__nv_bfloat16>(kp, st); break;
+    }
+  } else {
+    B200EP_CHECK_ARG(p.cap <= 40000, "GroupQueryAttention: generic path limited to cap <= 40000");
+    switch (a.dtype) {
+      case kF32: e = launch_generic<float>(kp, st); break;
+      case kF16: e = launch_generic<__half>(kp, st); break;
+      default: e = launch_generic<__nv_bfloat16>(kp, st); break;
+    }
+  }
+  return cuda_status(e, "GroupQueryAttention launch");
+}
+
+}  // namespace b200ep

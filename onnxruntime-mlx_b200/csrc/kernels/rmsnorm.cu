@@ -1,0 +1,83 @@
+// RMS norms for sm_100a: RMSNormalization / SimplifiedLayerNormalization and
+// SkipSimplifiedLayerNormalization (reference: rust/src/ops/norm.rs:163-246, which calls
+// mlx_fast_rms_norm).  One CTA per row; the row is read once into registers (vectorised,
+// up to 8 values per thread per pass), the sum of squares is reduced in fp32 across the CTA,
+// and the scaled row is written back.  The skip form writes the fp32 sum rounded to the I/O
+// dtype as the residual output and normalises the unrounded sum.
+#include "../common.cuh"
+#include "kernels.h"
+
+namespace b200ep {
+
+constexpr int kRmsThreads = 256;
+constexpr int kRmsMaxPerThread = 32;  // hidden <= 8192 held in registers
+
+template <typename T, bool SKIP>
+__global__ void __launch_bounds__(kRmsThreads)
+rms_norm_kernel(const T* __restrict__ X, const T* __restrict__ skip, const T* __restrict__ gamma,
+                T* __restrict__ Y, T* __restrict__ R, int64_t hidden, float eps) {
+  __shared__ float red[kRmsThreads / 32];
+  const int64_t row = blockIdx.x;
+  const T* x = X + row * hidden;
+  const T* sk = SKIP ? skip + row * hidden : nullptr;
+  float v[kRmsMaxPerThread];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRmsMaxPerThread; ++c) {
+    const int64_t j = threadIdx.x + (int64_t)c * kRmsThreads;
+    float t = 0.f;
+    if (j < hidden) {
+      t = to_f<T>(x[j]);
+      if (SKIP) {
+        t += to_f<T>(sk[j]);
+        if (R) R[row * hidden + j] = from_f<T>(t);
+      }
+    }
+    v[c] = t;
+    ss = fmaf(t, t, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kRmsThreads / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)hidden + eps);
+#pragma unroll
+  for (int c = 0; c < kRmsMaxPerThread; ++c) {
+    const int64_t j = threadIdx.x + (int64_t)c * kRmsThreads;
+    if (j < hidden) Y[row * hidden + j] = from_f<T>(v[c] * inv * to_f<T>(gamma[j]));
+  }
+}
+
+namespace {
+template <typename T>
+cudaError_t launch_t(const RmsArgs& a, cudaStream_t st) {
+  if (a.rows == 0) return cudaSuccess;
+  dim3 grid((unsigned)a.rows);
+  if (a.skip)
+    rms_norm_kernel<T, true><<<grid, kRmsThreads, 0, st>>>(
+        static_cast<const T*>(a.X), static_cast<const T*>(a.skip), static_cast<const T*>(a.gamma),
+        static_cast<T*>(a.Y), static_cast<T*>(a.residual), a.hidden, a.eps);
+  else
+    rms_norm_kernel<T, false><<<grid, kRmsThreads, 0, st>>>(
+        static_cast<const T*>(a.X), nullptr, static_cast<const T*>(a.gamma), static_cast<T*>(a.Y),
+        nullptr, a.hidden, a.eps);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_rms_norm(const RmsArgs& a, cudaStream_t st) {
+  if (a.hidden > (int64_t)kRmsThreads * kRmsMaxPerThread) return cudaErrorInvalidValue;
+  switch (a.dtype) {
+    case kF32: return launch_t<float>(a, st);
+    case kF16: return launch_t<__half>(a, st);
+    case kBF16: return launch_t<__nv_bfloat16>(a, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace b200ep

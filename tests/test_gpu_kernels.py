@@ -1,0 +1,342 @@
+"""GPU parity of the kernel-level C ABI (include/b200ep.h) against the CPU oracle and the golden
+fixtures built from the reference's tests.
+
+Tolerances: fp32 paths rtol = atol = 6e-5; fp16 / bf16 paths
+max-abs 1e-3 + rel 1e-2; dequantised weights bit-exact.  Reference test geometries come from
+tests/golden (tests/ops/test_matmulnbits_asym.py, test_mlx_ops.py, test_gqa11.py).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden_case, load_golden
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+with open(os.path.join(GOLDEN, "manifest.json")) as _f:
+    MANIFEST = json.load(_f)
+
+TOL = {"f32": dict(rtol=6e-5, atol=6e-5), "f16": dict(rtol=1e-2, atol=1e-3), "bf16": dict(rtol=1e-2, atol=1e-3)}
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from onnxruntime_ep_b200 import ops as _ops
+
+    return _ops
+
+
+@pytest.fixture(autouse=True)
+def _device_error_clean(ops):
+    ops.device_error(clear=True)
+    yield
+    torch.cuda.synchronize()
+    code, detail = ops.device_error(clear=True)
+    assert code == 0, f"kernel reported device error {code} (detail {detail})"
+
+
+def cuda(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def to_np(t):
+    return t.detach().cpu().numpy()
+
+
+# ---- MatMulNBits ---------------------------------------------------------------------------
+MNB = load_golden("matmulnbits.npz")
+MNB_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "matmulnbits")
+
+
+@pytest.mark.parametrize("name", MNB_CASES)
+def test_matmulnbits_golden(ops, name):
+    meta, c = MANIFEST[name], golden_case(MNB, name)
+    zp = cuda(c["zero_points"]) if "zero_points" in c else None
+    y = ops.matmulnbits(cuda(c["a"]), cuda(c["b"]), cuda(c["scales"]), zp, K=meta["K"], N=meta["N"],
+                       bits=meta["bits"], block_size=meta["block_size"])
+    got = to_np(y).astype(np.float32)
+    want = c["y"].astype(np.float32)
+    np.testing.assert_allclose(got, want, **TOL[meta["dtype"]])
+
+
+@pytest.mark.parametrize("name", MNB_CASES)
+def test_matmulnbits_dequant_bit_exact(ops, name):
+    meta, c = MANIFEST[name], golden_case(MNB, name)
+    zp = cuda(c["zero_points"]) if "zero_points" in c else None
+    w = ops.matmulnbits_dequant(cuda(c["b"]), cuda(c["scales"]), zp, K=meta["K"], N=meta["N"],
+                                bits=meta["bits"], block_size=meta["block_size"])
+    np.testing.assert_array_equal(to_np(w), c["w"])
+
+
+def make_mnb(rng, M, K, N, block=32, bits=4, dtype=np.float32, asym=True):
+    """BASELINE config 1 distributions: A ~ N(0,1), scales ~ U(0.005, 0.02), zp ~ U{0..15}."""
+    nblocks = (K + block - 1) // block
+    a = rng.standard_normal((M, K)).astype(dtype)
+    q = rng.integers(0, 1 << bits, size=(N, nblocks, block), dtype=np.uint8)
+    b = (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8) if bits == 4 else q
+    scales = rng.uniform(0.005, 0.02, size=N * nblocks).astype(dtype)
+    zp = None
+    if asym:
+        z = rng.integers(0, 1 << bits, size=(N, nblocks), dtype=np.uint8)
+        if bits == 4:
+            if nblocks % 2:
+                z = np.concatenate([z, np.zeros((N, 1), np.uint8)], axis=1)
+            zp = (z[:, 0::2] | (z[:, 1::2] << 4)).reshape(-1).astype(np.uint8)
+        else:
+            zp = z.reshape(-1)
+    return a, b, scales, zp
+
+
+@pytest.mark.parametrize("M", [1, 16, 512])
+def test_matmulnbits_config1_fp32(ops, M):
+    """fp32 A [M, 4096], B [4096, 4096] int4 block 32, fp32 scales, uint8 zp."""
+    rng = np.random.default_rng(0)
+    a, b, s, zp = make_mnb(rng, M, 4096, 4096)
+    want = oracle.matmulnbits(a, b, s, zp, N=4096, K=4096)
+    got = to_np(ops.matmulnbits(cuda(a), cuda(b), cuda(s), cuda(zp), K=4096, N=4096))
+    np.testing.assert_allclose(got, want, **TOL["f32"])
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (1, 14336, 4096), (1, 4096, 28672), (2, 4096, 4096),
+                                   (4, 4096, 1024), (16, 4096, 4096)])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_matmulnbits_llama_shapes(ops, M, K, N, dt):
+    rng = np.random.default_rng(M * 7 + K + N)
+    a, b, s, zp = make_mnb(rng, M, K, N, dtype=np.float32)
+    if dt == "f16":
+        a16, s16 = a.astype(np.float16), s.astype(np.float16)
+        want = oracle.matmulnbits(a16, b, s16, zp, N=N, K=K).astype(np.float32)
+        got = ops.matmulnbits(cuda(a16), cuda(b), cuda(s16), cuda(zp), K=K, N=N)
+    else:
+        ab, sb = oracle.f32_to_bf16_bits(a), oracle.f32_to_bf16_bits(s)
+        want = oracle.bf16_bits_to_f32(oracle.matmulnbits(ab, b, sb, zp, N=N, K=K, dtype="bf16"))
+        got = ops.matmulnbits(cuda(ab).view(torch.bfloat16), cuda(b), cuda(sb).view(torch.bfloat16), cuda(zp),
+                              K=K, N=N)
+    np.testing.assert_allclose(to_np(got.float()), want, **TOL[dt])
+
+
+def test_matmulnbits_symmetric_int8_and_odd_k(ops):
+    rng = np.random.default_rng(5)
+    for bits, K, block in [(8, 4096, 32), (4, 1176, 32), (4, 48, 16), (4, 4100, 128)]:
+        a, b, s, zp = make_mnb(rng, 3, K, 256, block=block, bits=bits, asym=False)
+        want = oracle.matmulnbits(a, b, s, None, N=256, K=K, bits=bits, block_size=block)
+        got = to_np(ops.matmulnbits(cuda(a), cuda(b), cuda(s), None, K=K, N=256, bits=bits, block_size=block))
+        np.testing.assert_allclose(got, want, **TOL["f32"])
+
+
+def test_matmulnbits_empty_m(ops):
+    rng = np.random.default_rng(1)
+    a, b, s, zp = make_mnb(rng, 1, 64, 32)
+    y = ops.matmulnbits(cuda(a[:0]), cuda(b), cuda(s), cuda(zp), K=64, N=32)
+    assert y.shape == (0, 32)
+
+
+def test_matmulnbits_rejects_bad_block(ops):
+    from onnxruntime_ep_b200 import B200EPError
+
+    rng = np.random.default_rng(1)
+    a, b, s, zp = make_mnb(rng, 1, 64, 32)
+    with pytest.raises(B200EPError, match="block_size"):
+        ops.matmulnbits(cuda(a), cuda(b), cuda(s), cuda(zp), K=64, N=32, block_size=24)
+
+
+# ---- RMS norms -----------------------------------------------------------------------------
+NORMS = load_golden("norms.npz")
+
+
+@pytest.mark.parametrize("name,eps", [("rms", 1e-6), ("sln", 1e-5), ("rms16", 1e-6)])
+def test_rms_norm_golden(ops, name, eps):
+    c = golden_case(NORMS, name)
+    y = to_np(ops.rms_norm(cuda(c["x"]), cuda(c["scale"]), eps))
+    dt = "f16" if c["x"].dtype == np.float16 else "f32"
+    np.testing.assert_allclose(y.astype(np.float32), c["y"].astype(np.float32),
+                               **(TOL[dt] if dt == "f16" else dict(rtol=1e-5, atol=1e-5)))
+
+
+def test_skip_rms_norm_golden(ops):
+    c = golden_case(NORMS, "skiprms")
+    y, r = ops.skip_rms_norm(cuda(c["x"]), cuda(c["skip"]), cuda(c["gamma"]), 1e-6)
+    np.testing.assert_allclose(to_np(y), c["y"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(to_np(r), c["residual"])
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 4096), (16, 4096), (512, 4096), (3, 8192), (5, 100)])
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_rms_norms_vs_oracle(ops, rows, hidden, dt):
+    rng = np.random.default_rng(rows + hidden)
+    x = rng.standard_normal((rows, hidden)).astype(np.float32)
+    sk = rng.standard_normal((rows, hidden)).astype(np.float32)
+    g = rng.standard_normal(hidden).astype(np.float32)
+    if dt == "f32":
+        conv, back, tdt, odt = (lambda v: v), (lambda v: v), torch.float32, None
+    elif dt == "f16":
+        conv, back, tdt, odt = (lambda v: v.astype(np.float16)), (lambda v: v.astype(np.float32)), torch.float16, None
+    else:
+        conv, back, tdt, odt = oracle.f32_to_bf16_bits, oracle.bf16_bits_to_f32, torch.bfloat16, "bf16"
+    xc, sc, gc = conv(x), conv(sk), conv(g)
+    tx = cuda(xc).view(tdt) if dt == "bf16" else cuda(xc)
+    ts = cuda(sc).view(tdt) if dt == "bf16" else cuda(sc)
+    tg = cuda(gc).view(tdt) if dt == "bf16" else cuda(gc)
+    tol = TOL[dt] if dt != "f32" else dict(rtol=1e-5, atol=1e-5)
+    want = back(oracle.rms_norm(xc, gc, 1e-5, dtype=odt))
+    got = ops.rms_norm(tx, tg, 1e-5)
+    np.testing.assert_allclose(to_np(got.float()), want, **tol)
+    wy, wr = oracle.skip_rms_norm(xc, sc, gc, 1e-5, dtype=odt)
+    y, r = ops.skip_rms_norm(tx, ts, tg, 1e-5)
+    np.testing.assert_allclose(to_np(y.float()), back(wy), **tol)
+    np.testing.assert_array_equal(to_np(r.float()), back(wr))
+
+
+# ---- GroupQueryAttention -------------------------------------------------------------------
+GQA = load_golden("gqa.npz")
+GQA_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "gqa")
+
+
+def run_gqa_case(ops, c, a, shared):
+    """Drive the shared-buffer kernel; the growing contract copies past into a present buffer."""
+    S = c["query"].shape[1]
+    total = int(c["total_sequence_length"][0])
+    past_cap = c["past_key"].shape[2]
+    if shared:
+        kk, vv = cuda(c["past_key"]), cuda(c["past_value"])
+    else:
+        B, HK, _, D = c["past_key"].shape
+        kk = torch.zeros(B, HK, total, D, dtype=torch.float32, device="cuda")
+        vv = torch.zeros_like(kk)
+        kk[:, :, :past_cap] = cuda(c["past_key"])
+        vv[:, :, :past_cap] = cuda(c["past_value"])
+    packed = "key" not in c
+    rope = "cos_cache" in c and a.get("do_rotary", 1)
+    out = ops.group_query_attention(
+        cuda(c["query"]), None if packed else cuda(c["key"]), None if packed else cuda(c["value"]), kk, vv,
+        cuda(c["seqlens_k"]), cuda(c["cos_cache"]) if rope else None, cuda(c["sin_cache"]) if rope else None,
+        num_heads=a["num_heads"], kv_heads=a["kv_num_heads"], scale=a.get("scale", 0.0),
+        do_rotary=rope, interleaved=a.get("rotary_interleaved", 0),
+        q_norm=cuda(c["q_norm"]) if "q_norm" in c else None, k_norm=cuda(c["k_norm"]) if "k_norm" in c else None,
+        qk_norm_eps=a.get("qk_norm_epsilon", 1e-6),
+        attention_bias=cuda(c["attention_bias"]) if "attention_bias" in c else None)
+    return to_np(out), to_np(kk), to_np(vv), total, S
+
+
+@pytest.mark.parametrize("name", GQA_CASES)
+def test_gqa_golden(ops, name):
+    meta, c = MANIFEST[name], golden_case(GQA, name)
+    out, pk, pv, total, S = run_gqa_case(ops, c, meta["attrs"], meta["shared"])
+    np.testing.assert_allclose(out, c["out"], rtol=2e-5, atol=2e-5)
+    np.testing.assert_allclose(pk[:, :, :total], c["present_key"][:, :, :total], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(pv[:, :, :total], c["present_value"][:, :, :total])
+    if meta["shared"]:  # rows beyond the valid prefix are untouched
+        np.testing.assert_array_equal(pk[:, :, total:], c["past_key"][:, :, total:])
+
+
+def make_gqa_inputs(rng, B, S, H, HK, D, past, cap, dtype=np.float16, max_seq=None):
+    q = rng.standard_normal((B, S, H * D)).astype(dtype)
+    k = rng.standard_normal((B, S, HK * D)).astype(dtype)
+    v = rng.standard_normal((B, S, HK * D)).astype(dtype)
+    kc = np.zeros((B, HK, cap, D), dtype=dtype)
+    vc = np.zeros((B, HK, cap, D), dtype=dtype)
+    kc[:, :, :past] = rng.standard_normal((B, HK, past, D)).astype(dtype)
+    vc[:, :, :past] = rng.standard_normal((B, HK, past, D)).astype(dtype)
+    max_seq = max_seq or cap + 4
+    half = D // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half, dtype=np.float64) / half))
+    ang = np.arange(max_seq, dtype=np.float64)[:, None] * inv[None, :]
+    cos, sin = np.cos(ang).astype(dtype), np.sin(ang).astype(dtype)
+    seqlens = np.full((B,), past + S - 1, dtype=np.int32)
+    return q, k, v, kc, vc, cos, sin, seqlens
+
+
+@pytest.mark.parametrize("B,past", [(1, 128), (1, 1024), (1, 8191), (8, 512), (8, 4096)])
+def test_gqa_config2_decode_fp16(ops, B, past):
+    """32 q heads, 8 kv heads, D 128, fp16, rotary base 10000 non-interleaved."""
+    rng = np.random.default_rng(B * 100003 + past)
+    H, HK, D, S = 32, 8, 128, 1
+    cap = past + S + 7
+    q, k, v, kc, vc, cos, sin, seqlens = make_gqa_inputs(rng, B, S, H, HK, D, past, cap)
+    want, wk, wv = oracle.gqa(q, k, v, kc.copy(), vc.copy(), seqlens, cos, sin, num_heads=H, kv_heads=HK,
+                              shared_buffer=True)
+    tk, tv = cuda(kc), cuda(vc)
+    out = ops.group_query_attention(cuda(q), cuda(k), cuda(v), tk, tv, cuda(seqlens), cuda(cos), cuda(sin),
+                                    num_heads=H, kv_heads=HK)
+    np.testing.assert_allclose(to_np(out).astype(np.float32), want.astype(np.float32), **TOL["f16"])
+    np.testing.assert_array_equal(to_np(tk), wk)  # append is bit-exact (same fp32 RoPE, one rounding)
+    np.testing.assert_array_equal(to_np(tv), wv)
+
+
+@pytest.mark.parametrize("S,H,HK,D,interleaved,window", [(1, 32, 8, 128, 1, -1), (2, 32, 8, 128, 0, -1),
+                                                        (3, 8, 1, 64, 0, 5), (1, 14, 2, 64, 0, -1),
+                                                        (1, 16, 16, 128, 0, -1), (4, 8, 2, 256, 0, -1)])
+def test_gqa_variants_fp16(ops, S, H, HK, D, interleaved, window):
+    rng = np.random.default_rng(S * 31 + H + D)
+    B, past = 2, 300
+    cap = past + S + 3
+    q, k, v, kc, vc, cos, sin, _ = make_gqa_inputs(rng, B, S, H, HK, D, past, cap)
+    seqlens = np.array([past + S - 1, past - 40 + S - 1], dtype=np.int32)  # ragged batch
+    want, wk, wv = oracle.gqa(q, k, v, kc.copy(), vc.copy(), seqlens, cos, sin, num_heads=H, kv_heads=HK,
+                              interleaved=interleaved, shared_buffer=True, local_window=window)
+    tk, tv = cuda(kc), cuda(vc)
+    out = ops.group_query_attention(cuda(q), cuda(k), cuda(v), tk, tv, cuda(seqlens), cuda(cos), cuda(sin),
+                                    num_heads=H, kv_heads=HK, interleaved=interleaved, local_window=window)
+    np.testing.assert_allclose(to_np(out).astype(np.float32), want.astype(np.float32), **TOL["f16"])
+    np.testing.assert_array_equal(to_np(tk), wk)
+    np.testing.assert_array_equal(to_np(tv), wv)
+
+
+def test_gqa_bf16_decode(ops):
+    rng = np.random.default_rng(11)
+    B, S, H, HK, D, past = 1, 1, 32, 8, 128, 2000
+    cap = past + 64
+    q, k, v, kc, vc, cos, sin, seqlens = make_gqa_inputs(rng, B, S, H, HK, D, past, cap, dtype=np.float32)
+    bf = oracle.f32_to_bf16_bits
+    args = [bf(x) for x in (q, k, v, kc, vc, cos, sin)]
+    kco, vco = args[3].copy(), args[4].copy()
+    want, wk, _ = oracle.gqa(args[0], args[1], args[2], kco, vco, seqlens, args[5], args[6], num_heads=H,
+                             kv_heads=HK, shared_buffer=True, dtype="bf16")
+    t = [cuda(x).view(torch.bfloat16) for x in args]
+    out = ops.group_query_attention(t[0], t[1], t[2], t[3], t[4], cuda(seqlens), t[5], t[6], num_heads=H,
+                                    kv_heads=HK)
+    np.testing.assert_allclose(to_np(out.float()), oracle.bf16_bits_to_f32(want), **TOL["bf16"])
+    np.testing.assert_array_equal(to_np(t[3].view(torch.int16)).view(np.uint16), wk)
+
+
+def test_gqa_repeated_decode_steps_match_oracle(ops):
+    """Sixteen consecutive decode steps on one shared buffer: the arrival counters reset and the
+    append offset advances from device-side seqlens_k."""
+    rng = np.random.default_rng(3)
+    B, H, HK, D, past0, steps = 2, 32, 8, 128, 700, 16
+    cap = past0 + steps + 1
+    q, k, v, kc, vc, cos, sin, _ = make_gqa_inputs(rng, B, 1, H, HK, D, past0, cap)
+    tk, tv = cuda(kc), cuda(vc)
+    ok, ov = kc.copy(), vc.copy()
+    for t in range(steps):
+        qs = rng.standard_normal(q.shape).astype(np.float16)
+        ks = rng.standard_normal(k.shape).astype(np.float16)
+        vs = rng.standard_normal(v.shape).astype(np.float16)
+        seqlens = np.full((B,), past0 + t, dtype=np.int32)
+        want, ok, ov = oracle.gqa(qs, ks, vs, ok, ov, seqlens, cos, sin, num_heads=H, kv_heads=HK,
+                                  shared_buffer=True)
+        out = ops.group_query_attention(cuda(qs), cuda(ks), cuda(vs), tk, tv, cuda(seqlens), cuda(cos),
+                                        cuda(sin), num_heads=H, kv_heads=HK)
+        np.testing.assert_allclose(to_np(out).astype(np.float32), want.astype(np.float32), **TOL["f16"])
+    np.testing.assert_array_equal(to_np(tk), ok)
+
+
+def test_gqa_out_of_range_is_reported_not_faulted(ops):
+    rng = np.random.default_rng(4)
+    B, S, H, HK, D, past = 1, 1, 8, 2, 64, 10
+    cap = 12
+    q, k, v, kc, vc, cos, sin, _ = make_gqa_inputs(rng, B, S, H, HK, D, past, cap)
+    seqlens = np.array([cap + 5], dtype=np.int32)  # beyond the buffer: the kernel must refuse it
+    ops.group_query_attention(cuda(q), cuda(k), cuda(v), cuda(kc), cuda(vc), cuda(seqlens), cuda(cos),
+                              cuda(sin), num_heads=H, kv_heads=HK)
+    torch.cuda.synchronize()
+    code, _ = ops.device_error(clear=True)
+    assert code == 101
