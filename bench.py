@@ -1,0 +1,482 @@
+"""Benchmark: Llama-3-8B-shaped int4 decode tokens/s through the B200 EP.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Workload (single GPU): 32 layers, hidden 4096, 32/8 heads, head 128, FFN 14336,
+vocab 128256, every projection MatMulNBits int4 block 32 with fp16 scales and uint8 zero points,
+random-init weights (seed 0), int4 GatherBlockQuantized embedding, prompt of 1024 random token
+ids prefilled through the same EP graph (untimed), then decode steps.  One step = one decode
+token for every sequence of the batch: the whole graph runs as one compiled partition (a CUDA
+graph replay) whose positions advance from device-side seqlens_k.
+
+Reported: `value` = decode tokens/s with inputs resident in HBM (CUDA events, max over ranks);
+`e2e` = the same through the compiled partition's C ABI with host buffers (token ids and
+sequence lengths staged host->device, logits read back every step); `roofline` = the dominant
+kernel (the fused gate/up MatMulNBits GEMV) timed live with CUDA events on a weight set larger
+than L2; `cpu_baseline` = the C oracle timed on the host cores for one decoder layer + lm_head
+and extrapolated to 32 layers.  --impl reference times that CPU oracle path alone (the
+reference implementation — Rust over MLX/Metal — cannot run on Linux; ORT's CPU EP is not
+installable here).
+
+Multi-GPU: one process per GPU under torchrun; every rank runs its own replica of the model on
+its batch (weak scaling); value = all ranks' tokens / max rank time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "onnxruntime-mlx_b200"))
+sys.path.insert(0, ROOT)
+
+PROMPT = 1024
+GEN = 256
+HBM_FALLBACK = 6553.0
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:  # noqa: BLE001
+        return {"hbm_gbs": HBM_FALLBACK, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                parts = [p.strip() for p in out.stdout.strip().split(",")]
+                if len(parts) >= 9:
+                    self.samples.append(parts)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if "Active" in s[5 + i]
+                          and "Not" not in s[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- the CPU baseline (oracle port) --------------------------------------------------------
+def cpu_layer_sample(cfg, batch, ctx, threads=0):
+    """One decoder layer + lm_head of a decode step on the C oracle; returns (seconds, desc)."""
+    import numpy as np
+
+    from oracle import oracle
+    from onnxruntime_ep_b200.decoder import quantize_params, rotary_caches
+
+    rng = np.random.default_rng(1)
+    dt = np.float16
+    hid, H, HK, D = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim
+    W = {}
+    for name, n, k in (("q", H * D, hid), ("k", HK * D, hid), ("v", HK * D, hid), ("o", hid, H * D),
+                       ("gate", cfg.ffn, hid), ("up", cfg.ffn, hid), ("down", hid, cfg.ffn),
+                       ("lm", cfg.vocab, hid)):
+        W[name] = (quantize_params(rng, n, k, cfg.block, dt), n, k)
+    x = rng.standard_normal((batch, 1, hid)).astype(dt)
+    g = rng.uniform(0.8, 1.2, hid).astype(dt)
+    cap = ctx + 8
+    kc = rng.standard_normal((batch, HK, cap, D)).astype(dt)
+    vc = rng.standard_normal((batch, HK, cap, D)).astype(dt)
+    cos, sin = rotary_caches(cap + 8, D, 10000.0, dt)
+    seq = np.full(batch, ctx, np.int32)
+
+    def mnb(a, key):
+        (b, s, z), n, k = W[key]
+        return oracle.matmulnbits(a, b, s, z, N=n, K=k, threads=threads)
+
+    t0 = time.perf_counter()
+    n1 = oracle.rms_norm(x, g, 1e-5, threads=threads)
+    q, k, v = mnb(n1, "q"), mnb(n1, "k"), mnb(n1, "v")
+    attn, _, _ = oracle.gqa(q, k, v, kc, vc, seq, cos, sin, num_heads=H, kv_heads=HK, shared_buffer=True,
+                            threads=threads)
+    o = mnb(attn, "o")
+    n2, r2 = oracle.skip_rms_norm(o, x, g, 1e-5, threads=threads)
+    ga, up = mnb(n2, "gate").astype(np.float32), mnb(n2, "up").astype(np.float32)
+    h = (ga / (1 + np.exp(-ga)) * up).astype(dt)
+    mnb(h, "down")
+    t_layer = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    mnb(n2, "lm")
+    t_lm = time.perf_counter() - t0
+    return t_layer, t_lm
+
+
+def cpu_baseline(cfg, batch, samples=2):
+    from oracle import oracle
+
+    oracle.build()
+    cores = oracle.max_threads()
+    cpu_layer_sample(cfg, batch, PROMPT)  # warm (page in, thread pool)
+    best = None
+    for _ in range(samples):
+        tl, tlm = cpu_layer_sample(cfg, batch, PROMPT)
+        step = cfg.layers * tl + tlm
+        best = step if best is None else min(best, step)
+    return {"value": batch / best, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"C oracle, 1 decoder layer + lm_head of a B={batch} decode step at context {PROMPT}, "
+                      f"extrapolated to {cfg.layers} layers (best of {samples}); ORT CPU EP unavailable here"}
+
+
+# ---- the GPU arm ---------------------------------------------------------------------------
+def dominant_kernel_roofline(batch, peaks, peak_kind):
+    """Live CUDA-event timing of the fused gate/up GEMV shape (N = 2 x 14336, K = 4096, int4 block
+    32, fp16 scales + uint8 zp) over rotating weight copies larger than L2."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    K, N, block = 4096, 2 * 14336, 32
+    nb = K // block
+    per = N * nb * block // 2 + N * nb * 2 + N * nb // 2
+    copies = max(3, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    Bs = [torch.randint(0, 256, (N, nb, block // 2), dtype=torch.uint8, device="cuda", generator=g)
+          for _ in range(copies)]
+    Ss = [(torch.rand(N * nb, device="cuda", generator=g) * 0.01 + 0.001).half() for _ in range(copies)]
+    Zs = [torch.randint(0, 256, (N * nb // 2,), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    a = torch.randn(batch, K, device="cuda").half()
+    y = torch.empty(batch, N, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            ops.matmulnbits(a, Bs[i], Ss[i], Zs[i], K=K, N=N, out=y)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                ops.matmulnbits(a, Bs[i], Ss[i], Zs[i], K=K, N=N, out=y)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    alg = per + a.numel() * 2 + y.numel() * 2
+    achieved = alg / launch_s / 1e9
+    peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
+    traffic = None
+    summ = os.path.join(ROOT, "profiles", "mnb_gemv_gate_up_fp16.txt")
+    if os.path.exists(summ):
+        for line in open(summ):
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = int(float(line.split(":")[1]))
+    return {"kernel": "mnb_gemv_kernel (fused gate/up: N=28672, K=4096, int4 b32, fp16)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
+            "launch_us": round(launch_s * 1e6, 2), "traffic": traffic}
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ep as E
+    from onnxruntime_ep_b200.decoder import LLAMA3_8B, build_decoder
+
+    cfg = LLAMA3_8B
+    B = args.batch
+    cap = PROMPT + GEN + 64
+    t_build = time.time()
+    g = build_decoder(cfg, batch=-1, seq=-1, cap=-1)
+    sess = E.Session(g)
+    part = sess.parts[0]
+    t_build = time.time() - t_build
+
+    kv = []
+    for i in range(cfg.layers):
+        kv.append([torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda")
+                   for _ in range(2)])
+    names_in = part.input_names
+    names_out = part.output_names
+
+    def bind(ids, seqlens, total, logits):
+        feeds = {"input_ids": ids, "seqlens_k": seqlens, "total_sequence_length": total}
+        outs = {"logits": logits}
+        for i in range(cfg.layers):
+            feeds[f"past_key_values.{i}.key"], feeds[f"past_key_values.{i}.value"] = kv[i]
+            outs[f"present.{i}.key"], outs[f"present.{i}.value"] = kv[i]
+        ins = (E.Tensor * len(names_in))(*[E.make_tensor(feeds[n]) for n in names_in])
+        out = (E.Tensor * len(names_out))(*[E.make_tensor(outs[n]) for n in names_out])
+        return ins, out
+
+    L = E._lib()
+    stream = torch.cuda.current_stream()
+
+    def step(ins, outs):
+        E.check(L.b200ep_compiled_run(part._c, ins, len(names_in), outs, len(names_out),
+                                      ctypes.c_void_p(stream.cuda_stream)))
+
+    # prefill the prompt through the same graph (untimed)
+    rng = np.random.default_rng(rank)
+    prompt = torch.from_numpy(rng.integers(0, cfg.vocab, size=(B, PROMPT), dtype=np.int64)).cuda()
+    pre_logits = torch.empty(B, PROMPT, cfg.vocab, dtype=torch.float16, device="cuda")
+    t_pre = time.time()
+    ins, outs = bind(prompt, torch.full((B,), PROMPT - 1, dtype=torch.int32, device="cuda"),
+                     torch.tensor([PROMPT], dtype=torch.int32, device="cuda"), pre_logits)
+    step(ins, outs)
+    torch.cuda.synchronize()
+    t_pre = time.time() - t_pre
+    del pre_logits
+
+    # decode: persistent device buffers, advanced in place every step
+    ids = torch.zeros(B, 1, dtype=torch.int64, device="cuda")
+    seqlens = torch.full((B,), PROMPT - 1, dtype=torch.int32, device="cuda")
+    total = torch.tensor([PROMPT], dtype=torch.int32, device="cuda")
+    logits = torch.empty(B, 1, cfg.vocab, dtype=torch.float16, device="cuda")
+    pool = torch.from_numpy(rng.integers(0, cfg.vocab, size=(max(GEN, args.steps + args.warmup) + 8, B, 1),
+                                         dtype=np.int64)).cuda()
+    ins, outs = bind(ids, seqlens, total, logits)
+    n_step = [0]
+
+    def decode_step():
+        ids.copy_(pool[n_step[0] % pool.shape[0]])
+        seqlens.add_(1)
+        total.add_(1)
+        step(ins, outs)
+        n_step[0] += 1
+
+    def reset_positions():
+        seqlens.fill_(PROMPT - 1)
+        total.fill_(PROMPT)
+
+    for _ in range(args.warmup):
+        decode_step()
+    torch.cuda.synchronize()
+    reset_positions()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            decode_step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+    value = world * B * args.steps / dev_s
+
+    # e2e through the C ABI with host buffers: ids / lengths staged H2D, logits read back per step
+    h_ids = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
+    h_seq = torch.full((B,), PROMPT - 1, dtype=torch.int32).pin_memory()
+    h_tot = torch.tensor([PROMPT], dtype=torch.int32).pin_memory()
+    h_logits = torch.empty(B, 1, cfg.vocab, dtype=torch.float16).pin_memory()
+    ins_h, outs_h = bind(h_ids, h_seq, h_tot, h_logits)
+    pool_h = pool.cpu()
+
+    def e2e_step(t):
+        h_ids.copy_(pool_h[t % pool_h.shape[0]])
+        h_seq.add_(1)
+        h_tot.add_(1)
+        step(ins_h, outs_h)  # synchronises: the logits are host-resident
+
+    for t in range(max(2, args.warmup)):
+        e2e_step(t)
+    h_seq.fill_(PROMPT - 1)
+    h_tot.fill_(PROMPT)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record()
+    for t in range(args.steps):
+        e2e_step(t)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    e2e_s = max_over_ranks(max(e0.elapsed_time(e1) / 1e3, wall), world)
+    e2e = {"value": round(world * B * args.steps / e2e_s, 2), "unit": "tokens/s",
+           "h2d_bytes_per_step": B * 8 + B * 4 + 4, "d2h_bytes_per_step": B * cfg.vocab * 2,
+           "path": "b200ep_compiled_run with pinned host tensors"}
+
+    peaks, peak_kind = measured_peaks()
+    roof = dominant_kernel_roofline(B, peaks, peak_kind)
+    desc = json.loads(part.describe())
+    result = {
+        "metric": f"int4 decode tokens/s (Llama-3-8B shape, batch {B})",
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dev_s / args.steps * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 weights, fp16 activations, fp32 accumulate",
+        "data": "synthetic: random-init int4 weights (seed 0), random token ids",
+        "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)",
+                   "layers": cfg.layers, "hidden": cfg.hidden, "heads": f"{cfg.heads}/{cfg.kv_heads}",
+                   "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B, "global_batch": B * world,
+                   "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + args.steps}",
+                   "kv_capacity": cap, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "weights 4.4 GB/step streamed from HBM (>> 126 MB L2)",
+                   "cuda_graph_replays": desc["graph_replays"], "fused_qkv": desc["fused_qkv"],
+                   "fused_swiglu": desc["fused_swiglu"], "prefill_s": round(t_pre, 2),
+                   "build_compile_s": round(t_build, 1)},
+        "e2e": e2e,
+        "roofline": roof,
+        "clocks": clocks.summary(),
+        "gpu_launches": part.launches_per_run() * args.steps,
+    }
+    if rank == 0 and not args.no_cpu:
+        result["cpu_baseline"] = cpu_baseline(cfg, B)
+    return result
+
+
+def run_reference(args, rank, world):
+    """The reference path's CPU timing (oracle port; see module docstring)."""
+    from onnxruntime_ep_b200.decoder import LLAMA3_8B
+
+    if rank != 0:
+        return None
+    from oracle import oracle
+
+    oracle.build()
+    cfg = LLAMA3_8B
+    B = args.batch
+    cores = oracle.max_threads()
+    for _ in range(max(1, min(args.warmup, 1))):
+        cpu_layer_sample(cfg, B, PROMPT)
+    t_total = 0.0
+    for _ in range(args.steps):
+        tl, tlm = cpu_layer_sample(cfg, B, PROMPT)
+        t_total += cfg.layers * tl + tlm
+    value = B * args.steps / t_total
+    sample = (f"C oracle (restatement of ORT CPU semantics), one decoder layer + lm_head per step at context "
+              f"{PROMPT}, extrapolated to {cfg.layers} layers; reference (Rust/MLX/Metal) and ORT CPU EP "
+              f"cannot run here")
+    return {
+        "impl": "reference",
+        "metric": f"int4 decode tokens/s (Llama-3-8B shape, batch {B})",
+        "value": round(value, 4),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_total / args.steps * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 weights, fp16 activations, double accumulate",
+        "data": "synthetic",
+        "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)", "batch": B},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    rank, world, local = dist_setup(args.gpus)
+    res = run_ours(args, rank, world, local)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

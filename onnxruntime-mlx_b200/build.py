@@ -70,6 +70,8 @@ def compile_one(src, force, ptxas_v):
         inc += ["-I", nccl_inc, "-DB200EP_HAVE_NCCL=1"]
     cmd = [NVCC, "-ccbin", HOST_CXX, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", "-c", src, "-o", obj, *inc]
+    if src.endswith(".cpp"):
+        cmd += ["-x", "cu"]  # host code shares the CUDA headers of the kernels
     if ptxas_v and src.endswith(".cu"):
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)

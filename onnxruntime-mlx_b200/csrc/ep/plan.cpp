@@ -1,0 +1,919 @@
+#include "plan.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <set>
+#include <sstream>
+#include <unordered_map>
+
+#include "../common.cuh"
+#include "../kernels/elementwise.h"
+#include "../kernels/kernels.h"
+#include "tp.h"
+
+namespace b200ep {
+
+DeviceErrorSlot* device_error_slot();
+
+DevMem::~DevMem() {
+  if (p) cudaFree(p);
+}
+
+int DevMem::alloc(size_t n) {
+  if (cudaMalloc(&p, std::max<size_t>(n, 16)) != cudaSuccess) {
+    cudaGetLastError();
+    p = nullptr;
+    return set_error(B200EP_ENOMEM, "device allocation of " + std::to_string(n) + " bytes failed");
+  }
+  bytes = n;
+  return B200EP_OK;
+}
+
+struct Plan::Program {
+  std::vector<Slot> slots;
+  std::vector<std::unique_ptr<DevMem>> mems;
+  std::map<std::string, cudaGraphExec_t> graphs;
+  ~Program() {
+    for (auto& kv : graphs)
+      if (kv.second) cudaGraphExecDestroy(kv.second);
+  }
+};
+
+Plan::~Plan() {
+  programs_.clear();
+  if (stream_) cudaStreamDestroy(stream_);
+  if (ev_in_) cudaEventDestroy(ev_in_);
+  if (ev_out_) cudaEventDestroy(ev_out_);
+}
+
+namespace {
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? "," : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+int64_t numel_of(const std::vector<int64_t>& s) {
+  int64_t n = 1;
+  for (auto d : s) n *= d;
+  return n;
+}
+
+bool env_on(const char* name) {
+  const char* v = getenv(name);
+  return v && *v && strcmp(v, "0") != 0;
+}
+
+}  // namespace
+
+int Plan::slot_of(const std::string& name) {
+  auto it = slot_index_.find(name);
+  if (it != slot_index_.end()) return it->second;
+  Slot s;
+  s.name = name;
+  slots_.push_back(s);
+  slot_index_[name] = (int)slots_.size() - 1;
+  return (int)slots_.size() - 1;
+}
+
+// ---- lowering -------------------------------------------------------------------------------
+int Plan::lower(const Graph& g, const std::vector<int>& nodes, std::string* err) {
+  std::set<std::string> produced;
+  for (int ni : nodes)
+    for (auto& o : g.nodes[ni].outputs)
+      if (!o.empty()) produced.insert(o);
+  std::set<int> inset(nodes.begin(), nodes.end());
+
+  auto value_slot = [&](const std::string& name) -> int {
+    if (name.empty()) return -1;
+    auto it = slot_index_.find(name);
+    if (it != slot_index_.end()) return it->second;
+    int id = slot_of(name);
+    Slot& s = slots_[id];
+    if (auto* init = g.initializer(name)) {
+      s.kind = Slot::kConst;
+      s.dtype = init->dtype;
+      s.cshape = init->shape;
+      pending_consts_[id] = g.initializers.at(name);
+    } else if (!produced.count(name)) {
+      s.kind = Slot::kInput;
+      s.io = (int)in_names_.size();
+      in_names_.push_back(name);
+      if (auto* vi = g.value(name)) s.dtype = vi->dtype;
+    } else if (auto* vi = g.value(name)) {
+      s.dtype = vi->dtype;
+    }
+    return id;
+  };
+
+  for (int ni : nodes) {
+    const Node& n = g.nodes[ni];
+    NodeView view(g, n);
+    const OpEntry* e = find_entry(n.domain, n.op_type, g.opset(n.domain));
+    if (!e) {
+      *err = "no handler for " + n.op_type;
+      return B200EP_EUNSUPPORTED;
+    }
+    Step st{};
+    st.name = n.name.empty() ? n.op_type : n.name;
+    for (auto& in : n.inputs) st.in.push_back(value_slot(in));
+    for (auto& o : n.outputs) st.out.push_back(o.empty() ? -1 : value_slot(o));
+    switch (e->kind) {
+      case OpKind::kMatMulNBits: {
+        st.kind = StepKind::kMnb;
+        st.K = n.int_attr("K", 0);
+        st.N = n.int_attr("N", 0);
+        st.bits = (int)n.int_attr("bits", 4);
+        st.block = (int)n.int_attr("block_size", 32);
+        st.wB = st.in[1];
+        st.wS = st.in[2];
+        st.wZ = st.in.size() > 3 ? st.in[3] : -1;
+        st.in.resize(1);
+        st.out.resize(1);
+        const int64_t nblocks = (st.K + st.block - 1) / st.block;
+        const Initializer* B = g.initializer(n.inputs[1]);
+        const Initializer* S = g.initializer(n.inputs[2]);
+        if (!B || (int64_t)B->bytes.size() != st.N * nblocks * st.block * st.bits / 8) {
+          *err = "MatMulNBits " + st.name + ": B has " + std::to_string(B ? B->bytes.size() : 0) +
+                 " bytes, expected N*nblocks*block*bits/8";
+          return B200EP_EINVAL;
+        }
+        if (!S || S->numel() != st.N * nblocks) {
+          *err = "MatMulNBits " + st.name + ": scale count does not match N * nblocks";
+          return B200EP_EINVAL;
+        }
+        if (st.wZ >= 0) {
+          const Initializer* Z = g.initializer(n.inputs[3]);
+          const int64_t zcols = st.bits == 4 ? (nblocks + 1) / 2 : nblocks;
+          if (!Z || (int64_t)Z->bytes.size() != st.N * zcols) {
+            *err = "MatMulNBits " + st.name + ": zero_points size does not match N * ceil(nblocks*bits/8)";
+            return B200EP_EINVAL;
+          }
+        }
+        break;
+      }
+      case OpKind::kGroupQueryAttention: {
+        st.kind = StepKind::kGqa;
+        st.num_heads = (int)n.int_attr("num_heads", 0);
+        st.kv_heads = (int)n.int_attr("kv_num_heads", 0);
+        st.packed = !n.input_present(1) && !n.input_present(2);
+        const ValueInfo* q = view.input_info(0);
+        st.head_size = (int)(st.packed ? q->shape[2] / (st.num_heads + 2 * st.kv_heads) : q->shape[2] / st.num_heads);
+        st.do_rotary = (int)(n.int_attr("do_rotary", 1) != 0 && n.input_present(7));
+        st.interleaved = (int)n.int_attr("rotary_interleaved", 0);
+        st.local_window = (int)n.int_attr("local_window_size", -1);
+        st.scale = n.float_attr("scale", 0.f);
+        st.qk_eps = n.float_attr("qk_norm_epsilon", 1e-6f);
+        st.in.resize(16, -1);
+        st.out.resize(3, -1);
+        if (st.out[1] < 0 || st.out[2] < 0) {
+          *err = "GroupQueryAttention " + st.name + ": present_key/present_value outputs are required";
+          return B200EP_EUNSUPPORTED;
+        }
+        break;
+      }
+      case OpKind::kRmsNorm:
+      case OpKind::kSimplifiedLayerNorm:
+        st.kind = StepKind::kRms;
+        st.eps = n.float_attr("epsilon", e->kind == OpKind::kRmsNorm ? 1e-6f : 1e-5f);
+        st.out.resize(1);
+        break;
+      case OpKind::kSkipSimplifiedLayerNorm: {
+        st.kind = StepKind::kRms;
+        st.skip = true;
+        st.eps = n.float_attr("epsilon", 1e-6f);
+        // outputs: [0] normalised, [last] residual sum (norm.rs:241-245); mean/inv-std are never produced
+        int residual = -1;
+        if (n.outputs.size() >= 2) residual = st.out.back();
+        for (size_t i = 1; i + 1 < n.outputs.size() && i < 3; ++i)
+          if (!n.outputs[i].empty()) {
+            const std::string& nm = n.outputs[i];
+            bool used = g.is_graph_output(nm);
+            for (auto& other : g.nodes)
+              for (auto& in : other.inputs) used |= in == nm;
+            if (used) {
+              *err = "SkipSimplifiedLayerNormalization " + st.name + ": mean/inv_std_var outputs are consumed but not produced";
+              return B200EP_EUNSUPPORTED;
+            }
+          }
+        st.out = {st.out[0], residual};
+        break;
+      }
+      case OpKind::kGatherBlockQuantized: {
+        st.kind = StepKind::kGbq;
+        st.block = (int)n.int_attr("block_size", 128);
+        st.wB = st.in[0];
+        st.wS = st.in[2];
+        st.wZ = st.in.size() > 3 ? st.in[3] : -1;
+        const Initializer* D = g.initializer(n.inputs[0]);
+        st.gbq_rows = D->shape[0];
+        st.gbq_dim = D->shape[1] * 2;
+        st.in = {st.in[1]};
+        st.out.resize(1);
+        break;
+      }
+      case OpKind::kAdd:
+      case OpKind::kSub:
+      case OpKind::kMul:
+        st.kind = StepKind::kBinary;
+        st.bop = e->kind == OpKind::kAdd ? kOpAdd : e->kind == OpKind::kSub ? kOpSub : kOpMul;
+        break;
+      case OpKind::kSigmoid:
+        st.kind = StepKind::kSigmoid;
+        break;
+      case OpKind::kCast:
+        st.kind = StepKind::kCast;
+        st.to = (int)n.int_attr("to", 0);
+        break;
+    }
+    steps_.push_back(std::move(st));
+  }
+
+  // boundary outputs: produced here and used outside the partition (or graph outputs)
+  std::set<std::string> outside_uses;
+  for (int ni = 0; ni < (int)g.nodes.size(); ++ni) {
+    if (inset.count(ni)) continue;
+    for (auto& in : g.nodes[ni].inputs) outside_uses.insert(in);
+  }
+  for (int ni : nodes)
+    for (auto& o : g.nodes[ni].outputs) {
+      if (o.empty()) continue;
+      if (g.is_graph_output(o) || outside_uses.count(o)) {
+        int id = slot_index_.at(o);
+        Slot& s = slots_[id];
+        s.kind = Slot::kOutput;
+        s.io = (int)out_names_.size();
+        out_names_.push_back(o);
+        const ValueInfo* vi = g.value(o);
+        out_dtypes_.push_back(vi ? vi->dtype : s.dtype);
+        if (vi) s.dtype = vi->dtype;
+      }
+    }
+  // dtypes of intermediates without value infos: inherit from the step's first float input
+  for (auto& st : steps_)
+    for (int o : st.out)
+      if (o >= 0 && slots_[o].dtype == 0) {
+        if (st.kind == StepKind::kCast) slots_[o].dtype = st.to;
+        else if (st.kind == StepKind::kGbq) slots_[o].dtype = slots_[st.wS].dtype;
+        else if (!st.in.empty() && st.in[0] >= 0) slots_[o].dtype = slots_[st.in[0]].dtype;
+      }
+  return B200EP_OK;
+}
+
+// ---- fusion passes --------------------------------------------------------------------------
+namespace {
+
+struct Uses {
+  std::vector<int> producer;            // slot -> step
+  std::vector<std::vector<int>> users;  // slot -> steps
+};
+
+Uses uses_of(const std::vector<Step>& steps, size_t nslots) {
+  Uses u;
+  u.producer.assign(nslots, -1);
+  u.users.assign(nslots, {});
+  for (int i = 0; i < (int)steps.size(); ++i) {
+    for (int o : steps[i].out)
+      if (o >= 0) u.producer[o] = i;
+    for (int s : steps[i].in)
+      if (s >= 0) u.users[s].push_back(i);
+  }
+  return u;
+}
+
+// concatenate per-row weight arrays (rows along N) of several MatMulNBits initializers
+std::shared_ptr<Initializer> concat_rows(const std::vector<std::shared_ptr<Initializer>>& parts,
+                                         const std::string& name) {
+  auto out = std::make_shared<Initializer>();
+  out->name = name;
+  out->dtype = parts[0]->dtype;
+  int64_t rows = 0;
+  size_t bytes = 0;
+  for (auto& p : parts) {
+    rows += p->shape.empty() ? 0 : p->shape[0];
+    bytes += p->bytes.size();
+  }
+  out->shape = parts[0]->shape;
+  if (!out->shape.empty()) out->shape[0] = rows;
+  out->bytes.reserve(bytes);
+  for (auto& p : parts) out->bytes.insert(out->bytes.end(), p->bytes.begin(), p->bytes.end());
+  return out;
+}
+
+bool same_gemv_family(const Step& a, const Step& b) {
+  return a.kind == StepKind::kMnb && b.kind == StepKind::kMnb && a.in[0] == b.in[0] && a.K == b.K &&
+         a.bits == b.bits && a.block == b.block && (a.wZ >= 0) == (b.wZ >= 0);
+}
+
+}  // namespace
+
+void Plan::fuse_qkv() {
+  for (bool changed = true; changed;) {
+    changed = false;
+    Uses u = uses_of(steps_, slots_.size());
+    for (int gi = 0; gi < (int)steps_.size() && !changed; ++gi) {
+      Step& g = steps_[gi];
+      if (g.kind != StepKind::kGqa || g.packed) continue;
+      const int q = g.in[0], k = g.in[1], v = g.in[2];
+      if (q < 0 || k < 0 || v < 0) continue;
+      const int pq = u.producer[q], pk = u.producer[k], pv = u.producer[v];
+      if (pq < 0 || pk < 0 || pv < 0 || pq == pk || pk == pv || pq == pv) continue;
+      const Step &sq = steps_[pq], &sk = steps_[pk], &sv = steps_[pv];
+      if (!same_gemv_family(sq, sk) || !same_gemv_family(sq, sv)) continue;
+      bool private_outs = true;
+      for (int s : {q, k, v}) private_outs &= slots_[s].kind == Slot::kTemp && u.users[s].size() == 1;
+      if (!private_outs) continue;
+      if (!pending_consts_.count(sq.wB) || !pending_consts_.count(sk.wB) || !pending_consts_.count(sv.wB)) continue;
+      Step m = sq;
+      m.name = sq.name + "+" + sk.name + "+" + sv.name;
+      m.N = sq.N + sk.N + sv.N;
+      auto cat = [&](int a, int b, int c, const std::string& nm) {
+        int id = slot_of(nm);
+        slots_[id].kind = Slot::kConst;
+        auto init = concat_rows({pending_consts_[a], pending_consts_[b], pending_consts_[c]}, nm);
+        slots_[id].dtype = init->dtype;
+        slots_[id].cshape = init->shape;
+        pending_consts_[id] = init;
+        return id;
+      };
+      m.wB = cat(sq.wB, sk.wB, sv.wB, m.name + "#B");
+      m.wS = cat(sq.wS, sk.wS, sv.wS, m.name + "#scales");
+      if (sq.wZ >= 0) m.wZ = cat(sq.wZ, sk.wZ, sv.wZ, m.name + "#zp");
+      const int qkv = slot_of(m.name + "#qkv");
+      slots_[qkv].dtype = slots_[q].dtype;
+      m.out = {qkv};
+      g.in[0] = qkv;
+      g.in[1] = g.in[2] = -1;
+      g.packed = true;
+      const int first = std::min({pq, pk, pv});
+      std::vector<int> drop = {pq, pk, pv};
+      std::sort(drop.rbegin(), drop.rend());
+      for (int d : drop) steps_.erase(steps_.begin() + d);
+      steps_.insert(steps_.begin() + first, m);
+      ++stats_.fused_qkv;
+      changed = true;
+    }
+  }
+}
+
+void Plan::fuse_swiglu() {
+  for (bool changed = true; changed;) {
+    changed = false;
+    Uses u = uses_of(steps_, slots_.size());
+    for (int i3 = 0; i3 < (int)steps_.size() && !changed; ++i3) {
+      const Step& m3 = steps_[i3];
+      if (m3.kind != StepKind::kBinary || m3.bop != kOpMul || m3.in.size() != 2) continue;
+      for (int order = 0; order < 2 && !changed; ++order) {
+        const int silu = m3.in[order], up = m3.in[1 - order];
+        const int i2 = u.producer[silu];
+        if (i2 < 0 || steps_[i2].kind != StepKind::kBinary || steps_[i2].bop != kOpMul) continue;
+        const Step& m2 = steps_[i2];
+        int gate = -1, sig = -1;
+        for (int o2 = 0; o2 < 2; ++o2) {
+          const int a = m2.in[o2], b = m2.in[1 - o2];
+          const int is = u.producer[b];
+          if (is >= 0 && steps_[is].kind == StepKind::kSigmoid && steps_[is].in[0] == a) {
+            gate = a;
+            sig = b;
+          }
+        }
+        if (gate < 0) continue;
+        const int isg = u.producer[sig];
+        const int pg = u.producer[gate], pu = u.producer[up];
+        if (pg < 0 || pu < 0 || pg == pu) continue;
+        const Step &sg = steps_[pg], &su = steps_[pu];
+        if (!same_gemv_family(sg, su) || sg.N != su.N) continue;
+        bool private_vals = true;
+        for (int s : {gate, sig, silu, up}) private_vals &= slots_[s].kind == Slot::kTemp;
+        private_vals &= u.users[gate].size() == 2 && u.users[sig].size() == 1 && u.users[silu].size() == 1 &&
+                        u.users[up].size() == 1;
+        if (!private_vals) continue;
+        if (slots_[m3.out[0]].dtype != slots_[gate].dtype) continue;
+        Step m = sg;
+        m.name = sg.name + "+" + su.name;
+        m.N = sg.N + su.N;
+        auto cat = [&](int a, int b, const std::string& nm) {
+          int id = slot_of(nm);
+          slots_[id].kind = Slot::kConst;
+          auto init = concat_rows({pending_consts_[a], pending_consts_[b]}, nm);
+          slots_[id].dtype = init->dtype;
+          slots_[id].cshape = init->shape;
+          pending_consts_[id] = init;
+          return id;
+        };
+        m.wB = cat(sg.wB, su.wB, m.name + "#B");
+        m.wS = cat(sg.wS, su.wS, m.name + "#scales");
+        if (sg.wZ >= 0) m.wZ = cat(sg.wZ, su.wZ, m.name + "#zp");
+        const int gu = slot_of(m.name + "#gate_up");
+        slots_[gu].dtype = slots_[gate].dtype;
+        m.out = {gu};
+        Step act{};
+        act.kind = StepKind::kSiluMul;
+        act.name = m.name + "#swiglu";
+        act.in = {gu};
+        act.out = {m3.out[0]};
+        act.N = sg.N;
+        std::vector<int> drop = {pg, pu, isg, i2, i3};
+        const int first = std::min(pg, pu);
+        std::sort(drop.rbegin(), drop.rend());
+        for (int d : drop) steps_.erase(steps_.begin() + d);
+        // act goes where m3 was (after removals, positions before i3 shift by the drops before it)
+        int pos_act = i3;
+        for (int d : drop)
+          if (d < i3) --pos_act;
+        steps_.insert(steps_.begin() + pos_act, act);
+        int pos_m = first;
+        steps_.insert(steps_.begin() + std::min<int>(pos_m, pos_act), m);
+        ++stats_.fused_swiglu;
+        changed = true;
+      }
+    }
+  }
+}
+
+int Plan::upload_constants(const Graph& g, std::string* err) {
+  std::set<int> used;
+  for (auto& st : steps_) {
+    for (int s : st.in)
+      if (s >= 0 && slots_[s].kind == Slot::kConst) used.insert(s);
+    for (int s : {st.wB, st.wS, st.wZ})
+      if (s >= 0) used.insert(s);
+  }
+  for (int id : used) {
+    auto it = pending_consts_.find(id);
+    if (it == pending_consts_.end()) {
+      *err = "constant " + slots_[id].name + " has no data";
+      return B200EP_EINTERNAL;
+    }
+    auto mem = std::make_shared<DevMem>();
+    int rc = mem->alloc(it->second->bytes.size());
+    if (rc) {
+      *err = "weight upload: out of device memory";
+      return rc;
+    }
+    if (!it->second->bytes.empty() &&
+        cudaMemcpy(mem->p, it->second->bytes.data(), it->second->bytes.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+      *err = "weight upload failed";
+      return B200EP_ECUDA;
+    }
+    slots_[id].cmem = mem;
+    slots_[id].ptr = mem->p;
+    slots_[id].shape = slots_[id].cshape;
+    if (it->second->bytes.size() <= 64) slots_[id].host_copy = it->second->bytes;
+    stats_.weight_bytes += (int64_t)it->second->bytes.size();
+  }
+  pending_consts_.clear();
+  return B200EP_OK;
+}
+
+std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& nodes, const EpConfig& cfg,
+                                    std::string* err) {
+  std::unique_ptr<Plan> p(new Plan());
+  p->cfg_ = cfg;
+  p->stats_.nodes = (int)nodes.size();
+  if (p->lower(g, nodes, err)) return nullptr;
+  if (cfg.fuse && !env_on("ONNXRUNTIME_EP_B200_NO_FUSION")) {
+    p->fuse_qkv();
+    p->fuse_swiglu();
+  }
+  if (cfg.tp && p->shard_for_tp(err)) return nullptr;
+  if (p->upload_constants(g, err)) return nullptr;
+  p->stats_.steps = (int)p->steps_.size();
+  if (cfg.verbose) fprintf(stderr, "[b200ep] compiled partition: %s\n", p->describe().c_str());
+  return p;
+}
+
+int Plan::shard_for_tp(std::string* err) {
+  if (!cfg_.tp || cfg_.tp->world == 1) return B200EP_OK;
+  *err = "tensor-parallel sharding is not available for this partition";
+  return B200EP_EUNSUPPORTED;
+}
+
+// ---- shape inference ------------------------------------------------------------------------
+int Plan::infer(std::vector<Slot>& S, std::string* err) const {
+  auto fail = [&](const std::string& m) {
+    *err = m;
+    return B200EP_EINVAL;
+  };
+  for (const Step& st : steps_) {
+    switch (st.kind) {
+      case StepKind::kMnb: {
+        const Slot& a = S[st.in[0]];
+        if (a.shape.empty() || a.shape.back() != st.K)
+          return fail("MatMulNBits " + st.name + ": input last dim " + shape_str(a.shape) + " != K=" + std::to_string(st.K));
+        auto sh = a.shape;
+        sh.back() = st.N;
+        S[st.out[0]].shape = sh;
+        break;
+      }
+      case StepKind::kGqa: {
+        const Slot& q = S[st.in[0]];
+        const Slot& pk = S[st.in[3]];
+        if (q.shape.size() != 3 || pk.shape.size() != 4)
+          return fail("GroupQueryAttention " + st.name + ": query must be rank 3 and past_key rank 4");
+        S[st.out[0]].shape = {q.shape[0], q.shape[1], (int64_t)st.num_heads * st.head_size};
+        int64_t cap = pk.shape[2];
+        const Slot& tot = S[st.in[6]];
+        if (tot.kind == Slot::kInput && !tot.host_copy.empty()) {
+          int32_t t = 0;
+          memcpy(&t, tot.host_copy.data(), 4);
+          cap = std::max<int64_t>(cap, t);
+        }
+        for (int o : {1, 2})
+          if (st.out[o] >= 0 && S[st.out[o]].shape.empty())
+            S[st.out[o]].shape = {pk.shape[0], pk.shape[1], cap, pk.shape[3]};
+        break;
+      }
+      case StepKind::kRms:
+        S[st.out[0]].shape = S[st.in[0]].shape;
+        if (st.skip && st.out[1] >= 0) S[st.out[1]].shape = S[st.in[0]].shape;
+        break;
+      case StepKind::kBinary: {
+        const auto &a = S[st.in[0]].shape, &b = S[st.in[1]].shape;
+        const size_t n = std::max(a.size(), b.size());
+        std::vector<int64_t> o(n);
+        for (size_t i = 0; i < n; ++i) {
+          int64_t da = i < a.size() ? a[a.size() - 1 - i] : 1;
+          int64_t db = i < b.size() ? b[b.size() - 1 - i] : 1;
+          if (da != db && da != 1 && db != 1) return fail("binary " + st.name + ": shapes do not broadcast");
+          o[n - 1 - i] = std::max(da, db);
+        }
+        S[st.out[0]].shape = o;
+        break;
+      }
+      case StepKind::kSigmoid:
+      case StepKind::kCast:
+        S[st.out[0]].shape = S[st.in[0]].shape;
+        break;
+      case StepKind::kSiluMul: {
+        auto sh = S[st.in[0]].shape;
+        sh.back() = st.N;
+        S[st.out[0]].shape = sh;
+        break;
+      }
+      case StepKind::kGbq: {
+        auto sh = S[st.in[0]].shape;
+        sh.push_back(st.gbq_dim);
+        S[st.out[0]].shape = sh;
+        break;
+      }
+      case StepKind::kAllReduce:
+        S[st.out[0]].shape = S[st.in[0]].shape;
+        break;
+      case StepKind::kAllGather: {
+        auto sh = S[st.in[0]].shape;
+        sh.back() = st.N;
+        S[st.out[0]].shape = sh;
+        break;
+      }
+    }
+  }
+  return B200EP_OK;
+}
+
+int Plan::output_shapes(const std::vector<TensorArg>& in, std::vector<std::vector<int64_t>>* shapes) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (in.size() != in_names_.size())
+    return set_error(B200EP_EINVAL, "expected " + std::to_string(in_names_.size()) + " inputs, got " +
+                                        std::to_string(in.size()));
+  std::vector<Slot> S = slots_;
+  for (auto& s : S) {
+    if (s.kind == Slot::kInput) {
+      s.shape = in[s.io].shape;
+      if (!in[s.io].on_device && in[s.io].data && numel_of(s.shape) == 1 && dtype_size(s.dtype) <= 8) {
+        s.host_copy.resize(dtype_size(s.dtype));
+        memcpy(s.host_copy.data(), in[s.io].data, s.host_copy.size());
+      }
+    } else if (s.kind != Slot::kConst) {
+      s.shape.clear();
+    }
+  }
+  std::string err;
+  if (infer(S, &err)) return set_error(B200EP_EINVAL, err);
+  shapes->assign(out_names_.size(), {});
+  for (auto& s : S)
+    if (s.kind == Slot::kOutput) (*shapes)[s.io] = s.shape;
+  return B200EP_OK;
+}
+
+// ---- launches -------------------------------------------------------------------------------
+int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t st) {
+  for (const Step& s : steps_) {
+    cudaError_t e = cudaSuccess;
+    switch (s.kind) {
+      case StepKind::kMnb: {
+        const Slot& a = S[s.in[0]];
+        MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
+                  s.wZ >= 0 ? static_cast<const uint8_t*>(S[s.wZ].ptr) : nullptr,
+                  S[s.out[0]].ptr, a.dtype, a.numel() / s.K, s.N, s.K, s.bits, s.block};
+        e = launch_matmulnbits(m, st);
+        break;
+      }
+      case StepKind::kGqa: {
+        const Slot& q = S[s.in[0]];
+        const Slot& past_k = S[s.in[3]];
+        const Slot& past_v = S[s.in[4]];
+        const Slot& pres_k = S[s.out[1]];
+        const Slot& pres_v = S[s.out[2]];
+        const int64_t B = q.shape[0], Sq = q.shape[1];
+        const int64_t pcap = past_k.shape[2], cap = pres_k.shape[2];
+        const int esz = dtype_size(q.dtype);
+        if (pres_k.ptr != past_k.ptr || pres_v.ptr != past_v.ptr) {
+          // growing contract: present = past rows followed by the new rows
+          const int64_t rows = std::min(pcap, cap);
+          const size_t row_bytes = (size_t)s.head_size * esz;
+          for (auto [dst, src] : {std::pair<void*, void*>{pres_k.ptr, past_k.ptr}, {pres_v.ptr, past_v.ptr}}) {
+            if (rows > 0) {
+              e = cudaMemcpy2DAsync(dst, cap * row_bytes, src, pcap * row_bytes, rows * row_bytes,
+                                    B * s.kv_heads, cudaMemcpyDeviceToDevice, st);
+              if (e != cudaSuccess) return cuda_status(e, "GroupQueryAttention present copy");
+            }
+          }
+        }
+        GqaArgs a{};
+        a.p.batch = B;
+        a.p.seq = Sq;
+        a.p.num_heads = s.num_heads;
+        a.p.kv_heads = s.kv_heads;
+        a.p.head_size = s.head_size;
+        a.p.cap = cap;
+        const Slot* cos = s.in[7] >= 0 ? &S[s.in[7]] : nullptr;
+        a.p.do_rotary = s.do_rotary && cos;
+        a.p.max_seq = cos ? cos->shape[0] : 0;
+        a.p.rotary_half = cos ? cos->shape[1] : 0;
+        a.p.interleaved = s.interleaved;
+        a.p.packed_qkv = s.packed;
+        a.p.local_window = s.local_window;
+        a.p.scale = s.scale;
+        a.p.qk_norm_eps = s.qk_eps;
+        if (s.in[10] >= 0) {
+          a.p.bias_batch = S[s.in[10]].shape[0];
+          a.p.bias_total = S[s.in[10]].shape[3];
+          a.bias = S[s.in[10]].ptr;
+        }
+        a.query = q.ptr;
+        a.key = s.packed ? nullptr : S[s.in[1]].ptr;
+        a.value = s.packed ? nullptr : S[s.in[2]].ptr;
+        a.kv_key = pres_k.ptr;
+        a.kv_value = pres_v.ptr;
+        a.seqlens_k = static_cast<const int32_t*>(S[s.in[5]].ptr);
+        a.cos_cache = cos ? cos->ptr : nullptr;
+        a.sin_cache = s.in[8] >= 0 ? S[s.in[8]].ptr : nullptr;
+        a.q_norm = s.in[14] >= 0 ? S[s.in[14]].ptr : nullptr;
+        a.k_norm = s.in[15] >= 0 ? S[s.in[15]].ptr : nullptr;
+        a.out = S[s.out[0]].ptr;
+        a.dtype = q.dtype;
+        a.workspace = S[s.ws_slot].ptr;
+        a.workspace_bytes = (size_t)S[s.ws_slot].numel();
+        int rc = launch_gqa(a, st);
+        if (rc) return rc;
+        continue;
+      }
+      case StepKind::kRms: {
+        const Slot& x = S[s.in[0]];
+        const int64_t hidden = x.shape.back();
+        RmsArgs r{x.ptr, s.skip ? S[s.in[1]].ptr : nullptr, S[s.in[s.skip ? 2 : 1]].ptr, S[s.out[0]].ptr,
+                  s.skip && s.out[1] >= 0 ? S[s.out[1]].ptr : nullptr, x.dtype, x.numel() / hidden, hidden, s.eps};
+        e = launch_rms_norm(r, st);
+        break;
+      }
+      case StepKind::kBinary: {
+        const Slot &a = S[s.in[0]], &b = S[s.in[1]], &y = S[s.out[0]];
+        BinaryGeom gm;
+        gm.rank = (int)y.shape.size();
+        gm.total = y.numel();
+        int64_t sa = 1, sb = 1;
+        for (int d = gm.rank - 1; d >= 0; --d) {
+          gm.out_dims[d] = y.shape[d];
+          const int ia = (int)a.shape.size() - (gm.rank - d), ib = (int)b.shape.size() - (gm.rank - d);
+          const int64_t da = ia >= 0 ? a.shape[ia] : 1, db = ib >= 0 ? b.shape[ib] : 1;
+          gm.a_strides[d] = da == 1 ? 0 : sa;
+          gm.b_strides[d] = db == 1 ? 0 : sb;
+          sa *= da;
+          sb *= db;
+        }
+        e = launch_binary(a.ptr, b.ptr, y.ptr, y.dtype, gm, s.bop, st);
+        break;
+      }
+      case StepKind::kSigmoid:
+        e = launch_sigmoid(S[s.in[0]].ptr, S[s.out[0]].ptr, S[s.in[0]].dtype, S[s.in[0]].numel(), st);
+        break;
+      case StepKind::kSiluMul: {
+        const Slot& gu = S[s.in[0]];
+        e = launch_silu_mul(gu.ptr, S[s.out[0]].ptr, gu.dtype, gu.numel() / (2 * s.N), s.N, st);
+        break;
+      }
+      case StepKind::kCast:
+        e = launch_cast(S[s.in[0]].ptr, S[s.in[0]].dtype, S[s.out[0]].ptr, s.to, S[s.in[0]].numel(), st);
+        break;
+      case StepKind::kGbq: {
+        const Slot& idx = S[s.in[0]];
+        GbqArgs a{static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
+                  s.wZ >= 0 ? static_cast<const uint8_t*>(S[s.wZ].ptr) : nullptr, idx.ptr, idx.dtype,
+                  S[s.out[0]].ptr, S[s.out[0]].dtype, idx.numel(), s.gbq_rows, s.gbq_dim, s.block,
+                  device_error_slot()};
+        e = launch_gather_block_quantized(a, st);
+        break;
+      }
+      case StepKind::kAllReduce:
+      case StepKind::kAllGather: {
+        int rc = tp_collective(*cfg_.tp, s, S, st);
+        if (rc) return rc;
+        continue;
+      }
+    }
+    if (e != cudaSuccess) return cuda_status(e, ("launch " + s.name).c_str());
+  }
+  (void)prog;
+  return B200EP_OK;
+}
+
+int Plan::launches_per_run() const {
+  int n = 0;
+  for (auto& s : steps_) n += 1;
+  return n;
+}
+
+int Plan::run(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t caller) {
+  std::lock_guard<std::mutex> lk(mu_);
+  // Work runs on the plan's own stream (capturable even when the caller uses the legacy
+  // stream), ordered after the caller's prior work and before its later work by two events.
+  if (!stream_) {
+    B200EP_CUDA_RET(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    B200EP_CUDA_RET(cudaEventCreateWithFlags(&ev_in_, cudaEventDisableTiming));
+    B200EP_CUDA_RET(cudaEventCreateWithFlags(&ev_out_, cudaEventDisableTiming));
+  }
+  cudaStream_t st = stream_;
+  B200EP_CUDA_RET(cudaEventRecord(ev_in_, caller));
+  B200EP_CUDA_RET(cudaStreamWaitEvent(st, ev_in_, 0));
+  int rc = run_locked(in, out, st);
+  cudaEventRecord(ev_out_, st);
+  cudaStreamWaitEvent(caller, ev_out_, 0);
+  return rc;
+}
+
+int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t st) {
+  if (in.size() != in_names_.size() || out.size() != out_names_.size())
+    return set_error(B200EP_EINVAL, "run: expected " + std::to_string(in_names_.size()) + " inputs and " +
+                                        std::to_string(out_names_.size()) + " outputs");
+  // shape key: input shapes plus which inputs are host-resident
+  std::string key;
+  for (size_t i = 0; i < in.size(); ++i) key += shape_str(in[i].shape) + (in[i].on_device ? "d" : "h") + ";";
+  for (size_t i = 0; i < out.size(); ++i) key += shape_str(out[i].shape) + (out[i].on_device ? "d" : "h") + ";";
+  auto it = programs_.find(key);
+  if (it == programs_.end()) {
+    auto prog = std::make_unique<Program>();
+    prog->slots = slots_;
+    for (auto& s : prog->slots) {
+      if (s.kind == Slot::kInput) {
+        s.shape = in[s.io].shape;
+        if (in[s.io].dtype != s.dtype && s.dtype != 0)
+          return set_error(B200EP_EINVAL, "input " + s.name + " has dtype " + std::to_string(in[s.io].dtype) +
+                                              ", expected " + std::to_string(s.dtype));
+        s.dtype = in[s.io].dtype;
+        if (!in[s.io].on_device && numel_of(s.shape) == 1 && dtype_size(s.dtype) <= 8) {
+          s.host_copy.resize(dtype_size(s.dtype));
+          memcpy(s.host_copy.data(), in[s.io].data, s.host_copy.size());
+        }
+      } else if (s.kind == Slot::kOutput) {
+        s.shape = out[s.io].shape;  // caller-provided (authoritative for present buffers)
+      } else if (s.kind != Slot::kConst) {
+        s.shape.clear();
+      }
+    }
+    std::string err;
+    if (infer(prog->slots, &err)) return set_error(B200EP_EINVAL, err);
+    for (auto& s : prog->slots)
+      if (s.kind == Slot::kOutput && s.shape != out[s.io].shape)
+        return set_error(B200EP_EINVAL, "output " + s.name + " bound with shape " + shape_str(out[s.io].shape) +
+                                            ", plan computes " + shape_str(s.shape));
+    // workspaces for attention steps
+    for (Step& stp : steps_)
+      if (stp.kind == StepKind::kGqa && stp.ws_slot < 0) {
+        Slot w;
+        w.name = stp.name + "#ws";
+        w.dtype = kU8;
+        stp.ws_slot = (int)slots_.size();
+        slots_.push_back(w);
+        prog->slots.push_back(w);
+      }
+    for (Step& stp : steps_)
+      if (stp.kind == StepKind::kGqa) {
+        const Slot& q = prog->slots[stp.in[0]];
+        b200ep_gqa_params p{};
+        p.batch = q.shape[0];
+        p.seq = q.shape[1];
+        p.num_heads = stp.num_heads;
+        p.kv_heads = stp.kv_heads;
+        p.head_size = stp.head_size;
+        p.cap = prog->slots[stp.out[1]].shape[2];
+        prog->slots[stp.ws_slot].shape = {(int64_t)gqa_workspace_bytes(p)};
+      }
+    // allocate temps (and staging for host boundary tensors)
+    for (size_t i = 0; i < prog->slots.size(); ++i) {
+      Slot& s = prog->slots[i];
+      const bool staged = (s.kind == Slot::kInput && !in[s.io].on_device) || (s.kind == Slot::kOutput && !out[s.io].on_device);
+      if (s.kind == Slot::kTemp || staged) {
+        const size_t bytes = (size_t)std::max<int64_t>(numel_of(s.shape), 1) * std::max(dtype_size(s.dtype), 1);
+        auto mem = std::make_unique<DevMem>();
+        if (int rc = mem->alloc(bytes)) return rc;
+        if (s.dtype == kU8) cudaMemset(mem->p, 0, bytes);  // attention workspaces start zeroed
+        s.ptr = mem->p;
+        prog->mems.push_back(std::move(mem));
+      }
+    }
+    it = programs_.emplace(key, std::move(prog)).first;
+  }
+  Program& prog = *it->second;
+  std::vector<Slot>& S = prog.slots;
+  // bind boundary tensors
+  std::string ptr_key;
+  for (auto& s : S) {
+    if (s.kind == Slot::kInput) {
+      const TensorArg& a = in[s.io];
+      if (a.on_device) {
+        s.ptr = a.data;
+      } else {
+        const size_t bytes = (size_t)numel_of(s.shape) * dtype_size(s.dtype);
+        if (bytes) B200EP_CUDA_RET(cudaMemcpyAsync(s.ptr, a.data, bytes, cudaMemcpyHostToDevice, st));
+        if (!s.host_copy.empty()) memcpy(s.host_copy.data(), a.data, s.host_copy.size());
+      }
+    } else if (s.kind == Slot::kOutput && out[s.io].on_device) {
+      s.ptr = out[s.io].data;
+    }
+    if (s.kind == Slot::kInput || s.kind == Slot::kOutput) {
+      char buf[32];
+      snprintf(buf, sizeof buf, "%p;", s.ptr);
+      ptr_key += buf;
+    }
+  }
+  ++stats_.runs;
+  const bool use_graph = cfg_.cuda_graph && !env_on("ONNXRUNTIME_EP_B200_NO_GRAPH");
+  if (use_graph) {
+    auto g = prog.graphs.find(ptr_key);
+    if (g == prog.graphs.end()) {
+      // The first run of a key executes eagerly (it also initialises lazily configured kernel
+      // attributes); the second captures.
+      if (prog.graphs.count("#warm" + ptr_key) == 0) {
+        prog.graphs["#warm" + ptr_key] = nullptr;
+        if (int rc = launch_steps(S, prog, st)) return rc;
+      } else {
+        cudaStreamCaptureStatus cs;
+        B200EP_CUDA_RET(cudaStreamIsCapturing(st, &cs));
+        if (cs != cudaStreamCaptureStatusNone) {
+          if (int rc = launch_steps(S, prog, st)) return rc;
+        } else {
+          cudaGraph_t graph = nullptr;
+          B200EP_CUDA_RET(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+          int rc = launch_steps(S, prog, st);
+          cudaError_t ce = cudaStreamEndCapture(st, &graph);
+          if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+          }
+          B200EP_CUDA_RET(ce);
+          cudaGraphExec_t exec = nullptr;
+          ce = cudaGraphInstantiate(&exec, graph, 0);
+          cudaGraphDestroy(graph);
+          B200EP_CUDA_RET(ce);
+          prog.graphs[ptr_key] = exec;
+          ++stats_.graph_captures;
+          B200EP_CUDA_RET(cudaGraphLaunch(exec, st));
+          ++stats_.graph_replays;
+        }
+      }
+    } else {
+      B200EP_CUDA_RET(cudaGraphLaunch(g->second, st));
+      ++stats_.graph_replays;
+    }
+  } else {
+    if (int rc = launch_steps(S, prog, st)) return rc;
+  }
+  // host outputs
+  for (auto& s : S)
+    if (s.kind == Slot::kOutput && !out[s.io].on_device) {
+      const size_t bytes = (size_t)numel_of(s.shape) * dtype_size(s.dtype);
+      if (bytes) B200EP_CUDA_RET(cudaMemcpyAsync(out[s.io].data, s.ptr, bytes, cudaMemcpyDeviceToHost, st));
+    }
+  bool any_host_out = false;
+  for (auto& o : out) any_host_out |= !o.on_device;
+  if (any_host_out) B200EP_CUDA_RET(cudaStreamSynchronize(st));
+  return B200EP_OK;
+}
+
+std::string Plan::describe() const {
+  std::ostringstream o;
+  o << "{\"nodes\":" << stats_.nodes << ",\"steps\":" << steps_.size() << ",\"fused_qkv\":" << stats_.fused_qkv
+    << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"weight_bytes\":" << stats_.weight_bytes
+    << ",\"runs\":" << stats_.runs << ",\"graph_captures\":" << stats_.graph_captures
+    << ",\"graph_replays\":" << stats_.graph_replays << ",\"ops\":[";
+  static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
+                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+  for (size_t i = 0; i < steps_.size(); ++i) o << (i ? "," : "") << "\"" << names[(int)steps_[i].kind] << "\"";
+  o << "]}";
+  return o.str();
+}
+
+}  // namespace b200ep

@@ -1,0 +1,153 @@
+// Compiled partition ("plan"): the B200 counterpart of the reference's Plan + compiled closures
+// (rust/src/engine.rs:409-573, rust/src/compiled.rs:503-1203).
+//
+// compile():  lowers the partition's nodes to device steps, uploads the initializers the steps
+//             read (weights stay resident in HBM), and runs the fusion passes
+//               - q/k/v MatMulNBits sharing one input -> one GEMV writing packed QKV, consumed by
+//                 GroupQueryAttention in its packed form;
+//               - gate/up MatMulNBits + Sigmoid/Mul/Mul (SwiGLU) -> one GEMV + one fused SiLU*up.
+// run():      binds the boundary tensors (device pointers in place; host tensors staged), infers
+//             the shapes of the step, allocates per-shape-key buffers once, and launches the
+//             steps.  With CUDA graphs on, the launches of a (shape key, boundary pointers) pair
+//             are captured once and replayed; decode positions come from device-side seqlens_k,
+//             so one graph serves every token of a decode loop.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "graph.h"
+#include "registry.h"
+
+namespace b200ep {
+
+struct TpContext;  // tensor-parallel communicator (tp.h)
+
+struct EpConfig {
+  bool cuda_graph = true;
+  bool fuse = true;
+  bool verbose = false;
+  std::string layer_partitions;  // "" = unset
+  std::shared_ptr<TpContext> tp;  // null = single GPU
+};
+
+struct TensorArg {
+  void* data = nullptr;
+  int dtype = 0;
+  std::vector<int64_t> shape;
+  bool on_device = true;
+};
+
+struct DevMem {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevMem() = default;
+  DevMem(const DevMem&) = delete;
+  DevMem& operator=(const DevMem&) = delete;
+  ~DevMem();
+  int alloc(size_t n);
+};
+
+struct Slot {
+  enum Kind { kTemp, kInput, kOutput, kConst } kind = kTemp;
+  std::string name;
+  int dtype = 0;
+  int io = -1;  // boundary index for inputs / outputs
+  std::shared_ptr<DevMem> cmem;       // constants
+  std::vector<int64_t> cshape;        // constants
+  std::vector<uint8_t> host_copy;     // constants small enough to read on the host
+  // per run
+  std::vector<int64_t> shape;
+  void* ptr = nullptr;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto d : shape) n *= d;
+    return n;
+  }
+};
+
+enum class StepKind { kMnb, kGqa, kRms, kBinary, kSigmoid, kSiluMul, kCast, kGbq, kAllReduce, kAllGather };
+
+struct Step {
+  StepKind kind;
+  std::string name;   // originating node(s)
+  std::vector<int> in, out;
+  // MatMulNBits
+  int64_t K = 0, N = 0;
+  int bits = 4, block = 32;
+  int wB = -1, wS = -1, wZ = -1;
+  // norms
+  float eps = 1e-5f;
+  bool skip = false;
+  // GroupQueryAttention
+  int num_heads = 0, kv_heads = 0, head_size = 0;
+  bool packed = false;
+  int do_rotary = 1, interleaved = 0, local_window = -1;
+  float scale = 0.f, qk_eps = 1e-6f;
+  int ws_slot = -1;  // workspace (temp, zero-filled when allocated)
+  // binary
+  int bop = 0;
+  // cast
+  int to = 0;
+  // GatherBlockQuantized
+  int64_t gbq_rows = 0, gbq_dim = 0;
+  // tensor parallel gather: shard width along the last axis
+  int64_t shard_cols = 0;
+};
+
+struct PlanStats {
+  int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0;
+  int64_t weight_bytes = 0;
+  int64_t runs = 0, graph_replays = 0, graph_captures = 0;
+};
+
+class Plan {
+ public:
+  static std::unique_ptr<Plan> compile(const Graph& g, const std::vector<int>& nodes, const EpConfig& cfg,
+                                       std::string* err);
+  ~Plan();
+  const std::vector<std::string>& input_names() const { return in_names_; }
+  const std::vector<std::string>& output_names() const { return out_names_; }
+  const std::vector<int>& output_dtypes() const { return out_dtypes_; }
+  // Output shapes for the given inputs (host reads only of host-resident scalar inputs).
+  int output_shapes(const std::vector<TensorArg>& in, std::vector<std::vector<int64_t>>* shapes);
+  int run(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t st);
+  std::string describe() const;
+  const PlanStats& stats() const { return stats_; }
+  // number of device kernels one run launches (for the launch-count claim of the bench)
+  int launches_per_run() const;
+
+ private:
+  struct Program;  // per-shape-key buffers and captured graphs
+  Plan() = default;
+  int lower(const Graph& g, const std::vector<int>& nodes, std::string* err);
+  int upload_constants(const Graph& g, std::string* err);
+  void fuse_qkv();
+  void fuse_swiglu();
+  int shard_for_tp(std::string* err);
+  int infer(std::vector<Slot>& slots, std::string* err) const;
+  int launch_steps(const std::vector<Slot>& slots, Program& prog, cudaStream_t st);
+  int run_locked(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t st);
+  int slot_of(const std::string& name);
+
+  EpConfig cfg_;
+  std::vector<Slot> slots_;
+  std::map<std::string, int> slot_index_;
+  std::vector<Step> steps_;
+  std::vector<std::string> in_names_, out_names_;
+  std::vector<int> out_dtypes_;
+  std::map<std::string, std::unique_ptr<Program>> programs_;
+  std::mutex mu_;
+  PlanStats stats_;
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr;
+  // host-side constant data used while lowering / fusing (weights before upload)
+  std::map<int, std::shared_ptr<Initializer>> pending_consts_;
+};
+
+}  // namespace b200ep

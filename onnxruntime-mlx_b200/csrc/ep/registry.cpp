@@ -3,6 +3,8 @@
 // Each predicate restates the accept/reject rules of the reference claim it names.
 #include "registry.h"
 
+#include <algorithm>
+#include <cstdarg>
 #include <cstdio>
 
 namespace b200ep {

@@ -1,0 +1,154 @@
+// Elementwise glue for a decoder partition (reference: rust/src/ops/elementwise.rs:925-985 —
+// Add/Sub/Mul/Sigmoid/Cast) plus the fused SwiGLU produced by the plan's gate/up merge and the
+// int4 GatherBlockQuantized embedding lookup (reference: rust/src/ops/quant.rs:1134-1200).
+// All arithmetic in fp32, one rounding to the output dtype.
+#include "../common.cuh"
+#include "elementwise.h"
+
+namespace b200ep {
+
+template <typename T>
+__global__ void binary_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y,
+                              BinaryGeom g, int op) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < g.total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = i, ia = 0, ib = 0;
+    for (int d = g.rank - 1; d >= 0; --d) {
+      const int64_t c = rem % g.out_dims[d];
+      rem /= g.out_dims[d];
+      ia += c * g.a_strides[d];
+      ib += c * g.b_strides[d];
+    }
+    const float x = to_f<T>(a[ia]), z = to_f<T>(b[ib]);
+    float r = op == kOpAdd ? x + z : op == kOpSub ? x - z : x * z;
+    y[i] = from_f<T>(r);
+  }
+}
+
+template <typename T>
+__global__ void sigmoid_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = to_f<T>(x[i]);
+    y[i] = from_f<T>(1.f / (1.f + __expf(-v)));
+  }
+}
+
+// gu: [rows, 2n] with the gate in columns [0, n) and up in [n, 2n); h = gate * sigmoid(gate) * up
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ h, int64_t rows, int64_t n) {
+  const int64_t total = rows * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n, c = i - r * n;
+    const float g = to_f<T>(gu[r * 2 * n + c]);
+    const float u = to_f<T>(gu[r * 2 * n + n + c]);
+    h[i] = from_f<T>(g / (1.f + __expf(-g)) * u);
+  }
+}
+
+template <typename TI, typename TO>
+__global__ void cast_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = from_f<TO>(to_f<TI>(x[i]));
+}
+
+// one warp per gathered row; indices int32 or int64, negative indices wrap (quant.rs:1134-1200)
+template <typename T, typename TI>
+__global__ void gbq_kernel(const uint8_t* __restrict__ data, const T* __restrict__ scales,
+                           const uint8_t* __restrict__ zp, const TI* __restrict__ idx, T* __restrict__ out,
+                           int64_t n_idx, int64_t rows, int64_t dim, int block, DeviceErrorSlot* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= n_idx) return;
+  int64_t r = (int64_t)idx[warp];
+  if (r < 0) r += rows;
+  if (r < 0 || r >= rows) {
+    if (lane == 0) report_device_error(err, 201, (int)warp);
+    return;
+  }
+  const int64_t nblocks = dim / block;
+  const uint8_t* row = data + r * (dim / 2);
+  for (int64_t j = lane; j < dim; j += 32) {
+    const uint8_t byte = row[j >> 1];
+    const int q = (j & 1) ? (byte >> 4) : (byte & 0x0f);
+    const int64_t blk = j / block;
+    int z = 8;
+    if (zp) {
+      const uint8_t zb = zp[r * ((nblocks + 1) / 2) + (blk >> 1)];
+      z = (blk & 1) ? (zb >> 4) : (zb & 0x0f);
+    }
+    out[warp * dim + j] = from_f<T>((float)(q - z) * to_f<T>(scales[r * nblocks + blk]));
+  }
+}
+
+namespace {
+int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
+
+template <typename F>
+cudaError_t by_dtype(int dt, F&& f) {
+  switch (dt) {
+    case kF32: return f(float{});
+    case kF16: return f(__half{});
+    case kBF16: return f(__nv_bfloat16{});
+  }
+  return cudaErrorInvalidValue;
+}
+}  // namespace
+
+cudaError_t launch_binary(const void* a, const void* b, void* y, int dtype, const BinaryGeom& g, int op,
+                          cudaStream_t st) {
+  if (g.total == 0) return cudaSuccess;
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    binary_kernel<T><<<grid_for(g.total), 256, 0, st>>>(static_cast<const T*>(a), static_cast<const T*>(b),
+                                                          static_cast<T*>(y), g, op);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_sigmoid(const void* x, void* y, int dtype, int64_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    sigmoid_kernel<T><<<grid_for(n), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y), n);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, int64_t n, cudaStream_t st) {
+  if (rows * n == 0) return cudaSuccess;
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    silu_mul_kernel<T><<<grid_for(rows * n), 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(h), rows, n);
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  return by_dtype(in_dt, [&](auto ti) {
+    using TI = decltype(ti);
+    return by_dtype(out_dt, [&](auto to) {
+      using TO = decltype(to);
+      cast_kernel<TI, TO><<<grid_for(n), 256, 0, st>>>(static_cast<const TI*>(x), static_cast<TO*>(y), n);
+      return cudaGetLastError();
+    });
+  });
+}
+
+cudaError_t launch_gather_block_quantized(const GbqArgs& a, cudaStream_t st) {
+  if (a.n_idx == 0) return cudaSuccess;
+  const int blocks = (int)((a.n_idx * 32 + 255) / 256);
+  return by_dtype(a.dtype, [&](auto tag) {
+    using T = decltype(tag);
+    if (a.idx_dtype == kI64)
+      gbq_kernel<T, int64_t><<<blocks, 256, 0, st>>>(a.data, static_cast<const T*>(a.scales), a.zp,
+                                                     static_cast<const int64_t*>(a.indices), static_cast<T*>(a.out),
+                                                     a.n_idx, a.rows, a.dim, a.block, a.err);
+    else
+      gbq_kernel<T, int32_t><<<blocks, 256, 0, st>>>(a.data, static_cast<const T*>(a.scales), a.zp,
+                                                     static_cast<const int32_t*>(a.indices), static_cast<T*>(a.out),
+                                                     a.n_idx, a.rows, a.dim, a.block, a.err);
+    return cudaGetLastError();
+  });
+}
+
+}  // namespace b200ep

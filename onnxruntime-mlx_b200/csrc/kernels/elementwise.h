@@ -1,0 +1,42 @@
+// Launchers for the elementwise glue kernels used by the EP plan executor.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200ep {
+
+struct DeviceErrorSlot;
+
+enum BinaryOp { kOpAdd = 0, kOpSub = 1, kOpMul = 2 };
+
+// Output dims and per-input element strides (0 on broadcast dims), rank <= 6, row-major.
+struct BinaryGeom {
+  int rank = 0;
+  int64_t total = 0;
+  int64_t out_dims[6] = {};
+  int64_t a_strides[6] = {};
+  int64_t b_strides[6] = {};
+};
+
+cudaError_t launch_binary(const void* a, const void* b, void* y, int dtype, const BinaryGeom& g, int op,
+                          cudaStream_t st);
+cudaError_t launch_sigmoid(const void* x, void* y, int dtype, int64_t n, cudaStream_t st);
+cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, int64_t n, cudaStream_t st);
+cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n, cudaStream_t st);
+
+struct GbqArgs {
+  const uint8_t* data;
+  const void* scales;
+  const uint8_t* zp;
+  const void* indices;
+  int idx_dtype;
+  void* out;
+  int dtype;
+  int64_t n_idx, rows, dim;
+  int block;
+  DeviceErrorSlot* err;
+};
+cudaError_t launch_gather_block_quantized(const GbqArgs& a, cudaStream_t st);
+
+}  // namespace b200ep

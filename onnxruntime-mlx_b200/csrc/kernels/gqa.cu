@@ -61,7 +61,7 @@ struct GqaKP {
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kNW = 4;        // consumer warps
+constexpr int kNW = 8;        // consumer warps
 constexpr int kKT = 32;       // keys per stage
 constexpr int kKPW = kKT / kNW;  // keys per warp per stage
 
@@ -150,6 +150,14 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int D, int esz, int RP,
   return L;
 }
 
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Signal a named barrier without waiting for it to complete.
+__device__ __forceinline__ void named_barrier_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 template <typename T, int EPL, int RP>
 __global__ void __launch_bounds__((kNW + 1) * 32)
 gqa_decode_kernel(GqaKP kp, int stages) {
@@ -160,6 +168,7 @@ gqa_decode_kernel(GqaKP kp, int stages) {
   constexpr int LOGNV = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
   constexpr int SHIFT = 5 - LOGNV;
   constexpr bool QREG = RP * EPL <= 32;
+  constexpr int kThreads = (kNW + 1) * 32;
 
   extern __shared__ __align__(128) unsigned char smem[];
   const DecodeSmem L = decode_smem_layout(D, (int)sizeof(T), RP, stages);
@@ -191,6 +200,8 @@ gqa_decode_kernel(GqaKP kp, int stages) {
   const int kbeg = ok ? min(lo + split * chunk, total) : 0;
   const int kend = ok ? min(kbeg + chunk, total) : 0;
   const int ntiles = (kend - kbeg + kKT - 1) / kKT;
+  // this CTA appends new rows iff its range holds some of [past, total)
+  const bool has_new = ok && kend > past && kbeg < total;
 
   if (threadIdx.x == 0) {
     flags[0] = 0;       // error flag
@@ -203,66 +214,79 @@ gqa_decode_kernel(GqaKP kp, int stages) {
     fence_mbarrier_init();
     if (!ok && split == 0 && kvh == 0) report_device_error(kp.err, kErrGqaRange, b);
   }
-
-  // --- prologue: rotated q rows, fused append of the new k / v rows --------------------------
-  for (int i = threadIdx.x; i < (RP - kp.R) * D; i += (kNW + 1) * 32) qs[kp.R * D + i] = 0.f;
-  if (warp < kNW && ok) {
-    const T* qin = static_cast<const T*>(kp.q);
-    for (int r = warp; r < kp.R; r += kNW) {
-      const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
-      float* row = qs + r * D;
-      const T* src = qin + ((int64_t)b * kp.S + s) * kp.qstride + (int64_t)h * D;
-      for (int i = lane; i < D; i += 32) row[i] = to_f<T>(src[i]);
-      __syncwarp();
-      rotate_row_warp<T>(row, D, past + s, kp, kp.qn);
-    }
-    const T* kin = static_cast<const T*>(kp.k);
-    const T* vin = static_cast<const T*>(kp.v);
-    for (int s = warp; s < kp.S; s += kNW) {
-      const int pos = past + s;
-      if (pos < kbeg || pos >= kend) continue;  // another split owns this row
-      float* row = scratch + warp * D;
-      const int64_t in_off = ((int64_t)b * kp.S + s) * kp.kstride + (int64_t)kvh * D;
-      for (int i = lane; i < D; i += 32) row[i] = to_f<T>(kin[in_off + kp.koff + i]);
-      __syncwarp();
-      rotate_row_warp<T>(row, D, pos, kp, kp.kn);
-      for (int i = lane; i < D; i += 32) {
-        kvk[(int64_t)pos * D + i] = from_f<T>(row[i]);
-        kvv[(int64_t)pos * D + i] = vin[in_off + kp.voff + i];
-      }
-    }
-    fence_proxy_async_global();
-  }
+  for (int i = threadIdx.x; i < (RP - kp.R) * D; i += kThreads) qs[kp.R * D + i] = 0.f;
   __syncthreads();
 
-  // --- producer warp -------------------------------------------------------------------------
   if (warp == kNW) {
-    if (lane == 0 && ok) {
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % stages;
-        if (t >= stages) {
-          if (!mbar_wait(&empty[s], ((t / stages) - 1) & 1)) {
-            atomicExch(&flags[0], 1);
-            break;
+    // --- producer warp: stream K/V tiles from the start; the tile holding the new rows waits
+    // for the consumers' append (named barrier 1).
+    bool gated = false, alive = ok;
+    for (int t = 0; t < ntiles && alive; ++t) {
+      const int s = t % stages;
+      const int j0 = kbeg + t * kKT;
+      const int nk = min(kKT, kend - j0);
+      if (has_new && !gated && j0 + nk > past) {
+        named_barrier(1, kThreads);
+        gated = true;
+      }
+      int go = 1;
+      if (lane == 0) {
+        if (t >= stages && !mbar_wait(&empty[s], ((t / stages) - 1) & 1)) {
+          atomicExch(&flags[0], 1);
+          go = 0;
+        } else {
+          const uint32_t bytes = (uint32_t)(nk * D * sizeof(T));
+          mbar_arrive_expect_tx(&full[s], 2 * bytes);
+          bulk_g2s(kbuf + (size_t)s * kKT * D, kvk + (int64_t)j0 * D, bytes, &full[s]);
+          bulk_g2s(vbuf + (size_t)s * kKT * D, kvv + (int64_t)j0 * D, bytes, &full[s]);
+          flags[2] = t + 1;
+        }
+      }
+      alive = __shfl_sync(0xffffffffu, go, 0) != 0;
+    }
+    if (has_new && !gated) named_barrier(1, kThreads);
+  } else {
+    // --- consumer warps: prologue (rotated q rows; fused append of the new k / v rows) ------
+    if (ok) {
+      const T* qin = static_cast<const T*>(kp.q);
+      for (int r = warp; r < kp.R; r += kNW) {
+        const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
+        float* row = qs + r * D;
+        const T* src = qin + ((int64_t)b * kp.S + s) * kp.qstride + (int64_t)h * D;
+        for (int i = lane; i < D; i += 32) row[i] = to_f<T>(src[i]);
+        __syncwarp();
+        rotate_row_warp<T>(row, D, past + s, kp, kp.qn);
+      }
+      if (has_new) {
+        const T* kin = static_cast<const T*>(kp.k);
+        const T* vin = static_cast<const T*>(kp.v);
+        for (int s = warp; s < kp.S; s += kNW) {
+          const int pos = past + s;
+          if (pos < kbeg || pos >= kend) continue;  // another split owns this row
+          float* row = scratch + warp * D;
+          const int64_t in_off = ((int64_t)b * kp.S + s) * kp.kstride + (int64_t)kvh * D;
+          for (int i = lane; i < D; i += 32) row[i] = to_f<T>(kin[in_off + kp.koff + i]);
+          __syncwarp();
+          rotate_row_warp<T>(row, D, pos, kp, kp.kn);
+          for (int i = lane; i < D; i += 32) {
+            kvk[(int64_t)pos * D + i] = from_f<T>(row[i]);
+            kvv[(int64_t)pos * D + i] = vin[in_off + kp.voff + i];
           }
         }
-        const int j0 = kbeg + t * kKT;
-        const int nk = min(kKT, kend - j0);
-        const uint32_t bytes = (uint32_t)(nk * D * sizeof(T));
-        mbar_arrive_expect_tx(&full[s], 2 * bytes);
-        bulk_g2s(kbuf + (size_t)s * kKT * D, kvk + (int64_t)j0 * D, bytes, &full[s]);
-        bulk_g2s(vbuf + (size_t)s * kKT * D, kvv + (int64_t)j0 * D, bytes, &full[s]);
-        flags[2] = t + 1;
+        fence_proxy_async_global();
+        // release the producer's gated tile; never wait here (the producer may be blocked on a
+        // free stage that only these warps can release)
+        named_barrier_arrive(1, kThreads);
       }
     }
-  } else {
-    // --- consumer warps ----------------------------------------------------------------------
+    named_barrier(2, kNW * 32);  // all q rows rotated
+
     float qreg[QREG ? RP : 1][EPL];
     if (QREG) {
 #pragma unroll
       for (int r = 0; r < (QREG ? RP : 1); ++r)
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) qreg[r][e] = r < kp.R ? qs[r * D + lane * EPL + e] : 0.f;
+        for (int e = 0; e < EPL; ++e) qreg[r][e] = qs[r * D + lane * EPL + e];
     }
     float m_run[RP], l_run[RP], o[RP][EPL];
 #pragma unroll
@@ -272,8 +296,7 @@ gqa_decode_kernel(GqaKP kp, int stages) {
 #pragma unroll
       for (int e = 0; e < EPL; ++e) o[r][e] = 0.f;
     }
-    // row handled by this lane's score after the reduce-scatter
-    const int my_idx = lane >> SHIFT;
+    const int my_idx = lane >> SHIFT;  // value index this lane holds after the reduce-scatter
     const int my_r = my_idx % RP;
     const int my_kk = my_idx / RP;
     const int my_s = my_r / kp.G;
@@ -334,25 +357,18 @@ gqa_decode_kernel(GqaKP kp, int stages) {
             v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
           }
         }
-        // score in log2 units with masks
         const int j = j0 + kl0 + my_kk;
         float sc = v[0] * kp.scale_log2;
-        bool valid = (j < kend) && (my_r < kp.R) && (j <= qpos) &&
-                     (kp.local_window <= 0 || j > qpos - kp.local_window);
-        if (valid && bias) {
-          if (j < kp.bias_total) sc += to_f<T>(bias[bias_row + j]) * kLog2e;
-        }
+        const bool valid = (j < kend) && (my_r < kp.R) && (j <= qpos) &&
+                           (kp.local_window <= 0 || j > qpos - kp.local_window);
+        if (valid && bias && j < kp.bias_total) sc += to_f<T>(bias[bias_row + j]) * kLog2e;
         if (!valid) sc = -INFINITY;
-        // per-row max / sum over the KWW keys: lanes sharing my_r differ in idx bits >= log2(RP)
         float mx = sc;
 #pragma unroll
         for (int off = RP << SHIFT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         float m_new[RP];
 #pragma unroll
-        for (int r = 0; r < RP; ++r) {
-          const float step_max = __shfl_sync(0xffffffffu, mx, r << SHIFT);
-          m_new[r] = fmaxf(m_run[r], step_max);
-        }
+        for (int r = 0; r < RP; ++r) m_new[r] = fmaxf(m_run[r], __shfl_sync(0xffffffffu, mx, r << SHIFT));
         float mrow = m_new[0];
 #pragma unroll
         for (int r = 1; r < RP; ++r)
@@ -388,9 +404,9 @@ gqa_decode_kernel(GqaKP kp, int stages) {
         }
         __syncwarp();
       }
+      __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    // publish this warp's state
 #pragma unroll
     for (int r = 0; r < RP; ++r) {
       float* w = wst + ((size_t)warp * RP + r) * (D + 2);
@@ -411,9 +427,8 @@ gqa_decode_kernel(GqaKP kp, int stages) {
   __syncthreads();
 
   // --- merge the warps; write the output or this split's partial -----------------------------
-  const int nthreads = (kNW + 1) * 32;
   float* part = kp.partial + ((((int64_t)b * kp.HK + kvh) * kp.splits + split) * RP) * (D + 2);
-  for (int idx = threadIdx.x; idx < kp.R * (D + 2); idx += nthreads) {
+  for (int idx = threadIdx.x; idx < kp.R * (D + 2); idx += kThreads) {
     const int r = idx / (D + 2), d = idx - r * (D + 2);
     float M = -INFINITY;
 #pragma unroll
@@ -447,23 +462,49 @@ gqa_decode_kernel(GqaKP kp, int stages) {
   __syncthreads();
   if (!flags[1]) return;
   __threadfence();
+  // --- last CTA of this (batch, kv-head): merge the splits ---------------------------------
+  // per-(split, row) weights first (one pass over the small m / l vectors), then every output
+  // element sums its splits with independent loads.
   const float* base = kp.partial + (((int64_t)b * kp.HK + kvh) * kp.splits) * RP * (D + 2);
-  for (int idx = threadIdx.x; idx < kp.R * D; idx += nthreads) {
-    const int r = idx / D, d = idx - r * D;
+  float* wsp = reinterpret_cast<float*>(smem + L.kbuf);  // [splits][RP] weights (tile buffers are free)
+  float* rowM = wsp + kp.splits * RP;                     // [RP]
+  for (int i = threadIdx.x; i < kp.splits * kp.R; i += kThreads) {
+    const int sp = i / kp.R, r = i - sp * kp.R;
+    wsp[sp * RP + r] = __ldcg(base + ((size_t)sp * RP + r) * (D + 2) + D);  // m
+  }
+  __syncthreads();
+  if (threadIdx.x < kp.R) {
+    const int r = threadIdx.x;
     float M = -INFINITY;
-    for (int sp = 0; sp < kp.splits; ++sp)
-      M = fmaxf(M, __ldcg(base + ((size_t)sp * RP + r) * (D + 2) + D));
-    float acc = 0.f, lsum = 0.f;
+    for (int sp = 0; sp < kp.splits; ++sp) M = fmaxf(M, wsp[sp * RP + r]);
+    float lsum = 0.f;
     for (int sp = 0; sp < kp.splits; ++sp) {
-      const float* ps = base + ((size_t)sp * RP + r) * (D + 2);
-      const float m = __ldcg(ps + D);
+      const float m = wsp[sp * RP + r];
       const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
-      acc = fmaf(__ldcg(ps + d), f, acc);
-      lsum = fmaf(__ldcg(ps + D + 1), f, lsum);
+      wsp[sp * RP + r] = f;
+      lsum = fmaf(__ldcg(base + ((size_t)sp * RP + r) * (D + 2) + D + 1), f, lsum);
     }
+    rowM[r] = lsum > 0.f ? 1.f / lsum : 0.f;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < kp.R * D; idx += kThreads) {
+    const int r = idx / D, d = idx - r * D;
+    float acc = 0.f;
+    int sp = 0;
+    for (; sp + 4 <= kp.splits; sp += 4) {
+      const float a0 = __ldcg(base + ((size_t)(sp + 0) * RP + r) * (D + 2) + d);
+      const float a1 = __ldcg(base + ((size_t)(sp + 1) * RP + r) * (D + 2) + d);
+      const float a2 = __ldcg(base + ((size_t)(sp + 2) * RP + r) * (D + 2) + d);
+      const float a3 = __ldcg(base + ((size_t)(sp + 3) * RP + r) * (D + 2) + d);
+      acc = fmaf(a0, wsp[(sp + 0) * RP + r], acc);
+      acc = fmaf(a1, wsp[(sp + 1) * RP + r], acc);
+      acc = fmaf(a2, wsp[(sp + 2) * RP + r], acc);
+      acc = fmaf(a3, wsp[(sp + 3) * RP + r], acc);
+    }
+    for (; sp < kp.splits; ++sp) acc = fmaf(__ldcg(base + ((size_t)sp * RP + r) * (D + 2) + d), wsp[sp * RP + r], acc);
     const int s = r / kp.G, g = r - s * kp.G, h = kvh * kp.G + g;
     T* out = static_cast<T*>(kp.out) + (((int64_t)b * kp.S + s) * kp.H + h) * D;
-    out[d] = from_f<T>(lsum > 0.f ? acc / lsum : 0.f);
+    out[d] = from_f<T>(acc * rowM[r]);
   }
   if (threadIdx.x == 0) kp.counters[b * kp.HK + kvh] = 0;
 }
@@ -588,7 +629,7 @@ bool decode_path(const b200ep_gqa_params& p, int esz) {
 int choose_splits(const b200ep_gqa_params& p) {
   const int64_t pairs = p.batch * p.kv_heads;
   int64_t want = (2 * 148 + pairs - 1) / pairs;
-  int64_t max_by_len = std::max<int64_t>(1, p.cap / kKT);
+  int64_t max_by_len = std::max<int64_t>(1, p.cap / (2 * kKT));
   return (int)std::max<int64_t>(1, std::min<int64_t>({want, max_by_len, 64}));
 }
 
@@ -619,7 +660,7 @@ cudaError_t launch_decode_t(const GqaKP& kp, cudaStream_t st) {
   } else {
   const int D = EPL * 32;
   const int tile = kKT * D * (int)sizeof(T);
-  int stages = tile <= 8192 ? 6 : tile <= 16384 ? 4 : 2;
+  int stages = tile <= 8192 ? 4 : tile <= 16384 ? 3 : 2;
   DecodeSmem L = decode_smem_layout(D, (int)sizeof(T), RP, stages);
   auto kern = gqa_decode_kernel<T, EPL, RP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);

@@ -67,156 +67,221 @@ __global__ void mnb_dequant_kernel(const uint8_t* __restrict__ B, const TS* __re
 }
 
 // ---- decode GEMV ----------------------------------------------------------------------------
-// Grid: one CTA per group of (8 / WPR) weight rows; WPR warps cooperate on one row (split along
-// K) so small-N projections still fill the GPU.  The activation rows are staged in shared
-// memory as fp32 in segments of SEGC 16-byte chunks; the smem row for each chunk is padded by
-// 4 floats so that the 128-bit reads of 8 consecutive lanes hit distinct banks.
+// Persistent grid (one wave).  Warp gw owns the row tuples gw, gw + total_warps, ...; a tuple is
+// R consecutive weight rows processed together so every activation value read from shared memory
+// serves R rows.  A warp walks its (tuple, group) items — a group is U 16-byte chunks per lane
+// of each of the R rows, lane-contiguous so one warp load covers 512 contiguous bytes — with the
+// next item's weights, scales and zero points already in flight (register double buffer).  The
+// first item's loads are issued before the activation is staged, so HBM streaming starts at once.
+// The activation is staged once per CTA as fp32 with a 4-float pad per chunk row (conflict-free
+// 128-bit reads for the 8 lanes of a shared-memory phase).  Dequant: 2^23 + q built by one byte
+// permute, minus (2^23 + zp) in one exact add, then fp32 FMAs; the block scale is applied once
+// per block.
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvU = 2;
 
-template <typename T, int BITS, int BLOCK, int MT, bool HAS_ZP>
-__global__ void __launch_bounds__(kGemvThreads, 3)
-mnb_gemv_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
-                const T* __restrict__ scales, const uint8_t* __restrict__ zp,
-                T* __restrict__ Y, int M, int N, int K, int nblocks, int chunks_per_row,
-                int segc, int wpr) {
-  constexpr int VPC = 128 / BITS;        // values per 16-byte chunk
-  constexpr int XS = VPC + 4;            // padded floats per chunk in smem
-  extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                      // [MT][segc][XS]
-  float* red = smem + MT * segc * XS;    // [kGemvWarps][MT] cross-warp partials
+template <int BITS, int BLOCK, int R, bool HAS_ZP>
+struct GemvBuf {
+  static constexpr int VPC = 128 / BITS;
+  static constexpr int NBC = BLOCK >= VPC ? 1 : VPC / BLOCK;
+  uint4 w[R][kGemvU];
+  float s[R][kGemvU][NBC];
+  int z[R][kGemvU][NBC];
+};
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_cta = kGemvWarps / wpr;
-  const int n = blockIdx.x * rows_per_cta + warp / wpr;
-  const int sub = warp % wpr;
-  const bool row_ok = n < N;
-  const size_t rowbytes = (size_t)chunks_per_row * 16;
-  const uint8_t* brow = B + (size_t)(row_ok ? n : 0) * rowbytes;
+template <typename T, int BITS, int BLOCK, int R, bool HAS_ZP>
+__device__ __forceinline__ void gemv_load(GemvBuf<BITS, BLOCK, R, HAS_ZP>& b, const uint8_t* __restrict__ B,
+                                          const T* __restrict__ scales, const uint8_t* __restrict__ zp,
+                                          int row0, int g, int lane, int N, int cpr, int nblocks) {
+  constexpr int VPC = 128 / BITS;
+  constexpr int NBC = BLOCK >= VPC ? 1 : VPC / BLOCK;
   const int zcols = (nblocks + 1) >> 1;
-
-  float acc[MT];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
-
-  for (int seg0 = 0; seg0 < chunks_per_row; seg0 += segc) {
-    const int nseg = min(segc, chunks_per_row - seg0);
-    __syncthreads();
-    // stage A[:, seg] as fp32 (zero beyond K and beyond M)
-    for (int i = threadIdx.x; i < MT * nseg * VPC; i += kGemvThreads) {
-      int m = i / (nseg * VPC);
-      int r = i - m * nseg * VPC;
-      int c = r / VPC, j = r - c * VPC;
-      int k = (seg0 + c) * VPC + j;
-      float v = (m < M && k < K) ? to_f<T>(A[(size_t)m * K + k]) : 0.f;
-      xs[(m * segc + c) * XS + j] = v;
-    }
-    __syncthreads();
-    if (!row_ok) continue;
-
-    constexpr int U = 4;
-    for (int c0 = sub * 32 + lane; c0 < nseg; c0 += 32 * wpr * U) {
-      uint4 wv[U];
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        int c = c0 + u * 32 * wpr;
-        if (c < nseg) wv[u] = ld_stream_u4(brow + (size_t)(seg0 + c) * 16);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        int c = c0 + u * 32 * wpr;
-        if (c >= nseg) break;
-        const int cg = seg0 + c;                 // global chunk index
-        const int k0 = cg * VPC;
-        const uint32_t words[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-        // blocks covered by this chunk: one (BLOCK >= VPC) or VPC/BLOCK (block 16, int4)
-        constexpr int NBC = BLOCK >= VPC ? 1 : VPC / BLOCK;
-        constexpr int WPB = 4 / NBC;             // 32-bit words per block inside the chunk
+    for (int u = 0; u < kGemvU; ++u) {
+      const int c = (g * kGemvU + u) * 32 + lane;
+      if (row < N && c < cpr) {
+        b.w[r][u] = ld_stream_u4(B + ((size_t)row * cpr + c) * 16);
 #pragma unroll
         for (int bc = 0; bc < NBC; ++bc) {
-          const int blk = k0 / BLOCK + bc;
-          const float s = to_f<T>(scales[(size_t)n * nblocks + blk]);
-          int z;
+          const int blk = c * VPC / BLOCK + bc;
+          b.s[r][u][bc] = to_f<T>(scales[(size_t)row * nblocks + blk]);
           if (HAS_ZP) {
             if (BITS == 4) {
-              uint8_t zb = zp[(size_t)n * zcols + (blk >> 1)];
-              z = (blk & 1) ? (zb >> 4) : (zb & 0x0f);
+              const uint8_t zb = zp[(size_t)row * zcols + (blk >> 1)];
+              b.z[r][u][bc] = (blk & 1) ? (zb >> 4) : (zb & 0x0f);
             } else {
-              z = zp[(size_t)n * nblocks + blk];
+              b.z[r][u][bc] = zp[(size_t)row * nblocks + blk];
             }
           } else {
-            z = 1 << (BITS - 1);
+            b.z[r][u][bc] = 1 << (BITS - 1);
           }
-          const float bias = -(8388608.0f + (float)z);
-          float part[MT];
+        }
+      } else {
+        b.w[r][u] = make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int m = 0; m < MT; ++m) part[m] = 0.f;
-#pragma unroll
-          for (int wi = 0; wi < WPB; ++wi) {
-            const int wj = bc * WPB + wi;
-            const uint32_t w = words[wj];
-            if (BITS == 4) {
-              const uint32_t lo = w & 0x0f0f0f0fu;         // nibbles k = 0,2,4,6 of the word
-              const uint32_t hi = (w >> 4) & 0x0f0f0f0fu;  // nibbles k = 1,3,5,7
-              float d[8];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                d[2 * j] = magic_byte(lo, j) + bias;
-                d[2 * j + 1] = magic_byte(hi, j) + bias;
-              }
-#pragma unroll
-              for (int m = 0; m < MT; ++m) {
-                const float4* xp = reinterpret_cast<const float4*>(xs + (m * segc + c) * XS + wj * 8);
-                float4 xa = xp[0], xb = xp[1];
-                part[m] = fmaf(xa.x, d[0], part[m]);
-                part[m] = fmaf(xa.y, d[1], part[m]);
-                part[m] = fmaf(xa.z, d[2], part[m]);
-                part[m] = fmaf(xa.w, d[3], part[m]);
-                part[m] = fmaf(xb.x, d[4], part[m]);
-                part[m] = fmaf(xb.y, d[5], part[m]);
-                part[m] = fmaf(xb.z, d[6], part[m]);
-                part[m] = fmaf(xb.w, d[7], part[m]);
-              }
-            } else {
-              float d[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) d[j] = magic_byte(w, j) + bias;
-#pragma unroll
-              for (int m = 0; m < MT; ++m) {
-                float4 xa = *reinterpret_cast<const float4*>(xs + (m * segc + c) * XS + wj * 4);
-                part[m] = fmaf(xa.x, d[0], part[m]);
-                part[m] = fmaf(xa.y, d[1], part[m]);
-                part[m] = fmaf(xa.z, d[2], part[m]);
-                part[m] = fmaf(xa.w, d[3], part[m]);
-              }
-            }
-          }
-#pragma unroll
-          for (int m = 0; m < MT; ++m) acc[m] = fmaf(part[m], s, acc[m]);
+        for (int bc = 0; bc < NBC; ++bc) {
+          b.s[r][u][bc] = 0.f;
+          b.z[r][u][bc] = 0;
         }
       }
     }
   }
+}
 
+template <int BITS, int BLOCK, int MT, int R, bool HAS_ZP>
+__device__ __forceinline__ void gemv_compute(const GemvBuf<BITS, BLOCK, R, HAS_ZP>& b, const float* __restrict__ xs,
+                                             int g, int lane, int cpr, float (&acc)[R][MT]) {
+  constexpr int VPC = 128 / BITS;
+  constexpr int XS = VPC + 4;
+  constexpr int NBC = BLOCK >= VPC ? 1 : VPC / BLOCK;
+  constexpr int WPB = 4 / NBC;
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = warp_sum(acc[m]);
-  if (wpr == 1) {
-    if (row_ok && lane == 0) {
+  for (int u = 0; u < kGemvU; ++u) {
+    const int c = (g * kGemvU + u) * 32 + lane;
+    if (c >= cpr) break;
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
-        if (m < M) Y[(size_t)m * N + n] = from_f<T>(acc[m]);
+    for (int bc = 0; bc < NBC; ++bc) {
+      float part[R][MT];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) part[r][m] = 0.f;
+#pragma unroll
+      for (int wi = 0; wi < WPB; ++wi) {
+        const int wj = bc * WPB + wi;
+        if (BITS == 4) {
+          float4 xa[MT], xb[MT];
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const float4* xp = reinterpret_cast<const float4*>(xs + ((size_t)m * cpr + c) * XS + wj * 8);
+            xa[m] = xp[0];
+            xb[m] = xp[1];
+          }
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint32_t w = wj == 0 ? b.w[r][u].x : wj == 1 ? b.w[r][u].y : wj == 2 ? b.w[r][u].z : b.w[r][u].w;
+            const float bias = -(8388608.0f + (float)b.z[r][u][bc]);
+            const uint32_t lo = w & 0x0f0f0f0fu, hi = (w >> 4) & 0x0f0f0f0fu;
+            float d[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              d[2 * j] = magic_byte(lo, j) + bias;
+              d[2 * j + 1] = magic_byte(hi, j) + bias;
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              float p = part[r][m];
+              p = fmaf(xa[m].x, d[0], p);
+              p = fmaf(xa[m].y, d[1], p);
+              p = fmaf(xa[m].z, d[2], p);
+              p = fmaf(xa[m].w, d[3], p);
+              p = fmaf(xb[m].x, d[4], p);
+              p = fmaf(xb[m].y, d[5], p);
+              p = fmaf(xb[m].z, d[6], p);
+              p = fmaf(xb[m].w, d[7], p);
+              part[r][m] = p;
+            }
+          }
+        } else {
+          float4 xa[MT];
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            xa[m] = *reinterpret_cast<const float4*>(xs + ((size_t)m * cpr + c) * XS + wj * 4);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint32_t w = wj == 0 ? b.w[r][u].x : wj == 1 ? b.w[r][u].y : wj == 2 ? b.w[r][u].z : b.w[r][u].w;
+            const float bias = -(8388608.0f + (float)b.z[r][u][bc]);
+            float d[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j] = magic_byte(w, j) + bias;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              float p = part[r][m];
+              p = fmaf(xa[m].x, d[0], p);
+              p = fmaf(xa[m].y, d[1], p);
+              p = fmaf(xa[m].z, d[2], p);
+              p = fmaf(xa[m].w, d[3], p);
+              part[r][m] = p;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m] = fmaf(part[r][m], b.s[r][u][bc], acc[r][m]);
     }
-    return;
   }
-  if (lane == 0) {
-#pragma unroll
-    for (int m = 0; m < MT; ++m) red[warp * MT + m] = acc[m];
+}
+
+template <typename T, int BITS, int BLOCK, int MT, int R, bool HAS_ZP>
+__global__ void __launch_bounds__(kGemvThreads, 2)
+mnb_gemv_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
+                const T* __restrict__ scales, const uint8_t* __restrict__ zp,
+                T* __restrict__ Y, int M, int N, int K, int nblocks, int cpr) {
+  constexpr int VPC = 128 / BITS;
+  constexpr int XS = VPC + 4;
+  extern __shared__ __align__(16) float xs[];  // [MT][cpr][XS]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kGemvWarps + warp;
+  const int tw = gridDim.x * kGemvWarps;
+  const int ntuples = (N + R - 1) / R;
+  const int gpr = (cpr + 32 * kGemvU - 1) / (32 * kGemvU);
+  const int my_tuples = gw < ntuples ? (ntuples - 1 - gw) / tw + 1 : 0;
+  const int nitems = my_tuples * gpr;
+
+  using Buf = GemvBuf<BITS, BLOCK, R, HAS_ZP>;
+  Buf b0, b1;
+  if (nitems > 0) gemv_load<T>(b0, B, scales, zp, gw * R, 0, lane, N, cpr, nblocks);
+
+  // stage the activation rows (fp32, padded) while the first weights are in flight
+  for (int m = 0; m < MT; ++m) {
+    for (int k = threadIdx.x; k < cpr * VPC; k += kGemvThreads) {
+      const int c = k / VPC, j = k - c * VPC;
+      xs[((size_t)m * cpr + c) * XS + j] = (m < M && k < K) ? to_f<T>(A[(size_t)m * K + k]) : 0.f;
+    }
   }
   __syncthreads();
-  if (row_ok && sub == 0 && lane < MT && lane < M) {
-    float v = 0.f;
-    for (int s2 = 0; s2 < wpr; ++s2) v += red[(warp + s2) * MT + lane];
-    Y[(size_t)lane * N + n] = from_f<T>(v);
+
+  float acc[R][MT];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+
+  auto finish_item = [&](int item) {
+    const int g = item % gpr;
+    if (g != gpr - 1) return;
+    const int row0 = (gw + (item / gpr) * tw) * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float v = warp_sum(acc[r][m]);
+        acc[r][m] = 0.f;
+        if (lane == 0 && m < M && row0 + r < N) Y[(size_t)m * N + row0 + r] = from_f<T>(v);
+      }
+  };
+
+  for (int item = 0; item < nitems; item += 2) {
+    // item -> buffer b0, item+1 -> buffer b1 (loaded one step ahead)
+    if (item + 1 < nitems) {
+      const int it = item + 1;
+      gemv_load<T>(b1, B, scales, zp, (gw + (it / gpr) * tw) * R, it % gpr, lane, N, cpr, nblocks);
+    }
+    gemv_compute<BITS, BLOCK, MT, R, HAS_ZP>(b0, xs, item % gpr, lane, cpr, acc);
+    finish_item(item);
+    if (item + 1 >= nitems) break;
+    if (item + 2 < nitems) {
+      const int it = item + 2;
+      gemv_load<T>(b0, B, scales, zp, (gw + (it / gpr) * tw) * R, it % gpr, lane, N, cpr, nblocks);
+    }
+    gemv_compute<BITS, BLOCK, MT, R, HAS_ZP>(b1, xs, (item + 1) % gpr, lane, cpr, acc);
+    finish_item(item + 1);
   }
 }
 
@@ -283,30 +348,42 @@ mnb_tile_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
 // ---- host launchers -------------------------------------------------------------------------
 namespace {
 
+int num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
 template <typename T, int BITS, int BLOCK, int MT, bool HAS_ZP>
 cudaError_t launch_gemv_t(const MnbArgs& a, cudaStream_t st) {
   constexpr int VPC = 128 / BITS;
   constexpr int XS = VPC + 4;
+  constexpr int R = MT <= 2 ? 2 : 1;
   const int64_t nblocks = (a.K + BLOCK - 1) / BLOCK;
-  const int chunks_per_row = (int)(nblocks * BLOCK * BITS / 8 / 16);
-  // segment size: keep the fp32 activation stage near 40 KB, whole 32-chunk multiples
-  int segc = (40 * 1024) / (MT * XS * 4);
-  segc = std::max(32, (segc / 32) * 32);
-  segc = std::min(segc, ((chunks_per_row + 31) / 32) * 32);
-  // warps per row: enough warps in flight for small N
-  int wpr = 1;
-  while (wpr < 8 && (int64_t)a.N * wpr < 148 * 48 && chunks_per_row >= 64 * wpr) wpr *= 2;
-  const int rows_per_cta = kGemvWarps / wpr;
-  const size_t smem = (size_t)(MT * segc * XS + kGemvWarps * MT) * sizeof(float);
-  auto kern = mnb_gemv_kernel<T, BITS, BLOCK, MT, HAS_ZP>;
-  if (smem > 48 * 1024) {
+  const int cpr = (int)(nblocks * BLOCK * BITS / 8 / 16);
+  const size_t smem = (size_t)MT * cpr * XS * sizeof(float);
+  auto kern = mnb_gemv_kernel<T, BITS, BLOCK, MT, R, HAS_ZP>;
+  static int configured_smem = 0;  // per instantiation
+  if ((int)smem > configured_smem && smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    configured_smem = (int)smem;
   }
-  dim3 grid((unsigned)div_up(a.N, rows_per_cta));
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem);
+  if (e != cudaSuccess) return e;
+  per_sm = std::max(1, per_sm);
+  const int64_t ntuples = (a.N + R - 1) / R;
+  const int64_t want = (ntuples + kGemvWarps - 1) / kGemvWarps;
+  const int grid = (int)std::min<int64_t>(want, (int64_t)per_sm * num_sms());
   kern<<<grid, kGemvThreads, smem, st>>>(
       static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales), a.zp,
-      static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, (int)nblocks, chunks_per_row, segc, wpr);
+      static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, (int)nblocks, cpr);
   return cudaGetLastError();
 }
 
@@ -337,7 +414,9 @@ template <typename T>
 cudaError_t launch_dtype(const MnbArgs& a, cudaStream_t st) {
   const int64_t nblocks = (a.K + a.block - 1) / a.block;
   const int64_t rowbytes = nblocks * a.block * a.bits / 8;
-  const bool gemv_ok = a.M <= 4 && rowbytes % 16 == 0 && a.K <= (1 << 24) &&
+  const int64_t mt = a.M <= 1 ? 1 : a.M <= 2 ? 2 : 4;
+  const int64_t stage_bytes = mt * (rowbytes / 16) * (128 / a.bits + 4) * 4;
+  const bool gemv_ok = a.M <= 4 && rowbytes % 16 == 0 && stage_bytes <= 200 * 1024 &&
                        (reinterpret_cast<uintptr_t>(a.B) % 16) == 0;
   if (gemv_ok) return a.bits == 4 ? launch_gemv_b<T, 4>(a, st) : launch_gemv_b<T, 8>(a, st);
   dim3 grid((unsigned)div_up(a.N, kTN), (unsigned)div_up(a.M, kTM));

@@ -177,6 +177,7 @@ int oracle_matmulnbits_dequant(const uint8_t* B, const void* scales, int scale_d
   if (block < 16 || (block & (block - 1))) return OR_EINVAL;
   if (!is_float_dt(scale_dt)) return OR_EINVAL;
   int64_t nblocks = (K + block - 1) / block;
+#pragma omp parallel for schedule(static)
   for (int64_t n = 0; n < N; ++n)
     for (int64_t k = 0; k < K; ++k) {
       int64_t blk = k / block;
@@ -196,10 +197,10 @@ int oracle_matmulnbits(const void* A, const uint8_t* B, const void* scales,
   float* W = (float*)malloc((size_t)N * (size_t)K * sizeof(float));
   float* Af = (float*)malloc((size_t)M * (size_t)K * sizeof(float));
   if (!W || !Af) { free(W); free(Af); return OR_EINVAL; }
+  set_threads(nthreads);
   int rc = oracle_matmulnbits_dequant(B, scales, dt, zp, N, K, bits, block, W);
   if (rc) { free(W); free(Af); return rc; }
   for (int64_t i = 0; i < M * K; ++i) Af[i] = load_f(A, i, dt);
-  set_threads(nthreads);
 #pragma omp parallel for schedule(static) collapse(2)
   for (int64_t m = 0; m < M; ++m)
     for (int64_t n = 0; n < N; ++n) {

@@ -1,0 +1,203 @@
+"""The EP end to end on the GPU: graphs built like the reference's tests, claimed, compiled into
+device plans (with fusion and CUDA graphs) and run, against the CPU oracle.
+
+The decoder case chains the oracle's per-op results exactly as ORT's CPU EP would execute the
+graph (each op rounds to fp16), so the tolerance here is the per-op fp16 one scaled by the
+depth of the composition (stated per test).
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def ep_mod():
+    from onnxruntime_ep_b200 import ep
+
+    return ep
+
+
+def cuda(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def test_single_matmulnbits_through_ep(ep_mod):
+    rng = np.random.default_rng(0)
+    M, K, N, block = 1, 4096, 4096, 32
+    nb = K // block
+    a = rng.standard_normal((1, M, K)).astype(np.float32)
+    q = rng.integers(0, 16, size=(N, nb, block), dtype=np.uint8)
+    b = (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
+    s = rng.uniform(0.005, 0.02, N * nb).astype(np.float32)
+    z = rng.integers(0, 256, size=N * nb // 2, dtype=np.uint8)
+    g = ep_mod.GraphBuilder()
+    g.input("a", ep_mod.FLOAT, [1, M, K])
+    g.initializer("b", b)
+    g.initializer("s", s)
+    g.initializer("z", z)
+    g.output("y", ep_mod.FLOAT, [1, M, N])
+    g.node("MatMulNBits", ["a", "b", "s", "z"], ["y"], domain="com.microsoft", K=K, N=N, bits=4, block_size=block)
+    sess = ep_mod.Session(g)
+    for host in (False, True):  # device-resident and host (data-transfer) boundaries
+        feeds = {"a": a if host else cuda(a)}
+        out = {"y": np.empty((1, M, N), np.float32)} if host else None
+        y = sess.run(feeds, out)["y"]
+        y = y if host else y.cpu().numpy()
+        np.testing.assert_allclose(y, oracle.matmulnbits(a, b, s, z, N=N, K=K), rtol=6e-5, atol=6e-5)
+
+
+def gqa_graph(ep_mod, B, S, H, HK, D, cap, present_cap, dtype):
+    g = ep_mod.GraphBuilder()
+    code = ep_mod.FLOAT16 if dtype == np.float16 else ep_mod.FLOAT
+    g.input("q", code, [B, S, H * D])
+    g.input("k", code, [B, S, HK * D])
+    g.input("v", code, [B, S, HK * D])
+    g.input("pk", code, [B, HK, cap, D])
+    g.input("pv", code, [B, HK, cap, D])
+    g.input("seqlens", ep_mod.INT32, [B])
+    g.input("total", ep_mod.INT32, [1])
+    half = D // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half) / half))
+    ang = np.arange(cap + 16)[:, None] * inv[None, :]
+    g.initializer("cos", np.cos(ang).astype(dtype), code)
+    g.initializer("sin", np.sin(ang).astype(dtype), code)
+    g.output("out", code, [B, S, H * D])
+    g.output("prk", code, [B, HK, present_cap, D])
+    g.output("prv", code, [B, HK, present_cap, D])
+    g.node("GroupQueryAttention", ["q", "k", "v", "pk", "pv", "seqlens", "total", "cos", "sin"], ["out", "prk", "prv"],
+           domain="com.microsoft", num_heads=H, kv_num_heads=HK, do_rotary=1)
+    return g, np.cos(ang).astype(dtype), np.sin(ang).astype(dtype)
+
+
+@pytest.mark.parametrize("shared", [True, False], ids=["shared-buffer", "growing"])
+def test_gqa_through_ep_both_kv_contracts(ep_mod, shared):
+    rng = np.random.default_rng(1)
+    B, S, H, HK, D, past = 2, 1, 32, 8, 128, 300
+    cap = past + 16 if shared else past
+    pcap = cap if shared else past + S
+    g, cos, sin = gqa_graph(ep_mod, B, S, H, HK, D, cap, pcap, np.float16)
+    sess = ep_mod.Session(g)
+    q = rng.standard_normal((B, S, H * D)).astype(np.float16)
+    k = rng.standard_normal((B, S, HK * D)).astype(np.float16)
+    v = rng.standard_normal((B, S, HK * D)).astype(np.float16)
+    pk = np.zeros((B, HK, cap, D), np.float16)
+    pv = np.zeros((B, HK, cap, D), np.float16)
+    pk[:, :, :past] = rng.standard_normal((B, HK, past, D))
+    pv[:, :, :past] = rng.standard_normal((B, HK, past, D))
+    seqlens = np.full(B, past + S - 1, np.int32)
+    total = np.array([past + S], np.int32)
+    tk, tv = cuda(pk), cuda(pv)
+    outs = {"prk": tk, "prv": tv} if shared else None
+    res = sess.run({"q": cuda(q), "k": cuda(k), "v": cuda(v), "pk": tk, "pv": tv, "seqlens": cuda(seqlens),
+                    "total": total}, outs)
+    want, wk, wv = oracle.gqa(q, k, v, pk.copy(), pv.copy(), seqlens, cos, sin, num_heads=H, kv_heads=HK,
+                              shared_buffer=shared, present_cap=pcap)
+    np.testing.assert_allclose(res["out"].float().cpu().numpy(), want.astype(np.float32), rtol=1e-2, atol=1e-3)
+    valid = past + S
+    np.testing.assert_array_equal(res["prk"].cpu().numpy()[:, :, :valid], wk[:, :, :valid])
+    np.testing.assert_array_equal(res["prv"].cpu().numpy()[:, :, :valid], wv[:, :, :valid])
+
+
+SMALL = dict(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000, max_seq=256)
+
+
+def oracle_decoder_step(cfg, W, ids, kv, seqlens):
+    """The decoder graph executed op by op on the CPU oracle, each op rounding to fp16."""
+    f16 = np.float16
+    B, S = ids.shape
+    x = oracle.gather_block_quantized(W["embed.q"], W["embed.scales"], ids, block_size=cfg.block)
+    res = None
+    for i in range(cfg.layers):
+        p = f"l{i}"
+        if res is None:
+            n1, r1 = oracle.rms_norm(x, W[f"{p}.ln1"], cfg.eps), x
+        else:
+            n1, r1 = oracle.skip_rms_norm(x, res, W[f"{p}.ln1"], cfg.eps)
+
+        def mnb(a, name, n, k):
+            return oracle.matmulnbits(a, W[name + ".B"], W[name + ".scales"], W[name + ".zp"], N=n, K=k)
+
+        H, HK, D = cfg.heads, cfg.kv_heads, cfg.head_dim
+        q = mnb(n1, f"{p}.q_proj", H * D, cfg.hidden)
+        k = mnb(n1, f"{p}.k_proj", HK * D, cfg.hidden)
+        v = mnb(n1, f"{p}.v_proj", HK * D, cfg.hidden)
+        attn, kv[i][0], kv[i][1] = oracle.gqa(q, k, v, kv[i][0], kv[i][1], seqlens, W["cos_cache"], W["sin_cache"],
+                                              num_heads=H, kv_heads=HK, scale=float(1.0 / np.sqrt(D)),
+                                              shared_buffer=True)
+        o = mnb(attn, f"{p}.o_proj", cfg.hidden, H * D)
+        n2, r2 = oracle.skip_rms_norm(o, r1, W[f"{p}.ln2"], cfg.eps)
+        gate = mnb(n2, f"{p}.gate_proj", cfg.ffn, cfg.hidden).astype(np.float32)
+        up = mnb(n2, f"{p}.up_proj", cfg.ffn, cfg.hidden).astype(np.float32)
+        sig = (1.0 / (1.0 + np.exp(-gate))).astype(f16).astype(np.float32)
+        silu = (gate * sig).astype(f16).astype(np.float32)
+        h = (silu * up).astype(f16)
+        x = mnb(h, f"{p}.down_proj", cfg.hidden, cfg.ffn)
+        res = r2
+    nf, _ = oracle.skip_rms_norm(x, res, W["final_norm"], cfg.eps)
+    return oracle.matmulnbits(nf, W["lm_head.B"], W["lm_head.scales"], W["lm_head.zp"], N=cfg.vocab, K=cfg.hidden)
+
+
+def test_small_decoder_prefill_and_decode_match_oracle(ep_mod):
+    from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
+
+    cfg = DecoderConfig(**SMALL)
+    B, P, cap, steps = 2, 8, 32, 4
+    Wp, Wd = {}, {}
+    sess_p = ep_mod.Session(build_decoder(cfg, batch=B, seq=P, cap=cap, weights_out=Wp))
+    sess_d = ep_mod.Session(build_decoder(cfg, batch=B, seq=1, cap=cap, weights_out=Wd))
+    d = json.loads(sess_d.parts[0].describe())
+    assert d["fused_qkv"] == cfg.layers and d["fused_swiglu"] == cfg.layers
+    rng = np.random.default_rng(7)
+    kv_dev = [[torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
+              for _ in range(cfg.layers)]
+    kv_ref = [[np.zeros((B, cfg.kv_heads, cap, cfg.head_dim), np.float16) for _ in range(2)] for _ in range(cfg.layers)]
+
+    # decode inputs live in persistent device buffers updated in place (IoBinding style), so the
+    # plan's CUDA graph, keyed by boundary pointers, is captured once and replayed
+    dec_ids = torch.zeros(B, 1, dtype=torch.int64, device="cuda")
+    dec_seq = torch.zeros(B, dtype=torch.int32, device="cuda")
+    dec_tot = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def feeds_for(ids, past):
+        if ids.shape[1] == 1:
+            dec_ids.copy_(cuda(ids))
+            dec_seq.fill_(past)
+            dec_tot.fill_(past + 1)
+            f = {"input_ids": dec_ids, "seqlens_k": dec_seq, "total_sequence_length": dec_tot}
+        else:
+            f = {"input_ids": cuda(ids), "seqlens_k": cuda(np.full(B, past + ids.shape[1] - 1, np.int32)),
+                 "total_sequence_length": cuda(np.array([past + ids.shape[1]], np.int32))}
+        outs = {}
+        for i in range(cfg.layers):
+            f[f"past_key_values.{i}.key"], f[f"past_key_values.{i}.value"] = kv_dev[i]
+            outs[f"present.{i}.key"], outs[f"present.{i}.value"] = kv_dev[i]
+        return f, outs
+
+    ids = rng.integers(0, cfg.vocab, size=(B, P), dtype=np.int64)
+    f, o = feeds_for(ids, 0)
+    got = sess_p.run(f, o)["logits"].float().cpu().numpy()
+    want = oracle_decoder_step(cfg, Wp, ids, kv_ref, np.full(B, P - 1, np.int32)).astype(np.float32)
+    scale = np.abs(want).max()
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2 * scale)
+    for t in range(steps):
+        ids = rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64)
+        f, o = feeds_for(ids, P + t)
+        got = sess_d.run(f, o)["logits"].float().cpu().numpy()
+        want = oracle_decoder_step(cfg, Wd, ids, kv_ref, np.full(B, P + t, np.int32)).astype(np.float32)
+        np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2 * np.abs(want).max())
+        # greedy next token agrees (top-1 of the logits)
+        assert (got.argmax(-1) == want.argmax(-1)).mean() >= 0.5
+    for i in range(cfg.layers):
+        np.testing.assert_allclose(kv_dev[i][0].float().cpu().numpy()[:, :, :P + steps],
+                                   kv_ref[i][0].astype(np.float32)[:, :, :P + steps], rtol=2e-2, atol=2e-2)
+    d = json.loads(sess_d.parts[0].describe())
+    assert d["graph_replays"] >= steps - 2  # one CUDA graph serves every decode step
