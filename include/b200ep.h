@@ -139,6 +139,22 @@ B200EP_API int b200ep_group_query_attention(
     const void* sin_cache, const void* q_norm, const void* k_norm, const void* attention_bias,
     void* out, int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* GroupQueryAttention that allocates nothing.  No counterpart in the reference: it exists for
+ * callers that may not allocate device memory once running (a server that reserves its HBM
+ * budget up front and treats later cudaMalloc as failure; a decode loop that must not allocate or
+ * free between tokens).  Same arguments and results as b200ep_group_query_attention without the
+ * workspace: the split-K scratch is a fixed library-owned device array of
+ * b200ep_gqa_noalloc_max_workspace() bytes (4 MiB) per GPU, held until the process exits.
+ * Geometries whose scratch (b200ep_gqa_workspace_size) exceeds it fail with B200EP_ERANGE.  The
+ * first call on a device looks up the array's address (make it before any stream capture).
+ * Every call shares the array: calls whose launches overlap on the GPU race on it. */
+B200EP_API int b200ep_group_query_attention_noalloc(
+    const b200ep_gqa_params* p, const void* query, const void* key, const void* value,
+    void* kv_key, void* kv_value, const int32_t* seqlens_k, const void* cos_cache,
+    const void* sin_cache, const void* q_norm, const void* k_norm, const void* attention_bias,
+    void* out, int dtype, void* stream);
+B200EP_API size_t b200ep_gqa_noalloc_max_workspace(void);
+
 #ifdef __cplusplus
 }
 #endif
