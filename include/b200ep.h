@@ -82,6 +82,25 @@ B200EP_API int b200ep_matmulnbits_dequant(const uint8_t* B, const void* scales,
                                           int out_dtype, int64_t N, int64_t K, int bits,
                                           int block_size, void* stream);
 
+/* Prepacked int4 weights for the tensor-core path (fp16 / bf16 activations, bits = 4, K % 16 == 0).
+ * The weight is repacked once into self-contained group records — 16 rows x 64 k of int4 values in
+ * mma.sync operand order followed by that group's block scales and zero points — stored tile-major
+ * so a run of rows is one contiguous stream for the TMA engine.  The B200 counterpart of the
+ * reference's one-time repack to MLX words (rust/src/ops/quant.rs:634-710).
+ * b200ep_matmulnbits_prepack_size gives the buffer size; b200ep_matmulnbits_prepack fills it
+ * (device to device); b200ep_matmulnbits_prepacked computes Y[M,N] = A . W^T like
+ * b200ep_matmulnbits (exact (q - zp) products accumulated in fp32 per block, scaled once per
+ * block). */
+B200EP_API int b200ep_matmulnbits_prepack_size(int64_t N, int64_t K, int bits, int block_size,
+                                               size_t* bytes);
+B200EP_API int b200ep_matmulnbits_prepack(const uint8_t* B, const void* scales,
+                                          const uint8_t* zero_points, int dtype, int64_t N,
+                                          int64_t K, int bits, int block_size, void* packed,
+                                          void* stream);
+B200EP_API int b200ep_matmulnbits_prepacked(const void* A, const void* packed, void* Y, int dtype,
+                                            int64_t M, int64_t N, int64_t K, int bits,
+                                            int block_size, void* stream);
+
 /* RMS norms -----------------------------------------------------------------------------------
  * Y = X / sqrt(mean(X^2, last axis) + eps) * gamma, fp32 accumulation.
  * Replaces: mlx_fast_rms_norm in rms_norm_op / simplified_layer_norm_op

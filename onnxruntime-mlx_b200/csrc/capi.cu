@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "kernels/kernels.h"
+#include "kernels/mnb_mma.h"
 
 namespace b200ep {
 
@@ -140,6 +141,55 @@ B200EP_API int b200ep_matmulnbits_dequant(const uint8_t* B, const void* scales,
   MnbDequantArgs a{B, scales, zero_points, W, scale_dtype, out_dtype, N, K, bits, block_size};
   return cuda_status(launch_matmulnbits_dequant(a, static_cast<cudaStream_t>(stream)),
                      "MatMulNBits dequant launch");
+  B200EP_GUARD_END
+}
+
+static int packed_args(int64_t N, int64_t K, int bits, int block, int dtype, MnbPacked* p) {
+  int rc = check_mnb_common(N, K, bits, block);
+  if (rc) return rc;
+  B200EP_CHECK_ARG(mnb_mma_supported(dtype, bits, block, K),
+                   "MatMulNBits prepacked path needs fp16/bf16, bits = 4 and K % 16 == 0");
+  *p = mnb_packed_geometry(N, K, block);
+  return B200EP_OK;
+}
+
+B200EP_API int b200ep_matmulnbits_prepack_size(int64_t N, int64_t K, int bits, int block_size, size_t* bytes) {
+  B200EP_GUARD_BEGIN
+  int rc = check_mnb_common(N, K, bits, block_size);
+  if (rc) return rc;
+  B200EP_CHECK_ARG(bits == 4 && K % 16 == 0, "MatMulNBits prepacked path needs bits = 4 and K % 16 == 0");
+  if (bytes) *bytes = mnb_packed_geometry(N, K, block_size).bytes;
+  return B200EP_OK;
+  B200EP_GUARD_END
+}
+
+B200EP_API int b200ep_matmulnbits_prepack(const uint8_t* B, const void* scales, const uint8_t* zero_points,
+                                          int dtype, int64_t N, int64_t K, int bits, int block_size, void* packed,
+                                          void* stream) {
+  B200EP_GUARD_BEGIN
+  MnbPacked p;
+  int rc = packed_args(N, K, bits, block_size, dtype, &p);
+  if (rc) return rc;
+  B200EP_CHECK_ARG(B && scales && packed, "MatMulNBits prepack: null pointer");
+  p.w = packed;
+  return cuda_status(launch_mnb_prepack(B, scales, zero_points, dtype, p, static_cast<cudaStream_t>(stream)),
+                     "MatMulNBits prepack launch");
+  B200EP_GUARD_END
+}
+
+B200EP_API int b200ep_matmulnbits_prepacked(const void* A, const void* packed, void* Y, int dtype, int64_t M,
+                                            int64_t N, int64_t K, int bits, int block_size, void* stream) {
+  B200EP_GUARD_BEGIN
+  MnbPacked p;
+  int rc = packed_args(N, K, bits, block_size, dtype, &p);
+  if (rc) return rc;
+  B200EP_CHECK_ARG(M >= 0 && M < (1ll << 31), "MatMulNBits: bad M");
+  B200EP_CHECK_ARG(M == 0 || (A && packed && Y), "MatMulNBits prepacked: null pointer");
+  B200EP_CHECK_ARG(reinterpret_cast<uintptr_t>(packed) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 4 == 0,
+                   "MatMulNBits prepacked: packed weights must be 16-byte and A 4-byte aligned");
+  p.w = const_cast<void*>(packed);
+  return cuda_status(launch_mnb_packed(A, p, Y, dtype, M, static_cast<cudaStream_t>(stream)),
+                     "MatMulNBits prepacked launch");
   B200EP_GUARD_END
 }
 

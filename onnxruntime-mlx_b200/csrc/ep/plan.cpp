@@ -10,6 +10,7 @@
 #include "../common.cuh"
 #include "../kernels/elementwise.h"
 #include "../kernels/kernels.h"
+#include "../kernels/mnb_mma.h"
 #include "tp.h"
 
 namespace b200ep {
@@ -434,8 +435,45 @@ void Plan::fuse_swiglu() {
 }
 
 int Plan::upload_constants(const Graph& g, std::string* err) {
+  // fp16 / bf16 int4 MatMulNBits: upload the ORT-layout weight once, repack it on the device into
+  // the tensor-core operand order, keep only the packed form
+  for (auto& st : steps_) {
+    if (st.kind != StepKind::kMnb || st.in.empty() || st.in[0] < 0) continue;
+    const int adt = slots_[st.in[0]].dtype;
+    if (env_on("ONNXRUNTIME_EP_B200_NO_PREPACK") || !mnb_mma_supported(adt, st.bits, st.block, st.K)) continue;
+    auto host = [&](int id) { return pending_consts_.count(id) ? pending_consts_[id] : nullptr; };
+    auto B = host(st.wB), S = host(st.wS), Z = st.wZ >= 0 ? host(st.wZ) : nullptr;
+    if (!B || !S || (st.wZ >= 0 && !Z)) continue;
+    MnbPacked pk = mnb_packed_geometry(st.N, st.K, st.block);
+    DevMem tb, ts, tz;
+    st.pk_w = std::make_shared<DevMem>();
+    int rc = 0;
+    rc |= tb.alloc(B->bytes.size());
+    rc |= ts.alloc(S->bytes.size());
+    if (Z) rc |= tz.alloc(Z->bytes.size());
+    rc |= st.pk_w->alloc(pk.bytes);
+    if (rc) {
+      *err = "weight upload: out of device memory";
+      return B200EP_ENOMEM;
+    }
+    cudaError_t e = cudaMemcpy(tb.p, B->bytes.data(), B->bytes.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(ts.p, S->bytes.data(), S->bytes.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && Z) e = cudaMemcpy(tz.p, Z->bytes.data(), Z->bytes.size(), cudaMemcpyHostToDevice);
+    pk.w = st.pk_w->p;
+    if (e == cudaSuccess)
+      e = launch_mnb_prepack(static_cast<const uint8_t*>(tb.p), ts.p, Z ? static_cast<const uint8_t*>(tz.p) : nullptr,
+                             adt, pk, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      *err = std::string("weight prepack failed: ") + cudaGetErrorString(e);
+      return B200EP_ECUDA;
+    }
+    st.prepacked = true;
+    stats_.weight_bytes += (int64_t)pk.bytes;
+  }
   std::set<int> used;
   for (auto& st : steps_) {
+    if (st.kind == StepKind::kMnb && st.prepacked) continue;
     for (int s : st.in)
       if (s >= 0 && slots_[s].kind == Slot::kConst) used.insert(s);
     for (int s : {st.wB, st.wS, st.wZ})
@@ -605,6 +643,12 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
     switch (s.kind) {
       case StepKind::kMnb: {
         const Slot& a = S[s.in[0]];
+        if (s.prepacked) {
+          MnbPacked pk = mnb_packed_geometry(s.N, s.K, s.block);
+          pk.w = s.pk_w->p;
+          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, a.numel() / s.K, st);
+          break;
+        }
         MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
                   s.wZ >= 0 ? static_cast<const uint8_t*>(S[s.wZ].ptr) : nullptr,
                   S[s.out[0]].ptr, a.dtype, a.numel() / s.K, s.N, s.K, s.bits, s.block};
@@ -908,7 +952,10 @@ std::string Plan::describe() const {
   o << "{\"nodes\":" << stats_.nodes << ",\"steps\":" << steps_.size() << ",\"fused_qkv\":" << stats_.fused_qkv
     << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"weight_bytes\":" << stats_.weight_bytes
     << ",\"runs\":" << stats_.runs << ",\"graph_captures\":" << stats_.graph_captures
-    << ",\"graph_replays\":" << stats_.graph_replays << ",\"ops\":[";
+    << ",\"graph_replays\":" << stats_.graph_replays;
+  int npk = 0;
+  for (auto& st : steps_) npk += st.prepacked;
+  o << ",\"prepacked_matmulnbits\":" << npk << ",\"ops\":[";
   static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
                                 "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
   for (size_t i = 0; i < steps_.size(); ++i) o << (i ? "," : "") << "\"" << names[(int)steps_[i].kind] << "\"";

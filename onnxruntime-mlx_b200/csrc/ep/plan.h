@@ -98,6 +98,9 @@ struct Step {
   int64_t gbq_rows = 0, gbq_dim = 0;
   // tensor parallel gather: shard width along the last axis
   int64_t shard_cols = 0;
+  // MatMulNBits weights prepacked for the tensor-core path (fp16/bf16, int4)
+  bool prepacked = false;
+  std::shared_ptr<DevMem> pk_w;
 };
 
 struct PlanStats {

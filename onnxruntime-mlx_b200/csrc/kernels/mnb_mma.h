@@ -1,0 +1,30 @@
+// Prepacked int4 MatMulNBits on the tensor cores (mnb_mma.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200ep {
+
+// Geometry and device buffer of one prepacked weight: ntiles x ksteps4 group records of
+// record_bytes each (16 rows x 64 k of int4 weights plus their block scales / zero points).
+struct MnbPacked {
+  int64_t N = 0, K = 0;
+  int block = 32;
+  int64_t nblocks_src = 0;  // blocks per row in the ORT layout
+  int64_t ntiles = 0;       // 16-row tiles
+  int64_t ksteps4 = 0;      // 64-k groups after padding K to a multiple of max(64, block)
+  int record_bytes = 0;
+  size_t bytes = 0;
+  void* w = nullptr;
+};
+
+int mnb_record_bytes(int block);
+MnbPacked mnb_packed_geometry(int64_t N, int64_t K, int block);
+bool mnb_mma_supported(int dtype, int bits, int block, int64_t K);
+cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8_t* zp, int scale_dtype,
+                               const MnbPacked& p, cudaStream_t st);
+cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st);
+
+}  // namespace b200ep

@@ -41,6 +41,9 @@ def _lib():
         L.b200ep_gqa_workspace_size.restype = ctypes.c_size_t
         L.b200ep_group_query_attention.argtypes = (
             [ctypes.POINTER(GqaParams)] + [vp] * 12 + [i32, vp, ctypes.c_size_t, vp])
+        L.b200ep_matmulnbits_prepack_size.argtypes = [i64, i64, i32, i32, ctypes.POINTER(ctypes.c_size_t)]
+        L.b200ep_matmulnbits_prepack.argtypes = [vp, vp, vp, i32, i64, i64, i32, i32, vp, vp]
+        L.b200ep_matmulnbits_prepacked.argtypes = [vp, vp, vp, i32, i64, i64, i64, i32, i32, vp]
         L.b200ep_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), i32]
         _configured = True
     return L
@@ -88,6 +91,29 @@ def matmulnbits_dequant(b, scales, zero_points=None, *, K, N, bits=4, block_size
                                             DT[str(out_dtype).replace("torch.", "")], N, K, bits,
                                             block_size, _stream(b.device)))
     return w
+
+
+def matmulnbits_prepack(b, scales, zero_points=None, *, K, N, bits=4, block_size=32):
+    """Repack ORT-layout int4 weights into tensor-core group records; returns the device buffer."""
+    import torch
+
+    size = ctypes.c_size_t(0)
+    check(_lib().b200ep_matmulnbits_prepack_size(N, K, bits, block_size, ctypes.byref(size)))
+    packed = torch.empty(int(size.value), dtype=torch.uint8, device=b.device)
+    check(_lib().b200ep_matmulnbits_prepack(_p(b), _p(scales), _p(zero_points), _dt(scales), N, K, bits, block_size,
+                                            _p(packed), _stream(b.device)))
+    return packed
+
+
+def matmulnbits_prepacked(a, packed, *, K, N, bits=4, block_size=32, out=None):
+    import torch
+
+    M = a.numel() // K
+    if out is None:
+        out = torch.empty(*a.shape[:-1], N, dtype=a.dtype, device=a.device)
+    check(_lib().b200ep_matmulnbits_prepacked(_p(a), _p(packed), _p(out), _dt(a), M, N, K, bits, block_size,
+                                              _stream(a.device)))
+    return out
 
 
 def rms_norm(x, gamma, eps, out=None):

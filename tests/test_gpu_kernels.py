@@ -340,3 +340,46 @@ def test_gqa_out_of_range_is_reported_not_faulted(ops):
     torch.cuda.synchronize()
     code, _ = ops.device_error(clear=True)
     assert code == 101
+
+
+# ---- prepacked tensor-core MatMulNBits -------------------------------------------------------
+@pytest.mark.parametrize("block", [16, 32, 64, 128])
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 37])
+@pytest.mark.parametrize("asym", [True, False], ids=["asym", "sym"])
+def test_matmulnbits_prepacked_vs_oracle(ops, block, M, asym):
+    rng = np.random.default_rng(block * 131 + M)
+    K, N = 512, 200  # N not a multiple of 16, K a multiple of 16 but not of 64 when block 16
+    a, b, s, zp = make_mnb(rng, M, K, N, block=block, dtype=np.float16, asym=asym)
+    packed = ops.matmulnbits_prepack(cuda(b), cuda(s), cuda(zp) if asym else None, K=K, N=N, block_size=block)
+    got = ops.matmulnbits_prepacked(cuda(a), packed, K=K, N=N, block_size=block).float().cpu().numpy()
+    want = oracle.matmulnbits(a, b, s, zp if asym else None, N=N, K=K, block_size=block).astype(np.float32)
+    np.testing.assert_allclose(got, want, **TOL["f16"])
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (1, 14336, 4096), (1, 4096, 28672), (16, 4096, 4096),
+                                   (512, 4096, 1024), (1, 1168, 96)])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_matmulnbits_prepacked_llama_shapes(ops, M, K, N, dt):
+    rng = np.random.default_rng(M + K * 3 + N)
+    a, b, s, zp = make_mnb(rng, M, K, N)
+    if dt == "f16":
+        a16, s16 = a.astype(np.float16), s.astype(np.float16)
+        want = oracle.matmulnbits(a16, b, s16, zp, N=N, K=K).astype(np.float32)
+        packed = ops.matmulnbits_prepack(cuda(b), cuda(s16), cuda(zp), K=K, N=N)
+        got = ops.matmulnbits_prepacked(cuda(a16), packed, K=K, N=N)
+    else:
+        ab, sb = oracle.f32_to_bf16_bits(a), oracle.f32_to_bf16_bits(s)
+        want = oracle.bf16_bits_to_f32(oracle.matmulnbits(ab, b, sb, zp, N=N, K=K, dtype="bf16"))
+        packed = ops.matmulnbits_prepack(cuda(b), cuda(sb).view(torch.bfloat16), cuda(zp), K=K, N=N)
+        got = ops.matmulnbits_prepacked(cuda(ab).view(torch.bfloat16), packed, K=K, N=N)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, **TOL[dt])
+
+
+def test_matmulnbits_prepacked_matches_ort_layout_kernel(ops):
+    """The tensor-core path and the ORT-layout GEMV agree on the same weights (fp16 activations)."""
+    rng = np.random.default_rng(9)
+    a, b, s, zp = make_mnb(rng, 2, 2048, 512, dtype=np.float16)
+    ref = ops.matmulnbits(cuda(a), cuda(b), cuda(s), cuda(zp), K=2048, N=512).float()
+    packed = ops.matmulnbits_prepack(cuda(b), cuda(s), cuda(zp), K=2048, N=512)
+    got = ops.matmulnbits_prepacked(cuda(a), packed, K=2048, N=512).float()
+    torch.testing.assert_close(got, ref, rtol=1e-2, atol=1e-3)
