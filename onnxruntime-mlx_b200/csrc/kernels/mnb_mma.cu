@@ -11,9 +11,9 @@
 //                       bits  4- 7: W[16t+g+8][16s+2c  ]   bits 20-23: W[16t+g+8][16s+2c+1]
 //                       bits  8-11: W[16t+g  ][16s+2c+8]   bits 24-27: W[16t+g  ][16s+2c+9]
 //                       bits 12-15: W[16t+g+8][16s+2c+8]   bits 28-31: W[16t+g+8][16s+2c+9]
-//   then, per quantisation block the record covers (slot) and row pair g: the scales of rows g
-//   and g+8 as one half2 / bf162, then their zero points as one byte (g + 8 in the high nibble);
-//   padded to 16 bytes.  Block 32: 512 + 80 = 592 bytes per 512 weight bytes, the same overhead
+//   then, per row pair g and quantisation block the record covers (slot): the scales of rows g
+//   and g+8 as one half2 / bf162 ([g][slot], so a lane loads all its slots at once), then their
+//   zero points as one byte ([g][slot], row g + 8 in the high nibble); padded to 16 bytes.  Block 32: 512 + 80 = 592 bytes per 512 weight bytes, the same overhead
 //   as ONNX Runtime's scales + packed zero points.
 //
 // Kernel.  One CTA streams a contiguous run of tiles.  A producer warp copies G records per
@@ -36,8 +36,8 @@ namespace b200ep {
 template <int BLOCK>
 struct Rec {
   static constexpr int kSlots = BLOCK >= 64 ? 1 : 64 / BLOCK;  // blocks per record
-  static constexpr int kSOff = 512;                            // uint32 scales[slot][8]
-  static constexpr int kZOff = 512 + kSlots * 32;              // uint8  zps[slot][8]
+  static constexpr int kSOff = 512;                            // uint32 scales[8][slot]
+  static constexpr int kZOff = 512 + kSlots * 32;              // uint8  zps[8][slot]
   static constexpr int kBytes = 512 + ((kSlots * 40 + 15) / 16) * 16;
   static constexpr int kUnit = BLOCK > 64 ? BLOCK / 64 : 1;   // records per block (kept by one warp)
 };
@@ -98,7 +98,7 @@ __global__ void mnb_prepack_kernel(const uint8_t* __restrict__ B, const TS* __re
     const bool is_z = off >= RC::kZOff;
     if (!is_z && ((off - RC::kSOff) & 3)) continue;  // one thread writes each 4-byte scale word
     const int idx = is_z ? off - RC::kZOff : (off - RC::kSOff) / 4;
-    const int slot = idx / 8, g = idx % 8;
+    const int g = idx / RC::kSlots, slot = idx % RC::kSlots;
     const int blk = SPB <= 4 ? (gi * 4) / SPB + slot : gi / (SPB / 4);
     const int64_t r0 = t * 16 + g, r1 = r0 + 8;
     if (is_z) {
@@ -123,53 +123,76 @@ __global__ void mnb_prepack_kernel(const uint8_t* __restrict__ B, const TS* __re
 }
 
 // ---- fragment dequant -------------------------------------------------------------------------
+// (a & b) | c as one LOP3.  The mask and magic constants live in registers (DqConst, built from a
+// kernel argument the compiler cannot fold): with two immediates the and/or pair costs two
+// integer-pipe instructions instead of one.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+struct DqConst {
+  uint32_t m0, m1, c0, c1;  // nibble masks 0x000F000F / 0x00F000F0 and the dtype's magic exponents
+};
+
 template <typename T> struct Dq;
 template <> struct Dq<__half> {
-  static __device__ __forceinline__ void run(uint32_t w, uint32_t bias_lo, uint32_t bias_hi, uint32_t (&a)[4]) {
+  static __device__ __forceinline__ DqConst consts(uint32_t zero) {
+    return DqConst{0x000F000Fu | zero, 0x00F000F0u | zero, 0x64006400u | zero, 0x54005400u | zero};
+  }
+  // (w & 0x000F000F) | 0x6400 -> 1024 + q; (w & 0x00F000F0) | 0x5400 -> 64 + q; exact subtract
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t bias_lo, uint32_t bias_hi, const DqConst& k,
+                                             uint32_t (&a)[4]) {
     const uint32_t w8 = w >> 8;
-    const uint32_t t0 = (w & 0x000F000Fu) | 0x64006400u;   // 1024 + q   rows g,   k 2c / 2c+1
-    const uint32_t t1 = (w & 0x00F000F0u) | 0x54005400u;   //   64 + q   rows g+8, k 2c / 2c+1
-    const uint32_t t2 = (w8 & 0x000F000Fu) | 0x64006400u;  // 1024 + q   rows g,   k 2c+8 / 2c+9
-    const uint32_t t3 = (w8 & 0x00F000F0u) | 0x54005400u;  //   64 + q   rows g+8, k 2c+8 / 2c+9
+    const uint32_t t0 = and_or(w, k.m0, k.c0);   // rows g,   k 2c / 2c+1
+    const uint32_t t1 = and_or(w, k.m1, k.c1);   // rows g+8, k 2c / 2c+1
+    const uint32_t t2 = and_or(w8, k.m0, k.c0);  // rows g,   k 2c+8 / 2c+9
+    const uint32_t t3 = and_or(w8, k.m1, k.c1);  // rows g+8, k 2c+8 / 2c+9
     asm("sub.f16x2 %0, %1, %2;" : "=r"(a[0]) : "r"(t0), "r"(bias_lo));
     asm("sub.f16x2 %0, %1, %2;" : "=r"(a[1]) : "r"(t1), "r"(bias_hi));
     asm("sub.f16x2 %0, %1, %2;" : "=r"(a[2]) : "r"(t2), "r"(bias_lo));
     asm("sub.f16x2 %0, %1, %2;" : "=r"(a[3]) : "r"(t3), "r"(bias_hi));
   }
+  // zr = the zero-point byte (z_g | z_{g+8} << 4) in bytes 0 and 2
   // bias_lo = (1024 + z_g) in both halves, bias_hi = (64 + z_{g+8}) in both halves
-  static __device__ __forceinline__ void bias(uint32_t zb, uint32_t& lo, uint32_t& hi) {
-    lo = ((zb & 0x0Fu) * 0x00010001u) | 0x64006400u;
-    hi = ((zb & 0xF0u) * 0x00010001u) | 0x54005400u;
+  static __device__ __forceinline__ void bias(uint32_t zr, const DqConst& k, uint32_t& lo, uint32_t& hi) {
+    lo = and_or(zr, k.m0, k.c0);
+    hi = and_or(zr, k.m1, k.c1);
   }
 };
 template <> struct Dq<__nv_bfloat16> {
-  // bf16 keeps 7 mantissa bits: every nibble is first moved to bits 0-3 of its half
-  static __device__ __forceinline__ void run(uint32_t w, uint32_t bias_lo, uint32_t bias_hi, uint32_t (&a)[4]) {
-    const uint32_t t0 = (w & 0x000F000Fu) | 0x43004300u;  // 128 + q
-    const uint32_t t1 = ((w >> 4) & 0x000F000Fu) | 0x43004300u;
-    const uint32_t t2 = ((w >> 8) & 0x000F000Fu) | 0x43004300u;
-    const uint32_t t3 = ((w >> 12) & 0x000F000Fu) | 0x43004300u;
+  static __device__ __forceinline__ DqConst consts(uint32_t zero) {
+    return DqConst{0x000F000Fu | zero, 0x000F000Fu | zero, 0x43004300u | zero, 0x43004300u | zero};
+  }
+  // bf16 keeps 7 mantissa bits: every nibble is first moved to bits 0-3 of its half (128 + q)
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t bias_lo, uint32_t bias_hi, const DqConst& k,
+                                             uint32_t (&a)[4]) {
+    const uint32_t t0 = and_or(w, k.m0, k.c0);
+    const uint32_t t1 = and_or(w >> 4, k.m0, k.c0);
+    const uint32_t t2 = and_or(w >> 8, k.m0, k.c0);
+    const uint32_t t3 = and_or(w >> 12, k.m0, k.c0);
     asm("sub.bf16x2 %0, %1, %2;" : "=r"(a[0]) : "r"(t0), "r"(bias_lo));
     asm("sub.bf16x2 %0, %1, %2;" : "=r"(a[1]) : "r"(t1), "r"(bias_hi));
     asm("sub.bf16x2 %0, %1, %2;" : "=r"(a[2]) : "r"(t2), "r"(bias_lo));
     asm("sub.bf16x2 %0, %1, %2;" : "=r"(a[3]) : "r"(t3), "r"(bias_hi));
   }
-  static __device__ __forceinline__ void bias(uint32_t zb, uint32_t& lo, uint32_t& hi) {
-    lo = ((zb & 0x0Fu) * 0x00010001u) | 0x43004300u;
-    hi = (((zb >> 4) & 0x0Fu) * 0x00010001u) | 0x43004300u;
+  static __device__ __forceinline__ void bias(uint32_t zr, const DqConst& k, uint32_t& lo, uint32_t& hi) {
+    lo = and_or(zr, k.m0, k.c0);
+    hi = and_or(zr >> 4, k.m0, k.c0);
   }
 };
 
 template <typename T>
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   if constexpr (std::is_same<T, __half>::value) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -184,30 +207,133 @@ __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
 }
 
 // ---- the TMA-fed streaming kernel -------------------------------------------------------------
-constexpr int kNC = 8;  // consumer warps
+constexpr int kNC = 8;        // consumer warps
+constexpr int kStages = 4;    // ring stages
+constexpr int kG = 32;        // records per stage (one bulk copy, ~19 KB for block 32)
 enum { kErrMnbTimeout = 301 };
 
 __device__ __forceinline__ void consumer_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kNC * 32) : "memory");
 }
 
-template <typename T, int BLOCK, int NT>
-__global__ void __launch_bounds__((kNC + 1) * 32)
-mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
-               int ntiles, int ksteps4, int G, int stages, int xrows, DeviceErrorSlot* err) {
+template <int N>
+__device__ __forceinline__ void lds_words(const unsigned char* p, uint32_t (&v)[N]) {
+  if constexpr (N == 1) {
+    v[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if constexpr (N == 2) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    v[0] = t.x, v[1] = t.y;
+  } else {
+    const uint4 t = *reinterpret_cast<const uint4*>(p);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  }
+}
+
+// Activation rows staged in shared memory in fragment order: per row and 64-k group, lane column
+// c owns 8 consecutive words (its B fragments of the group's 4 k-steps: k 2c,2c+1 then 2c+8,2c+9
+// of each k-step), so a lane loads a record's B operands with two 16-byte loads.
+__device__ __forceinline__ int xperm_src_word(int w) {  // word within a 64-k group, staged order -> k order
+  const int c = w >> 3, j = (w >> 1) & 3, h = w & 1;
+  return j * 8 + h * 4 + c;
+}
+
+// One unit (UNIT consecutive records of one warp): dequantise, MMA per k-step, scale per block.
+//   wq: this lane's 16 weight bytes of the first record; pq: the first record (parameters)
+//   xp: staged activation fragments of the first record (STAGED) — else ag/live/gi0 address the
+//   activation rows in global memory.  PAIR = false when only even token columns exist (M == 1):
+//   the odd-column accumulators are then left alone.
+template <typename T, int BLOCK, int NT, bool STAGED, bool PAIR>
+__device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned char* pq,
+                                         const unsigned char* const (&xp)[NT], const uint32_t* const (&ag)[NT],
+                                         const uint32_t (&live)[NT], int gi0, int ksteps, int g,
+                                         const DqConst& kq, float (&acc)[NT][4]) {
   using RC = Rec<BLOCK>;
   constexpr int SPB = BLOCK / 16;
+  constexpr int SL = RC::kSlots;
+  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+  float cb[NT][4];
+#pragma unroll
+  for (int r = 0; r < RC::kUnit; ++r) {
+    uint32_t b[NT][8];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if constexpr (STAGED) {
+        const uint4 lo = *reinterpret_cast<const uint4*>(xp[nt] + r * 128);
+        const uint4 hi = *reinterpret_cast<const uint4*>(xp[nt] + r * 128 + 16);
+        b[nt][0] = lo.x, b[nt][1] = lo.y, b[nt][2] = lo.z, b[nt][3] = lo.w;
+        b[nt][4] = hi.x, b[nt][5] = hi.y, b[nt][6] = hi.z, b[nt][7] = hi.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int s = (gi0 + r) * 4 + j;
+          const int sc = s < ksteps ? s : 0;
+          const uint32_t lv = s < ksteps ? live[nt] : 0u;
+          b[nt][2 * j] = __ldg(ag[nt] + sc * 8) & lv;
+          b[nt][2 * j + 1] = __ldg(ag[nt] + sc * 8 + 4) & lv;
+        }
+      }
+    }
+    const unsigned char* rec = pq + r * RC::kBytes;
+    const uint4 w4 = *reinterpret_cast<const uint4*>(wq + r * RC::kBytes);
+    const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
+    uint32_t sw[SL];
+    lds_words<SL>(rec + RC::kSOff + g * SL * 4, sw);
+    const uint32_t zz = SL == 1 ? (uint32_t)rec[RC::kZOff + g]
+                        : SL == 2 ? (uint32_t)*reinterpret_cast<const uint16_t*>(rec + RC::kZOff + g * 2)
+                                  : *reinterpret_cast<const uint32_t*>(rec + RC::kZOff + g * 4);
+    uint32_t bias_lo = 0, bias_hi = 0;
+    float2 scl = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool block_start = SPB <= 4 ? (j % SPB == 0) : (j == 0 && r == 0);
+      const bool block_end = SPB <= 4 ? (j % SPB == SPB - 1) : (j == 3 && r == RC::kUnit - 1);
+      const int sl = SPB <= 4 ? j / SPB : 0;
+      if (j % (SPB <= 4 ? SPB : 4) == 0) {  // parameters of the block this k-step belongs to
+        scl = s2_to_f2(sw[sl], BF);
+        Dq<T>::bias(__byte_perm(zz, 0, 0x4040 + 0x0101 * sl), kq, bias_lo, bias_hi);
+      }
+      uint32_t a[4];
+      Dq<T>::run(words[j], bias_lo, bias_hi, kq, a);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (block_start) cb[nt][0] = cb[nt][1] = cb[nt][2] = cb[nt][3] = 0.f;
+        mma16816<T>(cb[nt], a, b[nt][2 * j], b[nt][2 * j + 1]);
+      }
+      if (block_end) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[nt][0] = fmaf(cb[nt][0], scl.x, acc[nt][0]);
+          acc[nt][2] = fmaf(cb[nt][2], scl.y, acc[nt][2]);
+          if (PAIR) {
+            acc[nt][1] = fmaf(cb[nt][1], scl.x, acc[nt][1]);
+            acc[nt][3] = fmaf(cb[nt][3], scl.y, acc[nt][3]);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int BLOCK, int NT, bool PAIR>
+__global__ void __launch_bounds__((kNC + 1) * 32, 2)
+mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
+               int ntiles, int ksteps4, int xrows, uint32_t zero, DeviceErrorSlot* err) {
+  using RC = Rec<BLOCK>;
+  constexpr int SPB = BLOCK / 16;          // k-steps per block
+  constexpr int SL = RC::kSlots;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr int UNIT = RC::kUnit;
+  constexpr int PER = kG / (kNC * UNIT);   // units per warp per full stage
+  static_assert(kG % (kNC * UNIT) == 0, "stage must split evenly");
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + stages;
-  int* flags = reinterpret_cast<int*>(empty + stages);
+  uint64_t* empty = full + kStages;
+  int* flags = reinterpret_cast<int*>(empty + kStages);
   unsigned char* buf = smem + 256;
-  float* red = reinterpret_cast<float*>(buf + (size_t)stages * G * RC::kBytes);  // [kNC][NT][4][32]
-  // staged activation rows (xrows > 0): xrows + 1 rows of kpad halves (columns >= K and the last row
-  // zero), rows 16 bytes apart in bank order so the 8 row groups of a fragment load hit 32 banks
-  unsigned char* xs = reinterpret_cast<unsigned char*>(red + kNC * NT * 4 * 32);
+  float* red = reinterpret_cast<float*>(buf + (size_t)kStages * kG * RC::kBytes);  // [2][kNC][NT][4][32]
+  // staged activation rows (xrows > 0): xrows + 1 rows (the last one zero) of kpad halves,
+  // 16 bytes apart in bank order so the 8 row groups of a fragment load use all 32 banks
+  unsigned char* xs = reinterpret_cast<unsigned char*>(red + 2 * kNC * NT * 4 * 32);
   const int kpad = ksteps4 * 64;
   const int xstride = kpad * 2 + 16;
   const bool stage_x = xrows > 0;
@@ -215,14 +341,14 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = (int)((int64_t)ntiles * blockIdx.x / gridDim.x);
   const int t1 = (int)((int64_t)ntiles * (blockIdx.x + 1) / gridDim.x);
-  const int spt = (ksteps4 + G - 1) / G;  // stages per tile
+  const int spt = (ksteps4 + kG - 1) / kG;  // stages per tile
   const int nst = (t1 - t0) * spt;
   const int m0 = blockIdx.y * 8 * NT;
   const int ksteps = K / 16;
 
   if (threadIdx.x == 0) {
     flags[0] = 0;
-    for (int s = 0; s < stages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kNC);
     }
@@ -231,171 +357,157 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   __syncthreads();
   if (warp == kNC) {
     if (lane == 0) {
+      int slot = 0, t = t0, ga = 0;
+      uint32_t phase = 0;
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % stages;
-        if (i >= stages && !mbar_wait(&empty[slot], ((i / stages) - 1) & 1)) {
+        if (i >= kStages && !mbar_wait(&empty[slot], phase ^ 1)) {
           flags[0] = 1;
           break;
         }
-        const int t = t0 + i / spt;
-        const int ga = (i % spt) * G;
-        const int n = min(G, ksteps4 - ga);
+        const int n = min(kG, ksteps4 - ga);
         const uint32_t bytes = (uint32_t)(n * RC::kBytes);
         mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(buf + (size_t)slot * G * RC::kBytes, recs + ((size_t)t * ksteps4 + ga) * RC::kBytes, bytes,
+        bulk_g2s(buf + (size_t)slot * kG * RC::kBytes, recs + ((size_t)t * ksteps4 + ga) * RC::kBytes, bytes,
                  &full[slot]);
+        ga += kG;
+        if (ga >= ksteps4) ga = 0, ++t;
+        if (++slot == kStages) slot = 0, phase ^= 1;
       }
     }
     return;
   }
 
-  // consumers: stage the activation rows of this column chunk (zero beyond K and beyond M) while
-  // the producer's first copies are in flight
+  // consumers: stage the activation rows of this column chunk while the first copies are in flight
   if (stage_x) {
-    const int wpr = kpad / 2;  // 32-bit words per row
-    const int words = (xrows + 1) * wpr;
-    for (int idx = threadIdx.x; idx < words; idx += kNC * 32) {
-      const int r = idx / wpr, k = (idx - r * wpr) * 2;
-      const int m = m0 + r;
-      uint32_t v = 0;
-      if (r < xrows && m < M && k < K) v = *reinterpret_cast<const uint32_t*>(A + (size_t)m * K + k);
-      *reinterpret_cast<uint32_t*>(xs + (size_t)r * xstride + k * 2) = v;
+    // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
+    const int cpr = kpad / 8;  // 16-byte chunks per row
+    const int chunks = (xrows + 1) * cpr;
+    for (int base = threadIdx.x; base < chunks; base += 4 * kNC * 32) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * kNC * 32;
+        const int r = idx / cpr, k = (idx - r * cpr) * 8;
+        const int m = m0 + r;
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (idx < chunks && r < xrows && m < M && k < K) v[u] = *reinterpret_cast<const uint4*>(A + (size_t)m * K + k);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * kNC * 32;
+        if (idx < chunks) {
+          const int r = idx / cpr, kw = (idx - r * cpr) * 4;  // first source word of the chunk
+          const int grp = kw & ~31, sw = kw & 31;             // sw = j*8 + h*4 (c = 0..3 follow)
+          const int j = sw >> 3, h = (sw >> 2) & 1;
+          uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)r * xstride) + grp + 2 * j + h;
+          dst[0] = v[u].x, dst[8] = v[u].y, dst[16] = v[u].z, dst[24] = v[u].w;
+        }
+      }
     }
     consumer_barrier();
   }
   const int g = lane >> 2, c = lane & 3;
+  const unsigned char* xrow[NT];
   const uint32_t* arow[NT];
   uint32_t amask[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int m = m0 + nt * 8 + g;
-    if (stage_x) {
-      // lanes without a token read the zero row: no predicate or mask in the loop
-      const int r = m < M ? nt * 8 + g : xrows;  // m < M implies nt * 8 + g < xrows
-      arow[nt] = reinterpret_cast<const uint32_t*>(xs + (size_t)r * xstride) + c;
-      amask[nt] = 0xffffffffu;
-    } else {
-      amask[nt] = m < M ? 0xffffffffu : 0u;
-      arow[nt] = reinterpret_cast<const uint32_t*>(A + (size_t)(m < M ? m : 0) * K) + c;
-    }
+    // lanes without a token read the zero row: no predicate or mask in the loop
+    const int r = m < M ? nt * 8 + g : xrows;  // m < M implies nt * 8 + g < xrows
+    xrow[nt] = xs + (size_t)r * xstride + c * 32;
+    amask[nt] = m < M ? 0xffffffffu : 0u;
+    arow[nt] = reinterpret_cast<const uint32_t*>(A + (size_t)(m < M ? m : 0) * K) + c;
   }
-  float acc[NT][4], cb[NT][4];
+  const unsigned char* xzero = xs + (size_t)xrows * xstride + c * 32;
+  const DqConst kq = Dq<T>::consts(zero);
+  float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = cb[nt][e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
+  // per-warp bases: the warp's first record in stage 0 and its activation fragments
+  const unsigned char* wrec = buf + (size_t)warp * UNIT * RC::kBytes + lane * 16;
+  const unsigned char* wparam = buf + (size_t)warp * UNIT * RC::kBytes;
   bool alive = true;
+  int slot = 0, t = t0, ga = 0, tp = 0;
+  uint32_t phase = 0;
   for (int i = 0; i < nst; ++i) {
-    const int slot = i % stages;
-    if (alive && !mbar_wait(&full[slot], (i / stages) & 1)) {
+    if (alive && !mbar_wait(&full[slot], phase)) {
       flags[0] = 1;
       alive = false;
     }
-    const int t = t0 + i / spt;
-    const int ga = (i % spt) * G;
-    const int n = alive ? min(G, ksteps4 - ga) : 0;
-    const unsigned char* sb = buf + (size_t)slot * G * RC::kBytes;
-    // records of this stage, in units of UNIT records per warp (a 128-block stays with one warp)
-    for (int u = warp; u * UNIT < n; u += kNC) {
+    const int n = alive ? min(kG, ksteps4 - ga) : 0;
+    const size_t soff = (size_t)slot * kG * RC::kBytes;
+    if (stage_x && n == kG) {
+      // full stage: every address is a per-stage base plus a compile-time offset
+      const int xoff = (ga + warp * UNIT) * 128;
 #pragma unroll
-      for (int r = 0; r < UNIT; ++r) {
-        const int q = u * UNIT + r;
-        if (q >= n) break;
-        const int gi = ga + q;
-        const unsigned char* rec = sb + (size_t)q * RC::kBytes;
-        uint32_t b[NT][8];
-        if (stage_x) {
+      for (int pu = 0; pu < PER; ++pu) {
+        const int qoff = pu * kNC * UNIT;
+        const unsigned char* xp[NT];
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const uint32_t* xr = arow[nt] + gi * 32;  // 64 halves per group
+        for (int nt = 0; nt < NT; ++nt) xp[nt] = xrow[nt] + xoff + qoff * 128;
+        mnb_unit<T, BLOCK, NT, true, PAIR>(wrec + soff + qoff * RC::kBytes, wparam + soff + qoff * RC::kBytes, xp,
+                                     arow, amask, 0, ksteps, g, kq, acc);
+      }
+    } else {
+      // short stage (or activations read from global memory): units past the end rerun the
+      // stage's first unit against zero activations (finite parameters, contribution exactly 0)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              b[nt][2 * j] = xr[j * 8];
-              b[nt][2 * j + 1] = xr[j * 8 + 4];
-            }
-          }
-        } else {
+      for (int pu = 0; pu < PER; ++pu) {
+        const int q0 = (pu * kNC + warp) * UNIT;
+        const bool valid = q0 < n;
+        const int q = valid ? q0 : 0;
+        const unsigned char* xp[NT];
+        uint32_t live[NT];
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int s = gi * 4 + j;
-              const int sc = s < ksteps ? s : 0;
-              const uint32_t live = s < ksteps ? amask[nt] : 0u;
-              b[nt][2 * j] = __ldg(arow[nt] + sc * 8) & live;
-              b[nt][2 * j + 1] = __ldg(arow[nt] + sc * 8 + 4) & live;
-            }
+        for (int nt = 0; nt < NT; ++nt) {
+          xp[nt] = (valid ? xrow[nt] : xzero) + (ga + q) * 128;
+          live[nt] = valid ? amask[nt] : 0u;
         }
-        const uint4 w4 = *reinterpret_cast<const uint4*>(rec + lane * 16);
-        const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
-        uint32_t bias_lo = 0, bias_hi = 0;
-        float2 scl = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const bool block_end = SPB <= 4 ? (j % SPB == SPB - 1) : (j == 3 && r == UNIT - 1);
-          const int sl = SPB <= 4 ? j / SPB : 0;
-          if (j % (SPB <= 4 ? SPB : 4) == 0) {  // parameters of the block this k-step belongs to
-            const uint32_t sw = *reinterpret_cast<const uint32_t*>(rec + RC::kSOff + (sl * 8 + g) * 4);
-            const uint32_t zb = rec[RC::kZOff + sl * 8 + g];
-            scl = s2_to_f2(sw, BF);
-            Dq<T>::bias(zb, bias_lo, bias_hi);
-          }
-          uint32_t a[4];
-          Dq<T>::run(words[j], bias_lo, bias_hi, a);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma16816<T>(cb[nt], a, b[nt][2 * j], b[nt][2 * j + 1]);
-          if (block_end) {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              acc[nt][0] = fmaf(cb[nt][0], scl.x, acc[nt][0]);
-              acc[nt][1] = fmaf(cb[nt][1], scl.x, acc[nt][1]);
-              acc[nt][2] = fmaf(cb[nt][2], scl.y, acc[nt][2]);
-              acc[nt][3] = fmaf(cb[nt][3], scl.y, acc[nt][3]);
-              cb[nt][0] = cb[nt][1] = cb[nt][2] = cb[nt][3] = 0.f;
-            }
-          }
-        }
+        const unsigned char* r0 = buf + soff + (size_t)q * RC::kBytes;
+        if (stage_x)
+          mnb_unit<T, BLOCK, NT, true, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
+        else
+          mnb_unit<T, BLOCK, NT, false, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
-    if (i % spt == spt - 1) {
-      // tile finished: merge the consumers' partial sums
+    if (++slot == kStages) slot = 0, phase ^= 1;
+    ga += kG;
+    if (ga >= ksteps4) {
+      // tile finished: merge the consumers' partial sums.  red is double-buffered by tile parity, so
+      // one barrier per tile suffices (a buffer is rewritten only after the next tile's barrier,
+      // which every warp reaches after finishing its part of this merge).  Thread tid sums output
+      // row tid / 16, column tid % 16: the columns of a 1-token chunk spread over all warps.
+      float* rb = red + (size_t)(tp & 1) * kNC * NT * 4 * 32;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          red[((warp * NT + nt) * 4 + e) * 32 + lane] = acc[nt][e];
+          if (PAIR || !(e & 1)) rb[((warp * NT + nt) * 4 + e) * 32 + lane] = acc[nt][e];
           acc[nt][e] = 0.f;
         }
       consumer_barrier();
-      if (warp == 0) {
-        float sum[NT][4];
+      for (int tid = threadIdx.x; tid < 256; tid += kNC * 32) {
+        const int row = tid >> 4, col = tid & 15;
+        const int m = m0 + col, n = t * 16 + row;
+        if (col < 8 * NT && m < M && n < N) {
+          const int nt = col >> 3, cc = col & 7;
+          const int e = (row >= 8 ? 2 : 0) + (cc & 1);
+          const int ln = (row & 7) * 4 + (cc >> 1);
+          float v = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < kNC; ++w) v += red[((w * NT + nt) * 4 + e) * 32 + lane];
-            sum[nt][e] = v;
-          }
-        const int n0 = t * 16 + g, n1 = n0 + 8;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int m = m0 + nt * 8 + 2 * c;
-          if (m < M) {
-            if (n0 < N) Y[(size_t)m * N + n0] = from_f<T>(sum[nt][0]);
-            if (n1 < N) Y[(size_t)m * N + n1] = from_f<T>(sum[nt][2]);
-          }
-          if (m + 1 < M) {
-            if (n0 < N) Y[(size_t)(m + 1) * N + n0] = from_f<T>(sum[nt][1]);
-            if (n1 < N) Y[(size_t)(m + 1) * N + n1] = from_f<T>(sum[nt][3]);
-          }
+          for (int w = 0; w < kNC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
+          Y[(size_t)m * N + n] = from_f<T>(v);
         }
       }
-      consumer_barrier();
+      ++tp;
+      ga = 0;
+      ++t;
     }
   }
   if (flags[0] && threadIdx.x == 0) report_device_error(err, kErrMnbTimeout, blockIdx.x);
@@ -463,17 +575,16 @@ cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8
 DeviceErrorSlot* device_error_slot();
 
 namespace {
-template <typename T, int BLOCK, int NT>
+template <typename T, int BLOCK, int NT, bool PAIR>
 cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
   using RC = Rec<BLOCK>;
-  const int G = 16;  // records per stage (~9.5 KB for block 32)
-  const int stages = 4;
   // activation rows staged in shared memory when they fit in 64 KB (M = 1: K <= 16K)
   const int rows = (int)std::min<int64_t>(8 * NT, M);
   const size_t x_bytes = (size_t)(rows + 1) * (p.ksteps4 * 64 * 2 + 16);
-  const int xrows = x_bytes <= 64 * 1024 ? rows : 0;
-  const size_t smem = 256 + (size_t)stages * G * RC::kBytes + (size_t)kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
-  auto kern = mnb_tma_kernel<T, BLOCK, NT>;
+  const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
+  const int xrows = x_bytes <= 64 * 1024 && a16 ? rows : 0;
+  const size_t smem = 256 + (size_t)kStages * kG * RC::kBytes + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
+  auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR>;
   static size_t configured = 0;  // per instantiation: the largest dynamic smem set so far
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -493,13 +604,14 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   dim3 grid((unsigned)ctas, (unsigned)((M + 8 * NT - 1) / (8 * NT)));
   kern<<<grid, (kNC + 1) * 32, smem, st>>>(static_cast<const T*>(A), static_cast<const uint8_t*>(p.w),
                                            static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                                           (int)p.ksteps4, G, stages, xrows, device_error_slot());
+                                           (int)p.ksteps4, xrows, 0u, device_error_slot());
   return cudaGetLastError();
 }
 
 template <typename T, int BLOCK>
 cudaError_t launch_nt(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
-  return M <= 8 ? launch_tma_t<T, BLOCK, 1>(A, p, Y, M, st) : launch_tma_t<T, BLOCK, 2>(A, p, Y, M, st);
+  if (M == 1) return launch_tma_t<T, BLOCK, 1, false>(A, p, Y, M, st);
+  return M <= 8 ? launch_tma_t<T, BLOCK, 1, true>(A, p, Y, M, st) : launch_tma_t<T, BLOCK, 2, true>(A, p, Y, M, st);
 }
 
 template <typename T>
