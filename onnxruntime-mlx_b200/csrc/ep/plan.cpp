@@ -518,9 +518,58 @@ std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& node
   }
   if (cfg.tp && p->shard_for_tp(err)) return nullptr;
   if (p->upload_constants(g, err)) return nullptr;
+  if (cfg.fuse) p->fuse_prologues();
   p->stats_.steps = (int)p->steps_.size();
   if (cfg.verbose) fprintf(stderr, "[b200ep] compiled partition: %s\n", p->describe().c_str());
   return p;
+}
+
+void Plan::fuse_prologues() {
+  for (bool changed = true; changed;) {
+    changed = false;
+    Uses u = uses_of(steps_, slots_.size());
+    for (int im = 0; im < (int)steps_.size() && !changed; ++im) {
+      Step& m = steps_[im];
+      if (m.kind != StepKind::kMnb || !m.prepacked || m.pro) continue;
+      const int a = m.in[0];
+      const int ip = u.producer[a];
+      if (ip < 0 || ip >= im || slots_[a].kind != Slot::kTemp || u.users[a].size() != 1) continue;
+      const Step& p = steps_[ip];
+      if (p.kind == StepKind::kRms) {
+        // the residual output (skip form) is now written by the GEMV: its readers must follow it
+        const int res = p.skip && p.out.size() > 1 ? p.out[1] : -1;
+        bool ok = true;
+        if (res >= 0)
+          for (int r : u.users[res]) ok &= r > im;
+        // nothing between the norm and the GEMV may overwrite the norm's inputs
+        for (int k = ip + 1; k < im && ok; ++k)
+          for (int o : steps_[k].out)
+            for (int i : p.in) ok &= o != i;
+        if (!ok) continue;
+        m.pro = p.skip ? kProSkipRms : kProRms;
+        m.pro_x = p.in[0];
+        m.pro_skip = p.skip ? p.in[1] : -1;
+        m.pro_gamma = p.in[p.skip ? 2 : 1];
+        m.pro_res = res;
+        m.pro_eps = p.eps;
+        ++stats_.fused_norm;
+      } else if (p.kind == StepKind::kSiluMul && p.N == m.K) {
+        bool ok = true;
+        for (int k = ip + 1; k < im && ok; ++k)
+          for (int o : steps_[k].out) ok &= o != p.in[0];
+        if (!ok) continue;
+        m.pro = kProSiluMul;
+        m.pro_x = p.in[0];
+        m.pro_n = p.N;
+        ++stats_.fused_act;
+      } else {
+        continue;
+      }
+      m.name = p.name + ">" + m.name;
+      steps_.erase(steps_.begin() + ip);
+      changed = true;
+    }
+  }
 }
 
 int Plan::shard_for_tp(std::string* err) {
@@ -538,6 +587,12 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
   for (const Step& st : steps_) {
     switch (st.kind) {
       case StepKind::kMnb: {
+        if (st.pro) {  // the folded producer's outputs: its activation buffer and the residual
+          auto sh = S[st.pro_x].shape;
+          if (st.pro == kProSiluMul && !sh.empty()) sh.back() = st.pro_n;
+          S[st.in[0]].shape = sh;
+          if (st.pro_res >= 0) S[st.pro_res].shape = S[st.pro_x].shape;
+        }
         const Slot& a = S[st.in[0]];
         if (a.shape.empty() || a.shape.back() != st.K)
           return fail("MatMulNBits " + st.name + ": input last dim " + shape_str(a.shape) + " != K=" + std::to_string(st.K));
@@ -646,7 +701,32 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
         if (s.prepacked) {
           MnbPacked pk = mnb_packed_geometry(s.N, s.K, s.block);
           pk.w = s.pk_w->p;
-          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, a.numel() / s.K, st);
+          const int64_t M = a.numel() / s.K;
+          if (s.pro) {
+            MnbPro pro;
+            pro.kind = s.pro;
+            pro.x = S[s.pro_x].ptr;
+            pro.skip = s.pro_skip >= 0 ? S[s.pro_skip].ptr : nullptr;
+            pro.gamma = s.pro_gamma >= 0 ? S[s.pro_gamma].ptr : nullptr;
+            pro.residual = s.pro_res >= 0 ? S[s.pro_res].ptr : nullptr;
+            pro.eps = s.pro_eps;
+            bool aligned = true;
+            for (const void* q : {pro.x, pro.skip, pro.gamma, (const void*)pro.residual})
+              aligned &= (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+            if (aligned && mnb_prologue_fits(M, s.K, s.block)) {
+              e = launch_mnb_packed(nullptr, pk, S[s.out[0]].ptr, a.dtype, M, st, &pro);
+              break;
+            }
+            // rows too large to stage (prefill): the standalone producer, then the plain GEMV
+            if (s.pro == kProSiluMul) {
+              e = launch_silu_mul(pro.x, a.ptr, a.dtype, M, s.pro_n, st);
+            } else {
+              RmsArgs r{pro.x, pro.skip, pro.gamma, a.ptr, pro.residual, a.dtype, M, s.K, s.pro_eps};
+              e = launch_rms_norm(r, st);
+            }
+            if (e != cudaSuccess) break;
+          }
+          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st);
           break;
         }
         MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
@@ -950,7 +1030,8 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
 std::string Plan::describe() const {
   std::ostringstream o;
   o << "{\"nodes\":" << stats_.nodes << ",\"steps\":" << steps_.size() << ",\"fused_qkv\":" << stats_.fused_qkv
-    << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"weight_bytes\":" << stats_.weight_bytes
+    << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"fused_norm\":" << stats_.fused_norm
+    << ",\"fused_act\":" << stats_.fused_act << ",\"weight_bytes\":" << stats_.weight_bytes
     << ",\"runs\":" << stats_.runs << ",\"graph_captures\":" << stats_.graph_captures
     << ",\"graph_replays\":" << stats_.graph_replays;
   int npk = 0;

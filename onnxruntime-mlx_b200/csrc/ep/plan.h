@@ -5,7 +5,9 @@
 //             read (weights stay resident in HBM), and runs the fusion passes
 //               - q/k/v MatMulNBits sharing one input -> one GEMV writing packed QKV, consumed by
 //                 GroupQueryAttention in its packed form;
-//               - gate/up MatMulNBits + Sigmoid/Mul/Mul (SwiGLU) -> one GEMV + one fused SiLU*up.
+//               - gate/up MatMulNBits + Sigmoid/Mul/Mul (SwiGLU) -> one GEMV + one fused SiLU*up;
+//               - (Skip)SimplifiedLayerNorm or SiLU*up whose only consumer is a prepacked GEMV ->
+//                 folded into that GEMV's activation staging (decode-sized rows).
 // run():      binds the boundary tensors (device pointers in place; host tensors staged), infers
 //             the shapes of the step, allocates per-shape-key buffers once, and launches the
 //             steps.  With CUDA graphs on, the launches of a (shape key, boundary pointers) pair
@@ -101,10 +103,16 @@ struct Step {
   // MatMulNBits weights prepacked for the tensor-core path (fp16/bf16, int4)
   bool prepacked = false;
   std::shared_ptr<DevMem> pk_w;
+  // producer of in[0] folded into the GEMV's activation staging (MnbProKind); the standalone
+  // producer still runs into in[0] when the rows do not fit the staging area
+  int pro = 0;
+  int pro_x = -1, pro_skip = -1, pro_gamma = -1, pro_res = -1;
+  float pro_eps = 0.f;
+  int64_t pro_n = 0;  // SiLU*up: width of the gate (= K)
 };
 
 struct PlanStats {
-  int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0;
+  int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0, fused_norm = 0, fused_act = 0;
   int64_t weight_bytes = 0;
   int64_t runs = 0, graph_replays = 0, graph_captures = 0;
 };
@@ -132,6 +140,7 @@ class Plan {
   int upload_constants(const Graph& g, std::string* err);
   void fuse_qkv();
   void fuse_swiglu();
+  void fuse_prologues();
   int shard_for_tp(std::string* err);
   int infer(std::vector<Slot>& slots, std::string* err) const;
   int launch_steps(const std::vector<Slot>& slots, Program& prog, cudaStream_t st);

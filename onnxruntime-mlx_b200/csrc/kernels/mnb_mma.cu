@@ -209,6 +209,7 @@ __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
 // ---- the TMA-fed streaming kernel -------------------------------------------------------------
 constexpr int kNC = 8;        // consumer warps
 constexpr int kStages = 4;    // ring stages
+constexpr size_t kXStageMax = 64 * 1024;  // bytes of staged activation rows (else read from global)
 constexpr int kG = 32;        // records per stage (one bulk copy, ~19 KB for block 32)
 enum { kErrMnbTimeout = 301 };
 
@@ -235,6 +236,113 @@ __device__ __forceinline__ void lds_words(const unsigned char* p, uint32_t (&v)[
 __device__ __forceinline__ int xperm_src_word(int w) {  // word within a 64-k group, staged order -> k order
   const int c = w >> 3, j = (w >> 1) & 3, h = w & 1;
   return j * 8 + h * 4 + c;
+}
+
+// Write 8 consecutive activations (k .. k+7 of one row, k % 8 == 0) into the fragment-order row.
+__device__ __forceinline__ void xs_put(unsigned char* row, int k, uint4 v) {
+  const int kw = k >> 1;                           // first source word of the chunk
+  const int grp = kw & ~31, sw = kw & 31;          // sw = j*8 + h*4 (c = 0..3 follow)
+  const int j = sw >> 3, h = (sw >> 2) & 1;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(row) + grp + 2 * j + h;
+  dst[0] = v.x, dst[8] = v.y, dst[16] = v.z, dst[24] = v.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+  const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f<T>(h[i]);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  T* h = reinterpret_cast<T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = from_f<T>(f[i]);
+  return v;
+}
+
+// Fused producers of the staged activations (consumer threads only; ends before the caller's
+// barrier).  Arithmetic follows the standalone kernels: SiLU(g) * u as in silu_mul_kernel, and the
+// (skip) RMS norm as in rms_norm_kernel — fp32 sum of squares of the (unrounded) row, y =
+// (t * inv) * gamma rounded once; the skip form writes the rounded sum t to pro.residual from the
+// CTAs of column 0 (blockIdx.x == 0).  wsum: kNC floats of scratch for the per-warp partials.
+template <typename T>
+__device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride, int kpad, int xrows, int m0,
+                               int M, int K, float* wsum) {
+  const int tid = threadIdx.x, nthr = kNC * 32;
+  const int cpr = kpad / 8;
+  // zero row (index xrows) for lanes without a token
+  for (int kc = tid; kc < cpr; kc += nthr) xs_put(xs + (size_t)xrows * xstride, kc * 8, make_uint4(0, 0, 0, 0));
+  if (pro.kind == kProSiluMul) {
+    const T* gu = static_cast<const T*>(pro.x);
+    for (int idx = tid; idx < xrows * cpr; idx += nthr) {
+      const int r = idx / cpr, k = (idx - r * cpr) * 8;
+      const int m = m0 + r;
+      float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (m < M && k < K) {
+        float gf[8], uf[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(gu + (size_t)m * 2 * K + k), gf);
+        unpack8<T>(*reinterpret_cast<const uint4*>(gu + (size_t)m * 2 * K + K + k), uf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = gf[i] / (1.f + __expf(-gf[i])) * uf[i];
+      }
+      xs_put(xs + (size_t)r * xstride, k, pack8<T>(f));
+    }
+    return;
+  }
+  const T* X = static_cast<const T*>(pro.x);
+  const T* S = static_cast<const T*>(pro.skip);
+  const T* G = static_cast<const T*>(pro.gamma);
+  T* R = blockIdx.x == 0 ? static_cast<T*>(pro.residual) : nullptr;
+  const bool skip = pro.kind == kProSkipRms;
+  for (int r = 0; r < xrows; ++r) {
+    const int m = m0 + r;
+    if (m >= M) {
+      for (int kc = tid; kc < cpr; kc += nthr) xs_put(xs + (size_t)r * xstride, kc * 8, make_uint4(0, 0, 0, 0));
+      continue;
+    }
+    float ss = 0.f;
+    for (int kc = tid; kc * 8 < K; kc += nthr) {
+      float t[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(X + (size_t)m * K + kc * 8), t);
+      if (skip) {
+        float sk[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(S + (size_t)m * K + kc * 8), sk);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] += sk[i];
+        if (R) *reinterpret_cast<uint4*>(R + (size_t)m * K + kc * 8) = pack8<T>(t);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(t[i], t[i], ss);
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) wsum[tid >> 5] = ss;
+    consumer_barrier();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNC; ++w) tot += wsum[w];
+    const float inv = rsqrtf(tot / (float)K + pro.eps);
+    for (int kc = tid; kc < cpr; kc += nthr) {
+      const int k = kc * 8;
+      float y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (k < K) {
+        float t[8], gm[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(X + (size_t)m * K + k), t);
+        if (skip) {
+          float sk[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(S + (size_t)m * K + k), sk);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) t[i] += sk[i];
+        }
+        unpack8<T>(*reinterpret_cast<const uint4*>(G + k), gm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = t[i] * inv * gm[i];
+      }
+      xs_put(xs + (size_t)r * xstride, k, pack8<T>(y));
+    }
+    consumer_barrier();  // wsum is reused by the next row
+  }
 }
 
 // One unit (UNIT consecutive records of one warp): dequantise, MMA per k-step, scale per block.
@@ -317,7 +425,7 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
 template <typename T, int BLOCK, int NT, bool PAIR>
 __global__ void __launch_bounds__((kNC + 1) * 32, 2)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
-               int ntiles, int ksteps4, int xrows, uint32_t zero, DeviceErrorSlot* err) {
+               int ntiles, int ksteps4, int xrows, uint32_t zero, MnbPro pro, DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int SPB = BLOCK / 16;          // k-steps per block
   constexpr int SL = RC::kSlots;
@@ -379,30 +487,28 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
 
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
   if (stage_x) {
-    // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
-    const int cpr = kpad / 8;  // 16-byte chunks per row
-    const int chunks = (xrows + 1) * cpr;
-    for (int base = threadIdx.x; base < chunks; base += 4 * kNC * 32) {
-      uint4 v[4];
+    if (pro.kind == kProNone) {
+      // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
+      const int cpr = kpad / 8;  // 16-byte chunks per row
+      const int chunks = (xrows + 1) * cpr;
+      for (int base = threadIdx.x; base < chunks; base += 4 * kNC * 32) {
+        uint4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = base + u * kNC * 32;
-        const int r = idx / cpr, k = (idx - r * cpr) * 8;
-        const int m = m0 + r;
-        v[u] = make_uint4(0, 0, 0, 0);
-        if (idx < chunks && r < xrows && m < M && k < K) v[u] = *reinterpret_cast<const uint4*>(A + (size_t)m * K + k);
-      }
+        for (int u = 0; u < 4; ++u) {
+          const int idx = base + u * kNC * 32;
+          const int r = idx / cpr, k = (idx - r * cpr) * 8;
+          const int m = m0 + r;
+          v[u] = make_uint4(0, 0, 0, 0);
+          if (idx < chunks && r < xrows && m < M && k < K) v[u] = *reinterpret_cast<const uint4*>(A + (size_t)m * K + k);
+        }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = base + u * kNC * 32;
-        if (idx < chunks) {
-          const int r = idx / cpr, kw = (idx - r * cpr) * 4;  // first source word of the chunk
-          const int grp = kw & ~31, sw = kw & 31;             // sw = j*8 + h*4 (c = 0..3 follow)
-          const int j = sw >> 3, h = (sw >> 2) & 1;
-          uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)r * xstride) + grp + 2 * j + h;
-          dst[0] = v[u].x, dst[8] = v[u].y, dst[16] = v[u].z, dst[24] = v[u].w;
+        for (int u = 0; u < 4; ++u) {
+          const int idx = base + u * kNC * 32;
+          if (idx < chunks) xs_put(xs + (size_t)(idx / cpr) * xstride, (idx % cpr) * 8, v[u]);
         }
       }
+    } else {
+      stage_prologue<T>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * kNC * NT * 4 * 32 - kNC);
     }
     consumer_barrier();
   }
@@ -576,13 +682,14 @@ DeviceErrorSlot* device_error_slot();
 
 namespace {
 template <typename T, int BLOCK, int NT, bool PAIR>
-cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
+cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
   using RC = Rec<BLOCK>;
   // activation rows staged in shared memory when they fit in 64 KB (M = 1: K <= 16K)
   const int rows = (int)std::min<int64_t>(8 * NT, M);
   const size_t x_bytes = (size_t)(rows + 1) * (p.ksteps4 * 64 * 2 + 16);
   const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
-  const int xrows = x_bytes <= 64 * 1024 && a16 ? rows : 0;
+  const int xrows = x_bytes <= kXStageMax && (a16 || pro.kind != kProNone) ? rows : 0;
+  if (pro.kind != kProNone && !xrows) return cudaErrorInvalidValue;  // caller checks mnb_prologue_fits
   const size_t smem = 256 + (size_t)kStages * kG * RC::kBytes + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR>;
   static size_t configured = 0;  // per instantiation: the largest dynamic smem set so far
@@ -604,33 +711,43 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   dim3 grid((unsigned)ctas, (unsigned)((M + 8 * NT - 1) / (8 * NT)));
   kern<<<grid, (kNC + 1) * 32, smem, st>>>(static_cast<const T*>(A), static_cast<const uint8_t*>(p.w),
                                            static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                                           (int)p.ksteps4, xrows, 0u, device_error_slot());
+                                           (int)p.ksteps4, xrows, 0u, pro, device_error_slot());
   return cudaGetLastError();
 }
 
 template <typename T, int BLOCK>
-cudaError_t launch_nt(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
-  if (M == 1) return launch_tma_t<T, BLOCK, 1, false>(A, p, Y, M, st);
-  return M <= 8 ? launch_tma_t<T, BLOCK, 1, true>(A, p, Y, M, st) : launch_tma_t<T, BLOCK, 2, true>(A, p, Y, M, st);
+cudaError_t launch_nt(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
+  if (M == 1) return launch_tma_t<T, BLOCK, 1, false>(A, p, Y, M, st, pro);
+  return M <= 8 ? launch_tma_t<T, BLOCK, 1, true>(A, p, Y, M, st, pro)
+                : launch_tma_t<T, BLOCK, 2, true>(A, p, Y, M, st, pro);
 }
 
 template <typename T>
-cudaError_t launch_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
+cudaError_t launch_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
   switch (p.block) {
-    case 16: return launch_nt<T, 16>(A, p, Y, M, st);
-    case 32: return launch_nt<T, 32>(A, p, Y, M, st);
-    case 64: return launch_nt<T, 64>(A, p, Y, M, st);
-    case 128: return launch_nt<T, 128>(A, p, Y, M, st);
+    case 16: return launch_nt<T, 16>(A, p, Y, M, st, pro);
+    case 32: return launch_nt<T, 32>(A, p, Y, M, st, pro);
+    case 64: return launch_nt<T, 64>(A, p, Y, M, st, pro);
+    case 128: return launch_nt<T, 128>(A, p, Y, M, st, pro);
   }
   return cudaErrorInvalidValue;
 }
 }  // namespace
 
-cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st) {
+cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st,
+                              const MnbPro* pro) {
   if (M == 0) return cudaSuccess;
-  if (dtype == kF16) return launch_b<__half>(A, p, Y, M, st);
-  if (dtype == kBF16) return launch_b<__nv_bfloat16>(A, p, Y, M, st);
+  const MnbPro none{};
+  const MnbPro& pr = pro ? *pro : none;
+  if (dtype == kF16) return launch_b<__half>(A, p, Y, M, st, pr);
+  if (dtype == kBF16) return launch_b<__nv_bfloat16>(A, p, Y, M, st, pr);
   return cudaErrorInvalidValue;
+}
+
+bool mnb_prologue_fits(int64_t M, int64_t K, int block) {
+  const MnbPacked g = mnb_packed_geometry(1, K, block);
+  const int64_t rows = std::min<int64_t>(M <= 8 ? 8 : 16, M);
+  return M > 0 && K % 8 == 0 && (size_t)(rows + 1) * (g.ksteps4 * 64 * 2 + 16) <= kXStageMax;
 }
 
 }  // namespace b200ep

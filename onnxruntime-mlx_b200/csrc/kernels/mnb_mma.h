@@ -20,11 +20,28 @@ struct MnbPacked {
   void* w = nullptr;
 };
 
+// Producer of the GEMV's activations fused into its shared-memory staging (decode sizes only, see
+// mnb_prologue_fits).  kProRms / kProSkipRms: A = rms_norm(x [+ skip]) * gamma, the skip form also
+// writing the rounded sum x + skip to `residual` (may be null); kProSiluMul: A = silu(g) * u with
+// x = [M, 2K] holding g in columns [0, K) and u in [K, 2K).
+enum MnbProKind : int { kProNone = 0, kProRms = 1, kProSkipRms = 2, kProSiluMul = 3 };
+struct MnbPro {
+  int kind = kProNone;
+  const void* x = nullptr;
+  const void* skip = nullptr;
+  const void* gamma = nullptr;
+  void* residual = nullptr;
+  float eps = 0.f;
+};
+
 int mnb_record_bytes(int block);
 MnbPacked mnb_packed_geometry(int64_t N, int64_t K, int block);
 bool mnb_mma_supported(int dtype, int bits, int block, int64_t K);
 cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8_t* zp, int scale_dtype,
                                const MnbPacked& p, cudaStream_t st);
-cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st);
+cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st,
+                              const MnbPro* pro = nullptr);
+// Whether a prologue can run fused for M rows of K activations (they must fit the staging area).
+bool mnb_prologue_fits(int64_t M, int64_t K, int block);
 
 }  // namespace b200ep

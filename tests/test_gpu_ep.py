@@ -146,16 +146,25 @@ def oracle_decoder_step(cfg, W, ids, kv, seqlens):
     return oracle.matmulnbits(nf, W["lm_head.B"], W["lm_head.scales"], W["lm_head.zp"], N=cfg.vocab, K=cfg.hidden)
 
 
-def test_small_decoder_prefill_and_decode_match_oracle(ep_mod):
+WIDE = dict(layers=1, hidden=4096, heads=32, kv_heads=8, head_dim=128, ffn=4096, vocab=512, max_seq=64)
+
+
+@pytest.mark.parametrize("shape", ["small", "wide"])
+def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
+    """Prefill then decode steps against the op-by-op oracle.  'wide' (K = 4096) runs its 16-row
+    prefill through the unfused fallback (the rows do not fit the GEMV staging area) and its decode
+    steps through the fused norm / SiLU prologues."""
     from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
 
-    cfg = DecoderConfig(**SMALL)
-    B, P, cap, steps = 2, 8, 32, 4
+    cfg = DecoderConfig(**(SMALL if shape == "small" else WIDE))
+    B, P, cap, steps = 2, 8, 32, (4 if shape == "small" else 2)
     Wp, Wd = {}, {}
     sess_p = ep_mod.Session(build_decoder(cfg, batch=B, seq=P, cap=cap, weights_out=Wp))
     sess_d = ep_mod.Session(build_decoder(cfg, batch=B, seq=1, cap=cap, weights_out=Wd))
     d = json.loads(sess_d.parts[0].describe())
     assert d["fused_qkv"] == cfg.layers and d["fused_swiglu"] == cfg.layers
+    # every norm and SiLU*up folds into the staging of the GEMV that consumes it
+    assert d["fused_norm"] == 2 * cfg.layers + 1 and d["fused_act"] == cfg.layers
     rng = np.random.default_rng(7)
     kv_dev = [[torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
               for _ in range(cfg.layers)]
