@@ -1,3 +1,4 @@
+#include <cstdlib>
 // extern "C" kernel entry points declared in include/b200ep.h: argument validation, error
 // reporting and the library-owned GQA workspace.  Every entry point catches C++ exceptions and
 // returns a status; nothing here aborts the host process (the reference's FFI panic guard,
@@ -93,6 +94,13 @@ using namespace b200ep;
   catch (...) {                                                             \
     return set_error(B200EP_EINTERNAL, "unknown exception");                \
   }
+
+namespace b200ep {
+bool pdl_enabled() {
+  static const bool on = getenv("ONNXRUNTIME_EP_B200_NO_PDL") == nullptr;
+  return on;
+}
+}  // namespace b200ep
 
 extern "C" {
 

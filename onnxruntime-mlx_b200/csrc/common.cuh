@@ -132,4 +132,32 @@ __device__ __forceinline__ void report_device_error(DeviceErrorSlot* slot, int c
 
 inline int div_up(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
+// ---- programmatic dependent launch ------------------------------------------------------------
+// Kernels of a decode chain are launched with programmatic stream serialization: a kernel may be
+// scheduled while its predecessor is still running (its CTAs start once the predecessor's CTAs
+// have all executed pdl_trigger or exited).  Every such kernel calls pdl_wait() before it touches
+// memory an earlier kernel of the stream writes (and before it writes anything an earlier kernel
+// reads); the wait returns once the predecessor grid has completed and its writes are visible, so
+// the ordering stays transitive along the chain.  Work on constant data (weight streams) may run
+// before the wait.  Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();  // false when ONNXRUNTIME_EP_B200_NO_PDL is set
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace b200ep

@@ -10,6 +10,8 @@ namespace b200ep {
 template <typename T>
 __global__ void binary_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y,
                               BinaryGeom g, int op) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < g.total;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t rem = i, ia = 0, ib = 0;
@@ -27,6 +29,8 @@ __global__ void binary_kernel(const T* __restrict__ a, const T* __restrict__ b, 
 
 template <typename T>
 __global__ void sigmoid_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = to_f<T>(x[i]);
     y[i] = from_f<T>(1.f / (1.f + __expf(-v)));
@@ -36,6 +40,8 @@ __global__ void sigmoid_kernel(const T* __restrict__ x, T* __restrict__ y, int64
 // gu: [rows, 2n] with the gate in columns [0, n) and up in [n, 2n); h = gate * sigmoid(gate) * up
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ h, int64_t rows, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = rows * n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / n, c = i - r * n;
@@ -47,6 +53,8 @@ __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ h, int
 
 template <typename TI, typename TO>
 __global__ void cast_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = from_f<TO>(to_f<TI>(x[i]));
 }
@@ -56,6 +64,8 @@ template <typename T, typename TI>
 __global__ void gbq_kernel(const uint8_t* __restrict__ data, const T* __restrict__ scales,
                            const uint8_t* __restrict__ zp, const TI* __restrict__ idx, T* __restrict__ out,
                            int64_t n_idx, int64_t rows, int64_t dim, int block, DeviceErrorSlot* err) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= n_idx) return;
   int64_t r = (int64_t)idx[warp];
@@ -98,9 +108,8 @@ cudaError_t launch_binary(const void* a, const void* b, void* y, int dtype, cons
   if (g.total == 0) return cudaSuccess;
   return by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
-    binary_kernel<T><<<grid_for(g.total), 256, 0, st>>>(static_cast<const T*>(a), static_cast<const T*>(b),
-                                                          static_cast<T*>(y), g, op);
-    return cudaGetLastError();
+    return launch_k(binary_kernel<T>, dim3(grid_for(g.total)), dim3(256), 0, st, static_cast<const T*>(a),
+                    static_cast<const T*>(b), static_cast<T*>(y), g, op);
   });
 }
 
@@ -108,8 +117,8 @@ cudaError_t launch_sigmoid(const void* x, void* y, int dtype, int64_t n, cudaStr
   if (n == 0) return cudaSuccess;
   return by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
-    sigmoid_kernel<T><<<grid_for(n), 256, 0, st>>>(static_cast<const T*>(x), static_cast<T*>(y), n);
-    return cudaGetLastError();
+    return launch_k(sigmoid_kernel<T>, dim3(grid_for(n)), dim3(256), 0, st, static_cast<const T*>(x),
+                    static_cast<T*>(y), n);
   });
 }
 
@@ -117,8 +126,8 @@ cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, in
   if (rows * n == 0) return cudaSuccess;
   return by_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
-    silu_mul_kernel<T><<<grid_for(rows * n), 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(h), rows, n);
-    return cudaGetLastError();
+    return launch_k(silu_mul_kernel<T>, dim3(grid_for(rows * n)), dim3(256), 0, st, static_cast<const T*>(gu),
+                    static_cast<T*>(h), rows, n);
   });
 }
 
@@ -128,8 +137,8 @@ cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n
     using TI = decltype(ti);
     return by_dtype(out_dt, [&](auto to) {
       using TO = decltype(to);
-      cast_kernel<TI, TO><<<grid_for(n), 256, 0, st>>>(static_cast<const TI*>(x), static_cast<TO*>(y), n);
-      return cudaGetLastError();
+      return launch_k(cast_kernel<TI, TO>, dim3(grid_for(n)), dim3(256), 0, st, static_cast<const TI*>(x),
+                      static_cast<TO*>(y), n);
     });
   });
 }
@@ -140,14 +149,12 @@ cudaError_t launch_gather_block_quantized(const GbqArgs& a, cudaStream_t st) {
   return by_dtype(a.dtype, [&](auto tag) {
     using T = decltype(tag);
     if (a.idx_dtype == kI64)
-      gbq_kernel<T, int64_t><<<blocks, 256, 0, st>>>(a.data, static_cast<const T*>(a.scales), a.zp,
-                                                     static_cast<const int64_t*>(a.indices), static_cast<T*>(a.out),
-                                                     a.n_idx, a.rows, a.dim, a.block, a.err);
-    else
-      gbq_kernel<T, int32_t><<<blocks, 256, 0, st>>>(a.data, static_cast<const T*>(a.scales), a.zp,
-                                                     static_cast<const int32_t*>(a.indices), static_cast<T*>(a.out),
-                                                     a.n_idx, a.rows, a.dim, a.block, a.err);
-    return cudaGetLastError();
+      return launch_k(gbq_kernel<T, int64_t>, dim3(blocks), dim3(256), 0, st, a.data, static_cast<const T*>(a.scales),
+                      a.zp, static_cast<const int64_t*>(a.indices), static_cast<T*>(a.out), a.n_idx, a.rows, a.dim,
+                      a.block, a.err);
+    return launch_k(gbq_kernel<T, int32_t>, dim3(blocks), dim3(256), 0, st, a.data, static_cast<const T*>(a.scales),
+                    a.zp, static_cast<const int32_t*>(a.indices), static_cast<T*>(a.out), a.n_idx, a.rows, a.dim,
+                    a.block, a.err);
   });
 }
 

@@ -184,6 +184,8 @@ gqa_decode_kernel(GqaKP kp, int stages) {
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();  // the KV buffers and this step's q/k/v come from earlier kernels
+  pdl_trigger();
   const int past = past_len(kp, b);
   const int total = past + kp.S;
   const bool ok = range_ok(kp, past);
@@ -514,6 +516,8 @@ gqa_decode_kernel(GqaKP kp, int stages) {
 // rotated and written with v into the KV buffer.
 template <typename T>
 __global__ void gqa_append_kernel(GqaKP kp) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float rowbuf[];  // [warps][D]
   const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_tok = kp.H + kp.HK;
@@ -558,6 +562,8 @@ __global__ void gqa_append_kernel(GqaKP kp) {
 // One CTA (128 threads) per (b, s, h) query row; scores for all keys staged in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(128) gqa_generic_kernel(GqaKP kp) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sh[];  // [D] q, [cap] scores, [4] reduction
   const int row = blockIdx.x;
   const int h = row % kp.H, s = (row / kp.H) % kp.S, b = row / (kp.H * kp.S);
@@ -666,8 +672,7 @@ cudaError_t launch_decode_t(const GqaKP& kp, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (e != cudaSuccess) return e;
   dim3 grid(kp.splits, kp.HK, kp.B);
-  kern<<<grid, (kNW + 1) * 32, L.total, st>>>(kp, stages);
-  return cudaGetLastError();
+  return launch_k(kern, grid, dim3((kNW + 1) * 32), (size_t)L.total, st, kp, stages);
   }
 }
 
@@ -700,8 +705,8 @@ template <typename T>
 cudaError_t launch_generic(const GqaKP& kp, cudaStream_t st) {
   const int warps = 4;
   const int items = kp.B * kp.S * (kp.H + kp.HK);
-  gqa_append_kernel<T><<<div_up(items, warps), warps * 32, warps * kp.D * sizeof(float), st>>>(kp);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(gqa_append_kernel<T>, dim3(div_up(items, warps)), dim3(warps * 32),
+                           warps * kp.D * sizeof(float), st, kp);
   if (e != cudaSuccess) return e;
   const size_t smem = (size_t)(kp.D + kp.cap + 4) * sizeof(float);
   auto kern = gqa_generic_kernel<T>;
@@ -709,8 +714,7 @@ cudaError_t launch_generic(const GqaKP& kp, cudaStream_t st) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<kp.B * kp.S * kp.H, 128, smem, st>>>(kp);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(kp.B * kp.S * kp.H), dim3(128), smem, st, kp);
 }
 
 }  // namespace

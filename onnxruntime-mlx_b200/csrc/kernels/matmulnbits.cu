@@ -53,6 +53,8 @@ template <typename TS, typename TO, int BITS>
 __global__ void mnb_dequant_kernel(const uint8_t* __restrict__ B, const TS* __restrict__ scales,
                                    const uint8_t* __restrict__ zp, TO* __restrict__ W, int64_t N,
                                    int64_t K, int block, int64_t nblocks) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = N * K;
   const int64_t rowbytes = nblocks * block * BITS / 8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -223,6 +225,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 mnb_gemv_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
                 const T* __restrict__ scales, const uint8_t* __restrict__ zp,
                 T* __restrict__ Y, int M, int N, int K, int nblocks, int cpr) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VPC = 128 / BITS;
   constexpr int XS = VPC + 4;
   extern __shared__ __align__(16) float xs[];  // [MT][cpr][XS]
@@ -295,6 +299,8 @@ mnb_tile_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
                 const T* __restrict__ scales, const uint8_t* __restrict__ zp,
                 T* __restrict__ Y, int M, int N, int K, int block, int nblocks) {
   __shared__ float as[kTK][kTM + 4];
+  pdl_wait();
+  pdl_trigger();
   __shared__ float ws[kTK][kTN + 4];
   const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -381,10 +387,9 @@ cudaError_t launch_gemv_t(const MnbArgs& a, cudaStream_t st) {
   const int64_t ntuples = (a.N + R - 1) / R;
   const int64_t want = (ntuples + kGemvWarps - 1) / kGemvWarps;
   const int grid = (int)std::min<int64_t>(want, (int64_t)per_sm * num_sms());
-  kern<<<grid, kGemvThreads, smem, st>>>(
-      static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales), a.zp,
-      static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, (int)nblocks, cpr);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(kGemvThreads), smem, st, static_cast<const T*>(a.A), a.B,
+                  static_cast<const T*>(a.scales), a.zp, static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K,
+                  (int)nblocks, cpr);
 }
 
 template <typename T, int BITS, int BLOCK, bool HAS_ZP>
@@ -420,15 +425,9 @@ cudaError_t launch_dtype(const MnbArgs& a, cudaStream_t st) {
                        (reinterpret_cast<uintptr_t>(a.B) % 16) == 0;
   if (gemv_ok) return a.bits == 4 ? launch_gemv_b<T, 4>(a, st) : launch_gemv_b<T, 8>(a, st);
   dim3 grid((unsigned)div_up(a.N, kTN), (unsigned)div_up(a.M, kTM));
-  if (a.bits == 4)
-    mnb_tile_kernel<T, 4><<<grid, 256, 0, st>>>(
-        static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales), a.zp,
-        static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, a.block, (int)nblocks);
-  else
-    mnb_tile_kernel<T, 8><<<grid, 256, 0, st>>>(
-        static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales), a.zp,
-        static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, a.block, (int)nblocks);
-  return cudaGetLastError();
+  auto kern = a.bits == 4 ? mnb_tile_kernel<T, 4> : mnb_tile_kernel<T, 8>;
+  return launch_k(kern, grid, dim3(256), 0, st, static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales),
+                  a.zp, static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K, a.block, (int)nblocks);
 }
 
 template <typename TS, typename TO>
@@ -436,13 +435,9 @@ cudaError_t launch_dequant_t(const MnbDequantArgs& a, cudaStream_t st) {
   const int64_t nblocks = (a.K + a.block - 1) / a.block;
   const int64_t total = a.N * a.K;
   int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  if (a.bits == 4)
-    mnb_dequant_kernel<TS, TO, 4><<<grid, 256, 0, st>>>(a.B, static_cast<const TS*>(a.scales), a.zp,
-                                                        static_cast<TO*>(a.W), a.N, a.K, a.block, nblocks);
-  else
-    mnb_dequant_kernel<TS, TO, 8><<<grid, 256, 0, st>>>(a.B, static_cast<const TS*>(a.scales), a.zp,
-                                                        static_cast<TO*>(a.W), a.N, a.K, a.block, nblocks);
-  return cudaGetLastError();
+  auto kern = a.bits == 4 ? mnb_dequant_kernel<TS, TO, 4> : mnb_dequant_kernel<TS, TO, 8>;
+  return launch_k(kern, dim3(grid), dim3(256), 0, st, a.B, static_cast<const TS*>(a.scales), a.zp,
+                  static_cast<TO*>(a.W), a.N, a.K, a.block, nblocks);
 }
 
 template <typename TS>

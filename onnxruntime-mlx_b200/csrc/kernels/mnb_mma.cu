@@ -463,6 +463,9 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     fence_mbarrier_init();
   }
   __syncthreads();
+  // the next kernel of the stream may be scheduled now; the weight stream reads constants only, the
+  // consumers wait for the previous kernel before they read activations or write outputs
+  pdl_trigger();
   if (warp == kNC) {
     if (lane == 0) {
       int slot = 0, t = t0, ga = 0;
@@ -486,6 +489,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   }
 
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
+  pdl_wait();
   if (stage_x) {
     if (pro.kind == kProNone) {
       // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
@@ -709,10 +713,9 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   }
   const int64_t ctas = std::min<int64_t>(p.ntiles, (int64_t)per_sm * num_sms());
   dim3 grid((unsigned)ctas, (unsigned)((M + 8 * NT - 1) / (8 * NT)));
-  kern<<<grid, (kNC + 1) * 32, smem, st>>>(static_cast<const T*>(A), static_cast<const uint8_t*>(p.w),
-                                           static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                                           (int)p.ksteps4, xrows, 0u, pro, device_error_slot());
-  return cudaGetLastError();
+  return launch_k(kern, grid, dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
+                  static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
+                  (int)p.ksteps4, xrows, 0u, pro, device_error_slot());
 }
 
 template <typename T, int BLOCK>

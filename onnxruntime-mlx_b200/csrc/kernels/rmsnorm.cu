@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(kRmsThreads)
 rms_norm_kernel(const T* __restrict__ X, const T* __restrict__ skip, const T* __restrict__ gamma,
                 T* __restrict__ Y, T* __restrict__ R, int64_t hidden, float eps) {
   __shared__ float red[kRmsThreads / 32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const T* x = X + row * hidden;
   const T* sk = SKIP ? skip + row * hidden : nullptr;
@@ -59,14 +61,12 @@ cudaError_t launch_t(const RmsArgs& a, cudaStream_t st) {
   if (a.rows == 0) return cudaSuccess;
   dim3 grid((unsigned)a.rows);
   if (a.skip)
-    rms_norm_kernel<T, true><<<grid, kRmsThreads, 0, st>>>(
-        static_cast<const T*>(a.X), static_cast<const T*>(a.skip), static_cast<const T*>(a.gamma),
-        static_cast<T*>(a.Y), static_cast<T*>(a.residual), a.hidden, a.eps);
-  else
-    rms_norm_kernel<T, false><<<grid, kRmsThreads, 0, st>>>(
-        static_cast<const T*>(a.X), nullptr, static_cast<const T*>(a.gamma), static_cast<T*>(a.Y),
-        nullptr, a.hidden, a.eps);
-  return cudaGetLastError();
+    return launch_k(rms_norm_kernel<T, true>, grid, dim3(kRmsThreads), 0, st, static_cast<const T*>(a.X),
+                    static_cast<const T*>(a.skip), static_cast<const T*>(a.gamma), static_cast<T*>(a.Y),
+                    static_cast<T*>(a.residual), a.hidden, a.eps);
+  return launch_k(rms_norm_kernel<T, false>, grid, dim3(kRmsThreads), 0, st, static_cast<const T*>(a.X),
+                  static_cast<const T*>(nullptr), static_cast<const T*>(a.gamma), static_cast<T*>(a.Y),
+                  static_cast<T*>(nullptr), a.hidden, a.eps);
 }
 }  // namespace
 
