@@ -18,8 +18,10 @@ and extrapolated to 32 layers.  --impl reference times that CPU oracle path alon
 reference implementation — Rust over MLX/Metal — cannot run on Linux; ORT's CPU EP is not
 installable here).
 
-Multi-GPU: one process per GPU under torchrun; every rank runs its own replica of the model on
-its batch (weak scaling); value = all ranks' tokens / max rank time.
+Multi-GPU: one process per GPU under torchrun, one model sharded over the ranks (tensor
+parallel, strong scaling): q/k/v, gate/up and the vocabulary projection split by output rows
+(attention by KV head), o_proj / down_proj split by K blocks and followed by an NCCL all-reduce,
+the logits all-gathered; every rank decodes the same tokens; value = tokens / max rank time.
 """
 
 from __future__ import annotations
@@ -52,26 +54,55 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons every 200 ms while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region runs: NVML every
+    10 ms (read-only queries), else nvidia-smi every 200 ms."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.samples = []
+        self.samples = []  # (sm_mhz, max_mhz, reason_names)
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+
+    def _handle(self):
+        import pynvml  # nvidia_ml_py
+
+        pynvml.nvmlInit()
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:  # noqa: BLE001
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def _run(self):
+        try:
+            nv, h = self._handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = get_reasons(h)
+                self.samples.append((float(sm), float(mx), [n for b, n in self.NAMES.items() if bits & b]))
+                self._stop.wait(0.01)
+            return
+        except Exception:  # noqa: BLE001
+            pass
+        fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={fields}",
                                       "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                parts = [p.strip() for p in out.stdout.strip().split(",")]
-                if len(parts) >= 9:
-                    self.samples.append(parts)
+                p = [x.strip() for x in out.stdout.strip().split(",")]
+                if len(p) >= 6:
+                    self.samples.append((float(p[0]), float(p[1]),
+                                         [names[i] for i in range(4) if "Active" in p[2 + i] and "Not" not in p[2 + i]]))
             except Exception:  # noqa: BLE001
                 pass
             self._stop.wait(0.2)
@@ -88,14 +119,10 @@ class ClockSampler:
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if "Active" in s[5 + i]
-                          and "Not" not in s[5 + i]})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples),
+                "reasons": sorted({n for s in self.samples for n in s[2]}), "samples": len(self.samples)}
 
 
 def dist_setup(n_gpus):
@@ -197,9 +224,11 @@ def cpu_baseline(cfg, batch, samples=2):
 
 
 # ---- the GPU arm ---------------------------------------------------------------------------
-def dominant_kernel_roofline(batch, peaks, peak_kind):
-    """Live CUDA-event timing of the fused gate/up GEMV shape (N = 2 x 14336, K = 4096, int4 block
-    32, fp16 scales + uint8 zp) over rotating weight copies larger than L2."""
+def dominant_kernel_roofline(batch, peaks, peak_kind, reps=10):
+    """Live CUDA-event timing of the dominant decode kernel — the fused gate/up int4 GEMV (N = 2 x
+    14336, K = 4096, block 32, fp16 scales + uint8 zero points) on the tensor-core path the plan
+    uses (weights prepacked into group records) — over rotating weight copies larger than L2,
+    replayed from a CUDA graph on the stream the kernels run on."""
     import numpy as np
     import torch
 
@@ -207,27 +236,29 @@ def dominant_kernel_roofline(batch, peaks, peak_kind):
 
     K, N, block = 4096, 2 * 14336, 32
     nb = K // block
-    per = N * nb * block // 2 + N * nb * 2 + N * nb // 2
+    per = N * nb * block // 2 + N * nb * 2 + N * nb // 2  # ORT-layout bytes of one weight set
     copies = max(3, int(np.ceil(3 * 126e6 / per)))
     g = torch.Generator(device="cuda").manual_seed(0)
-    Bs = [torch.randint(0, 256, (N, nb, block // 2), dtype=torch.uint8, device="cuda", generator=g)
-          for _ in range(copies)]
-    Ss = [(torch.rand(N * nb, device="cuda", generator=g) * 0.01 + 0.001).half() for _ in range(copies)]
-    Zs = [torch.randint(0, 256, (N * nb // 2,), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    packs = []
+    for _ in range(copies):
+        Bq = torch.randint(0, 256, (N, nb, block // 2), dtype=torch.uint8, device="cuda", generator=g)
+        S = (torch.rand(N * nb, device="cuda", generator=g) * 0.01 + 0.001).half()
+        Z = torch.randint(0, 256, (N * nb // 2,), dtype=torch.uint8, device="cuda", generator=g)
+        packs.append(ops.matmulnbits_prepack(Bq, S, Z, K=K, N=N, block_size=block))
+        del Bq, S, Z
     a = torch.randn(batch, K, device="cuda").half()
     y = torch.empty(batch, N, device="cuda", dtype=torch.float16)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         for i in range(copies):
-            ops.matmulnbits(a, Bs[i], Ss[i], Zs[i], K=K, N=N, out=y)
+            ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for i in range(copies):
-                ops.matmulnbits(a, Bs[i], Ss[i], Zs[i], K=K, N=N, out=y)
+                ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
         graph.replay()
         stream.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 10
         e0.record(stream)
         for _ in range(reps):
             graph.replay()
@@ -238,15 +269,15 @@ def dominant_kernel_roofline(batch, peaks, peak_kind):
     achieved = alg / launch_s / 1e9
     peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
     traffic = None
-    summ = os.path.join(ROOT, "profiles", "mnb_gemv_gate_up_fp16.txt")
+    summ = os.path.join(ROOT, "profiles", "mnb_tma_kernel_gate_up_m1.md")
     if os.path.exists(summ):
         for line in open(summ):
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = int(float(line.split(":")[1]))
-    return {"kernel": "mnb_gemv_kernel (fused gate/up: N=28672, K=4096, int4 b32, fp16)", "bound": "hbm",
-            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
-            "launch_us": round(launch_s * 1e6, 2), "traffic": traffic}
+    return {"kernel": "mnb_tma_kernel (fused gate/up: N=28672, K=4096, int4 b32, fp16, prepacked records)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs (of {peak_kind})",
+            "algorithmic_bytes_per_launch": alg, "launch_us": round(launch_s * 1e6, 2), "traffic": traffic}
 
 
 def run_ours(args, rank, world, local):
@@ -259,15 +290,24 @@ def run_ours(args, rank, world, local):
     cfg = LLAMA3_8B
     B = args.batch
     cap = PROMPT + GEN + 64
+    tp = world > 1  # one model sharded over the ranks (tensor parallel), the same tokens on every rank
     t_build = time.time()
+    ep = E.ExecutionProvider(device_id=local)
+    if tp:
+        import torch.distributed as dist
+
+        uid = [E.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ep.set_tensor_parallel(rank, world, uid[0])
     g = build_decoder(cfg, batch=-1, seq=-1, cap=-1)
-    sess = E.Session(g)
+    sess = E.Session(g, ep)
     part = sess.parts[0]
     t_build = time.time() - t_build
 
+    hk = cfg.kv_heads // world if tp else cfg.kv_heads
     kv = []
     for i in range(cfg.layers):
-        kv.append([torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda")
+        kv.append([torch.zeros(B, hk, cap, cfg.head_dim, dtype=torch.float16, device="cuda")
                    for _ in range(2)])
     names_in = part.input_names
     names_out = part.output_names
@@ -290,7 +330,7 @@ def run_ours(args, rank, world, local):
                                       ctypes.c_void_p(stream.cuda_stream)))
 
     # prefill the prompt through the same graph (untimed)
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(0 if tp else rank)
     prompt = torch.from_numpy(rng.integers(0, cfg.vocab, size=(B, PROMPT), dtype=np.int64)).cuda()
     pre_logits = torch.empty(B, PROMPT, cfg.vocab, dtype=torch.float16, device="cuda")
     t_pre = time.time()
@@ -337,7 +377,8 @@ def run_ours(args, rank, world, local):
         torch.cuda.synchronize()
     barrier(world)
     dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
-    value = world * B * args.steps / dev_s
+    seqs = B if tp else world * B  # sequences the whole job decodes per step
+    value = seqs * args.steps / dev_s
 
     # e2e through the C ABI with host buffers: ids / lengths staged H2D, logits read back per step
     h_ids = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
@@ -367,7 +408,7 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     e2e_s = max_over_ranks(max(e0.elapsed_time(e1) / 1e3, wall), world)
-    e2e = {"value": round(world * B * args.steps / e2e_s, 2), "unit": "tokens/s",
+    e2e = {"value": round(seqs * args.steps / e2e_s, 2), "unit": "tokens/s",
            "h2d_bytes_per_step": B * 8 + B * 4 + 4, "d2h_bytes_per_step": B * cfg.vocab * 2,
            "path": "b200ep_compiled_run with pinned host tensors"}
 
@@ -383,15 +424,18 @@ def run_ours(args, rank, world, local):
         "warmup": args.warmup,
         "ms_per_step": round(dev_s / args.steps * 1e3, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp else "weak",
         "vs_baseline": None,
         "dtype": "int4 weights, fp16 activations, fp32 accumulate",
         "data": "synthetic: random-init int4 weights (seed 0), random token ids",
         "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)",
                    "layers": cfg.layers, "hidden": cfg.hidden, "heads": f"{cfg.heads}/{cfg.kv_heads}",
-                   "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B, "global_batch": B * world,
+                   "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B, "global_batch": seqs,
                    "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + args.steps}",
-                   "kv_capacity": cap, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "kv_capacity": cap,
+                   "parallelism": (f"tp{world}: q/k/v, gate/up and lm_head split by output rows (attention by "
+                                   f"KV head), o/down by K blocks + NCCL all-reduce, logits all-gathered")
+                   if tp else "single GPU",
                    "l2": "weights 4.4 GB/step streamed from HBM (>> 126 MB L2)",
                    "cuda_graph_replays": desc["graph_replays"], "fused_qkv": desc["fused_qkv"],
                    "fused_swiglu": desc["fused_swiglu"], "prefill_s": round(t_pre, 2),
@@ -401,6 +445,12 @@ def run_ours(args, rank, world, local):
         "clocks": clocks.summary(),
         "gpu_launches": part.launches_per_run() * args.steps,
     }
+    # release the compiled partition (its CUDA graphs hold NCCL calls) before the process group goes
+    del part, sess, ep, ins, outs, ins_h, outs_h
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
     if rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline(cfg, B)
     return result
@@ -457,6 +507,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the dominant kernel (the roofline leg); used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -466,6 +518,17 @@ def main():
         res = run_reference(args, rank, world)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+
+    if args.kernel_only:
+        import torch
+
+        from onnxruntime_ep_b200 import load_library
+
+        load_library()
+        torch.cuda.set_device(0)
+        peaks, peak_kind = measured_peaks()
+        print(json.dumps(dominant_kernel_roofline(args.batch, peaks, peak_kind, reps=2)), flush=True)
         return
 
     rank, world, local = dist_setup(args.gpus)

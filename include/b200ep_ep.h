@@ -93,6 +93,15 @@ B200EP_API int b200ep_compiled_run(b200ep_compiled* c, const b200ep_tensor* inpu
 B200EP_API const char* b200ep_compiled_describe(b200ep_compiled* c);
 B200EP_API int b200ep_compiled_launches_per_run(const b200ep_compiled* c);
 
+/* Host-only preview of the tensor-parallel plan of `rank` of `world` for the whole graph: lowers,
+ * fuses and shards (no device memory, no NCCL) and writes a JSON array describing every step —
+ * MatMulNBits geometry with FNV-1a hashes of the sliced weight initializers, attention heads, and
+ * the inserted AllReduce / AllGather steps in launch order.  No counterpart in the reference (which
+ * has no multi-GPU path); it lets the sharding be checked on a machine without GPUs.  *needed
+ * receives the JSON length + 1; out may be NULL to query it. */
+B200EP_API int b200ep_tp_shard_preview(const b200ep_graph* g, int rank, int world, char* out, size_t cap,
+                                      size_t* needed);
+
 /* Tensor parallelism: attach this process (rank of world, one GPU each) to a communicator before
  * compiling; `nccl_unique_id` is the 128-byte ncclUniqueId rank 0 created
  * (b200ep_tp_unique_id) and broadcast.  Compiled plans then shard column-/row-parallel. */

@@ -374,6 +374,33 @@ B200EP_API int b200ep_tp_unique_id(void* out128) {
   GUARD_END
 }
 
+B200EP_API int b200ep_tp_shard_preview(const b200ep_graph* g, int rank, int world, char* out, size_t cap,
+                                      size_t* needed) {
+  GUARD_BEGIN
+  B200EP_CHECK_ARG(g && world >= 1 && rank >= 0 && rank < world, "bad graph or rank/world");
+  b200ep::EpConfig cfg;
+  cfg.host_only = true;
+  if (world > 1) {
+    cfg.tp = std::make_shared<TpContext>();
+    cfg.tp->rank = rank;
+    cfg.tp->world = world;
+  }
+  std::vector<int> nodes(g->g.nodes.size());
+  for (size_t i = 0; i < nodes.size(); ++i) nodes[i] = (int)i;
+  std::string err;
+  auto plan = Plan::compile(g->g, nodes, cfg, &err);
+  if (!plan) return set_error(B200EP_EUNSUPPORTED, "shard preview failed: " + err);
+  const std::string js = plan->preview();
+  if (needed) *needed = js.size() + 1;
+  if (out && cap > 0) {
+    const size_t n = std::min(cap - 1, js.size());
+    memcpy(out, js.data(), n);
+    out[n] = 0;
+  }
+  return B200EP_OK;
+  GUARD_END
+}
+
 B200EP_API int b200ep_ep_set_tensor_parallel(b200ep_ep* ep, int rank, int world, const void* nccl_unique_id) {
   GUARD_BEGIN
   B200EP_CHECK_ARG(ep && world >= 1 && rank >= 0 && rank < world, "bad tensor-parallel rank/world");

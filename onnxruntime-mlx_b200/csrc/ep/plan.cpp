@@ -517,6 +517,7 @@ std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& node
     p->fuse_swiglu();
   }
   if (cfg.tp && p->shard_for_tp(err)) return nullptr;
+  if (cfg.host_only) return p;
   if (p->upload_constants(g, err)) return nullptr;
   if (cfg.fuse) p->fuse_prologues();
   p->stats_.steps = (int)p->steps_.size();
@@ -572,10 +573,214 @@ void Plan::fuse_prologues() {
   }
 }
 
+namespace {
+
+// Row / block slicing of MatMulNBits initializers (ORT layout: B [N, nblocks, block*bits/8],
+// scales [N * nblocks] or [N, nblocks], zero points [N, ceil(nblocks/2)] packed int4 or [N, nblocks]).
+std::shared_ptr<Initializer> slice_rows(const Initializer& in, int64_t n_total,
+                                        const std::vector<std::pair<int64_t, int64_t>>& ranges,
+                                        const std::string& name) {
+  auto out = std::make_shared<Initializer>();
+  out->name = name;
+  out->dtype = in.dtype;
+  const size_t row_bytes = in.bytes.size() / (size_t)n_total;
+  int64_t rows = 0;
+  for (auto [a, b] : ranges) {
+    out->bytes.insert(out->bytes.end(), in.bytes.begin() + a * row_bytes, in.bytes.begin() + b * row_bytes);
+    rows += b - a;
+  }
+  out->shape = in.shape;
+  if (in.shape.size() >= 2 && in.shape[0] == n_total)
+    out->shape[0] = rows;
+  else
+    out->shape = {in.numel() / n_total * rows};
+  return out;
+}
+
+// blocks [b0, b1) of every row; elem_bits = bits per block entry (B: block*bits, scales: 8*esz,
+// packed int4 zero points: 4)
+std::shared_ptr<Initializer> slice_blocks(const Initializer& in, int64_t n, int64_t nblocks, int64_t b0, int64_t b1,
+                                          int elem_bits, const std::string& name) {
+  auto out = std::make_shared<Initializer>();
+  out->name = name;
+  out->dtype = in.dtype;
+  const int64_t nb = b1 - b0;
+  const size_t in_row = in.bytes.size() / (size_t)n;
+  if (elem_bits % 8 == 0) {
+    const size_t eb = elem_bits / 8;
+    for (int64_t r = 0; r < n; ++r) {
+      const uint8_t* src = in.bytes.data() + r * in_row + b0 * eb;
+      out->bytes.insert(out->bytes.end(), src, src + nb * eb);
+    }
+  } else {  // packed nibbles, low nibble = even block
+    const size_t out_row = (size_t)(nb + 1) / 2;
+    out->bytes.assign(out_row * n, 0);
+    for (int64_t r = 0; r < n; ++r)
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t byte = in.bytes[r * in_row + (b0 + b) / 2];
+        const uint8_t nib = ((b0 + b) & 1) ? (byte >> 4) : (byte & 0x0f);
+        out->bytes[r * out_row + b / 2] |= (uint8_t)((b & 1) ? nib << 4 : nib);
+      }
+  }
+  if (in.shape.size() == 3) out->shape = {n, nb, in.shape[2]};
+  else if (in.shape.size() == 2) out->shape = {n, (int64_t)(out->bytes.size() / n)};
+  else out->shape = {(int64_t)out->bytes.size() / std::max(1, dtype_size(in.dtype))};
+  return out;
+}
+
+}  // namespace
+
 int Plan::shard_for_tp(std::string* err) {
   if (!cfg_.tp || cfg_.tp->world == 1) return B200EP_OK;
-  *err = "tensor-parallel sharding is not available for this partition";
-  return B200EP_EUNSUPPORTED;
+  const int W = cfg_.tp->world, rk = cfg_.tp->rank;
+  auto fail = [&](const std::string& m) {
+    *err = "tensor parallel (" + std::to_string(W) + " ranks): " + m;
+    return B200EP_EUNSUPPORTED;
+  };
+  auto replace_const = [&](int id, std::shared_ptr<Initializer> init) {
+    const int nid = slot_of(init->name);
+    slots_[nid].kind = Slot::kConst;
+    slots_[nid].dtype = init->dtype;
+    slots_[nid].cshape = init->shape;
+    pending_consts_[nid] = init;
+    (void)id;
+    return nid;
+  };
+  // column split: keep output rows `ranges` of step m
+  auto split_cols = [&](Step& m, const std::vector<std::pair<int64_t, int64_t>>& ranges) -> int {
+    for (int w : {m.wB, m.wS, m.wZ})
+      if (w >= 0 && !pending_consts_.count(w)) return fail(m.name + ": weights not available for slicing");
+    const std::string tag = "#tp" + std::to_string(rk) + "of" + std::to_string(W);
+    m.wB = replace_const(m.wB, slice_rows(*pending_consts_[m.wB], m.N, ranges, m.name + "#B" + tag));
+    m.wS = replace_const(m.wS, slice_rows(*pending_consts_[m.wS], m.N, ranges, m.name + "#scales" + tag));
+    if (m.wZ >= 0) m.wZ = replace_const(m.wZ, slice_rows(*pending_consts_[m.wZ], m.N, ranges, m.name + "#zp" + tag));
+    int64_t n = 0;
+    for (auto [a, b] : ranges) n += b - a;
+    m.N = n;
+    return B200EP_OK;
+  };
+  // row split: keep input columns [k0, k1) of step m (block aligned)
+  auto split_k = [&](Step& m, int64_t k0, int64_t k1) -> int {
+    if (k0 % m.block || k1 % m.block || m.K % m.block) return fail(m.name + ": K shard not block aligned");
+    for (int w : {m.wB, m.wS, m.wZ})
+      if (w >= 0 && !pending_consts_.count(w)) return fail(m.name + ": weights not available for slicing");
+    const int64_t nblocks = m.K / m.block, b0 = k0 / m.block, b1 = k1 / m.block;
+    const std::string tag = "#tp" + std::to_string(rk) + "of" + std::to_string(W);
+    m.wB = replace_const(m.wB, slice_blocks(*pending_consts_[m.wB], m.N, nblocks, b0, b1, m.block * m.bits,
+                                            m.name + "#B" + tag));
+    const Initializer& sc = *pending_consts_[m.wS];
+    m.wS = replace_const(m.wS, slice_blocks(sc, m.N, nblocks, b0, b1, 8 * dtype_size(sc.dtype),
+                                            m.name + "#scales" + tag));
+    if (m.wZ >= 0)
+      m.wZ = replace_const(m.wZ, slice_blocks(*pending_consts_[m.wZ], m.N, nblocks, b0, b1, m.bits == 4 ? 4 : 8,
+                                              m.name + "#zp" + tag));
+    m.K = k1 - k0;
+    return B200EP_OK;
+  };
+  std::vector<int> row_parallel;  // steps whose partial sums need an all-reduce
+  std::set<int> done;
+  Uses u = uses_of(steps_, slots_.size());
+  for (int gi = 0; gi < (int)steps_.size(); ++gi) {
+    Step& g = steps_[gi];
+    if (g.kind != StepKind::kGqa) continue;
+    const int H = g.num_heads, HK = g.kv_heads, D = g.head_size;
+    if (H % W || HK % W) return fail("attention heads " + std::to_string(H) + "/" + std::to_string(HK) +
+                                     " do not divide over the ranks");
+    const int64_t hq = H / W, hk = HK / W;
+    if (g.packed) {
+      const int p = u.producer[g.in[0]];
+      if (p < 0 || steps_[p].kind != StepKind::kMnb || steps_[p].N != (int64_t)(H + 2 * HK) * D)
+        return fail(g.name + ": packed q/k/v does not come from one MatMulNBits");
+      if (int rc = split_cols(steps_[p], {{rk * hq * D, (rk + 1) * hq * D},
+                                          {(int64_t)H * D + rk * hk * D, (int64_t)H * D + (rk + 1) * hk * D},
+                                          {(int64_t)(H + HK) * D + rk * hk * D, (int64_t)(H + HK) * D + (rk + 1) * hk * D}}))
+        return rc;
+      done.insert(p);
+    } else {
+      const int64_t per[3] = {hq, hk, hk};
+      for (int j = 0; j < 3; ++j) {
+        const int p = u.producer[g.in[j]];
+        if (p < 0 || steps_[p].kind != StepKind::kMnb) return fail(g.name + ": q/k/v do not come from MatMulNBits");
+        if (int rc = split_cols(steps_[p], {{rk * per[j] * D, (rk + 1) * per[j] * D}})) return rc;
+        done.insert(p);
+      }
+    }
+    g.num_heads = (int)hq;
+    g.kv_heads = (int)hk;
+    for (int c : u.users[g.out[0]]) {
+      Step& o = steps_[c];
+      if (o.kind != StepKind::kMnb || o.in[0] != g.out[0] || done.count(c)) return fail(g.name + ": output consumer");
+      if (int rc = split_k(o, rk * hq * D, (rk + 1) * hq * D)) return rc;
+      done.insert(c);
+      row_parallel.push_back(c);
+    }
+  }
+  for (int ai = 0; ai < (int)steps_.size(); ++ai) {
+    Step& a = steps_[ai];
+    if (a.kind != StepKind::kSiluMul) continue;
+    const int64_t F = a.N;
+    if (F % W) return fail("FFN width does not divide over the ranks");
+    const int64_t f = F / W;
+    const int p = u.producer[a.in[0]];
+    if (p < 0 || steps_[p].kind != StepKind::kMnb || steps_[p].N != 2 * F) return fail(a.name + ": gate/up producer");
+    if (int rc = split_cols(steps_[p], {{rk * f, (rk + 1) * f}, {F + rk * f, F + (rk + 1) * f}})) return rc;
+    done.insert(p);
+    a.N = f;
+    for (int c : u.users[a.out[0]]) {
+      Step& d = steps_[c];
+      if (d.kind != StepKind::kMnb || d.in[0] != a.out[0] || done.count(c)) return fail(a.name + ": output consumer");
+      if (int rc = split_k(d, rk * f, (rk + 1) * f)) return rc;
+      done.insert(c);
+      row_parallel.push_back(c);
+    }
+  }
+  // vocabulary-split projection onto a partition output, then an all-gather of the logits
+  std::vector<int> gathered;
+  for (int li = 0; li < (int)steps_.size(); ++li) {
+    Step& l = steps_[li];
+    if (l.kind != StepKind::kMnb || done.count(li) || slots_[l.out[0]].kind != Slot::kOutput || l.N % W) continue;
+    const int64_t n = l.N / W, full = l.N;
+    if (int rc = split_cols(l, {{rk * n, (rk + 1) * n}})) return rc;
+    l.shard_cols = full;  // remembered for the gather step
+    done.insert(li);
+    gathered.push_back(li);
+  }
+  // insert the collectives after their producers (back to front keeps the indices valid)
+  std::vector<std::pair<int, Step>> ins;
+  for (int c : row_parallel) {
+    Step& m = steps_[c];
+    const int out = m.out[0];
+    const int part = slot_of(m.name + "#partial");
+    slots_[part].dtype = slots_[out].dtype;
+    m.out[0] = part;
+    Step ar{};
+    ar.kind = StepKind::kAllReduce;
+    ar.name = m.name + "#allreduce";
+    ar.in = {part};
+    ar.out = {out};
+    ins.push_back({c, ar});
+  }
+  for (int li : gathered) {
+    Step& l = steps_[li];
+    const int out = l.out[0];
+    const int shard = slot_of(l.name + "#shard");
+    const int stage = slot_of(l.name + "#gather");
+    slots_[shard].dtype = slots_[stage].dtype = slots_[out].dtype;
+    l.out[0] = shard;
+    Step ag{};
+    ag.kind = StepKind::kAllGather;
+    ag.name = l.name + "#allgather";
+    ag.in = {shard};
+    ag.out = {out};
+    ag.N = l.shard_cols;
+    ag.shard_cols = l.N;
+    ag.ws_slot = stage;
+    l.shard_cols = 0;
+    ins.push_back({li, ag});
+  }
+  std::sort(ins.begin(), ins.end(), [](auto& x, auto& y) { return x.first > y.first; });
+  for (auto& [pos, st] : ins) steps_.insert(steps_.begin() + pos + 1, st);
+  return B200EP_OK;
 }
 
 // ---- shape inference ------------------------------------------------------------------------
@@ -659,6 +864,7 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
         auto sh = S[st.in[0]].shape;
         sh.back() = st.N;
         S[st.out[0]].shape = sh;
+        if (st.ws_slot >= 0) S[st.ws_slot].shape = {S[st.in[0]].numel() * (st.N / std::max<int64_t>(st.shard_cols, 1))};
         break;
       }
     }
@@ -856,7 +1062,7 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
 
 int Plan::launches_per_run() const {
   int n = 0;
-  for (auto& s : steps_) n += 1;
+  for (auto& s : steps_) n += s.kind != StepKind::kAllReduce && s.kind != StepKind::kAllGather;
   return n;
 }
 
@@ -1025,6 +1231,39 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
   for (auto& o : out) any_host_out |= !o.on_device;
   if (any_host_out) B200EP_CUDA_RET(cudaStreamSynchronize(st));
   return B200EP_OK;
+}
+
+std::string Plan::preview() const {
+  static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
+                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+  auto fnv = [](const std::vector<uint8_t>& b) {
+    uint64_t h = 1469598103934665603ull;
+    for (uint8_t c : b) h = (h ^ c) * 1099511628211ull;
+    return h;
+  };
+  std::ostringstream o;
+  o << "[";
+  for (size_t i = 0; i < steps_.size(); ++i) {
+    const Step& st = steps_[i];
+    o << (i ? "," : "") << "{\"op\":\"" << names[(int)st.kind] << "\",\"name\":\"" << st.name << "\"";
+    if (st.kind == StepKind::kMnb) {
+      o << ",\"N\":" << st.N << ",\"K\":" << st.K;
+      const char* keys[3] = {"B", "scales", "zp"};
+      const int ids[3] = {st.wB, st.wS, st.wZ};
+      for (int j = 0; j < 3; ++j) {
+        auto it = pending_consts_.find(ids[j]);
+        if (ids[j] >= 0 && it != pending_consts_.end())
+          o << ",\"" << keys[j] << "\":\"" << std::hex << fnv(it->second->bytes) << std::dec << "\"";
+      }
+    } else if (st.kind == StepKind::kGqa) {
+      o << ",\"heads\":" << st.num_heads << ",\"kv_heads\":" << st.kv_heads;
+    } else if (st.kind == StepKind::kSiluMul || st.kind == StepKind::kAllGather) {
+      o << ",\"N\":" << st.N;
+    }
+    o << "}";
+  }
+  o << "]";
+  return o.str();
 }
 
 std::string Plan::describe() const {

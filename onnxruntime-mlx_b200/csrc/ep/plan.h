@@ -36,6 +36,7 @@ struct EpConfig {
   bool verbose = false;
   std::string layer_partitions;  // "" = unset
   std::shared_ptr<TpContext> tp;  // null = single GPU
+  bool host_only = false;         // lower, fuse and shard on the host only (no upload): preview()
 };
 
 struct TensorArg {
@@ -129,6 +130,9 @@ class Plan {
   int output_shapes(const std::vector<TensorArg>& in, std::vector<std::vector<int64_t>>* shapes);
   int run(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t st);
   std::string describe() const;
+  // Host-side view of the compiled steps (host_only plans): per step its kind, name and geometry,
+  // and for MatMulNBits a 64-bit FNV-1a hash of each (sliced) weight initializer.
+  std::string preview() const;
   const PlanStats& stats() const { return stats_; }
   // number of device kernels one run launches (for the launch-count claim of the bench)
   int launches_per_run() const;

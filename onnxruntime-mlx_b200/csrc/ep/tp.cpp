@@ -32,9 +32,22 @@ int tp_collective(const TpContext& tp, const Step& s, const std::vector<Slot>& S
   if (s.kind == StepKind::kAllReduce) {
     r = ncclAllReduce(x.ptr, y.ptr, (size_t)x.numel(), dt, ncclSum, static_cast<ncclComm_t>(tp.comm), st);
   } else {
-    // gather [rows, shard] blocks from every rank into [world, rows, shard]; the plan's gather
-    // step owns a staging slot laid out rank-major and permutes it to [rows, world*shard]
-    r = ncclAllGather(x.ptr, y.ptr, (size_t)x.numel(), dt, static_cast<ncclComm_t>(tp.comm), st);
+    // every rank holds [rows, shard] columns of [rows, shard * world]: gather rank-major, then
+    // place each rank's block at its column offset (one 2-D copy per rank; none for one row)
+    const int64_t shard = s.shard_cols, rows = x.numel() / std::max<int64_t>(shard, 1);
+    if (rows == 1) {
+      r = ncclAllGather(x.ptr, y.ptr, (size_t)x.numel(), dt, static_cast<ncclComm_t>(tp.comm), st);
+    } else {
+      const Slot& stage = S[s.ws_slot];
+      r = ncclAllGather(x.ptr, stage.ptr, (size_t)x.numel(), dt, static_cast<ncclComm_t>(tp.comm), st);
+      const size_t esz = (size_t)dtype_size(x.dtype);
+      for (int k = 0; r == ncclSuccess && k < tp.world; ++k) {
+        cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(y.ptr) + k * shard * esz, (size_t)s.N * esz,
+                                          static_cast<const char*>(stage.ptr) + (size_t)k * rows * shard * esz,
+                                          shard * esz, shard * esz, rows, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_status(e, "tensor-parallel gather placement");
+      }
+    }
   }
   if (r != ncclSuccess) return set_error(B200EP_ENCCL, std::string("NCCL: ") + ncclGetErrorString(r));
   return B200EP_OK;

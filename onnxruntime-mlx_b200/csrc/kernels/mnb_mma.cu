@@ -208,10 +208,20 @@ __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
 
 // ---- the TMA-fed streaming kernel -------------------------------------------------------------
 constexpr int kNC = 8;        // consumer warps
-constexpr int kStages = 4;    // ring stages
+constexpr int kMaxStages = 4; // ring stages (chosen per launch: 2..4)
 constexpr size_t kXStageMax = 64 * 1024;  // bytes of staged activation rows (else read from global)
 constexpr int kG = 32;        // records per stage (one bulk copy, ~19 KB for block 32)
 enum { kErrMnbTimeout = 301 };
+
+__device__ __forceinline__ int64_t lmin(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// Tile-major records [beg(c), beg(c + 1)) of CTA c: whole tiles, spread evenly.
+struct RecSplit {
+  int64_t R;  // records
+  int G;      // CTAs
+  int ks;     // records per tile
+  __device__ __forceinline__ int64_t beg(int c) const { return c >= G ? R : ((R / ks) * c / G) * ks; }
+};
 
 __device__ __forceinline__ void consumer_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kNC * 32) : "memory");
@@ -425,7 +435,8 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
 template <typename T, int BLOCK, int NT, bool PAIR>
 __global__ void __launch_bounds__((kNC + 1) * 32, 2)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
-               int ntiles, int ksteps4, int xrows, uint32_t zero, MnbPro pro, DeviceErrorSlot* err) {
+               int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro,
+               DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int SPB = BLOCK / 16;          // k-steps per block
   constexpr int SL = RC::kSlots;
@@ -435,10 +446,10 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   static_assert(kG % (kNC * UNIT) == 0, "stage must split evenly");
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kStages;
-  int* flags = reinterpret_cast<int*>(empty + kStages);
+  uint64_t* empty = full + kMaxStages;
+  int* flags = reinterpret_cast<int*>(empty + kMaxStages);
   unsigned char* buf = smem + 256;
-  float* red = reinterpret_cast<float*>(buf + (size_t)kStages * kG * RC::kBytes);  // [2][kNC][NT][4][32]
+  float* red = reinterpret_cast<float*>(buf + (size_t)stages * kG * RC::kBytes);  // [2][kNC][NT][4][32]
   // staged activation rows (xrows > 0): xrows + 1 rows (the last one zero) of kpad halves,
   // 16 bytes apart in bank order so the 8 row groups of a fragment load use all 32 banks
   unsigned char* xs = reinterpret_cast<unsigned char*>(red + 2 * kNC * NT * 4 * 32);
@@ -447,16 +458,14 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   const bool stage_x = xrows > 0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = (int)((int64_t)ntiles * blockIdx.x / gridDim.x);
-  const int t1 = (int)((int64_t)ntiles * (blockIdx.x + 1) / gridDim.x);
-  const int spt = (ksteps4 + kG - 1) / kG;  // stages per tile
-  const int nst = (t1 - t0) * spt;
+  const RecSplit part{(int64_t)ntiles * ksteps4, (int)gridDim.x, ksteps4};
+  const int64_t rbeg = part.beg(blockIdx.x), rend = part.beg(blockIdx.x + 1);
   const int m0 = blockIdx.y * 8 * NT;
   const int ksteps = K / 16;
 
   if (threadIdx.x == 0) {
     flags[0] = 0;
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kNC);
     }
@@ -468,21 +477,22 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   pdl_trigger();
   if (warp == kNC) {
     if (lane == 0) {
-      int slot = 0, t = t0, ga = 0;
+      // the CTA's records in stages of at most kG that never cross a tile boundary
+      int slot = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < nst; ++i) {
-        if (i >= kStages && !mbar_wait(&empty[slot], phase ^ 1)) {
+      int64_t r = rbeg;
+      for (int i = 0; r < rend; ++i) {
+        if (i >= stages && !mbar_wait(&empty[slot], phase ^ 1)) {
           flags[0] = 1;
           break;
         }
-        const int n = min(kG, ksteps4 - ga);
+        const int64_t tile_end = (r / ksteps4 + 1) * ksteps4;
+        const int n = (int)lmin(kG, lmin(rend, tile_end) - r);
         const uint32_t bytes = (uint32_t)(n * RC::kBytes);
         mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(buf + (size_t)slot * kG * RC::kBytes, recs + ((size_t)t * ksteps4 + ga) * RC::kBytes, bytes,
-                 &full[slot]);
-        ga += kG;
-        if (ga >= ksteps4) ga = 0, ++t;
-        if (++slot == kStages) slot = 0, phase ^= 1;
+        bulk_g2s(buf + (size_t)slot * kG * RC::kBytes, recs + (size_t)r * RC::kBytes, bytes, &full[slot]);
+        r += n;
+        if (++slot == stages) slot = 0, phase ^= 1;
       }
     }
     return;
@@ -541,14 +551,17 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   const unsigned char* wrec = buf + (size_t)warp * UNIT * RC::kBytes + lane * 16;
   const unsigned char* wparam = buf + (size_t)warp * UNIT * RC::kBytes;
   bool alive = true;
-  int slot = 0, t = t0, ga = 0, tp = 0;
+  int slot = 0, tp = 0;
   uint32_t phase = 0;
-  for (int i = 0; i < nst; ++i) {
+  int t = (int)(rbeg / ksteps4), ga = (int)(rbeg - (int64_t)t * ksteps4);
+  int gend = (int)lmin(rend - (int64_t)t * ksteps4, ksteps4);  // end of the segment
+  while ((int64_t)t * ksteps4 + ga < rend) {
     if (alive && !mbar_wait(&full[slot], phase)) {
       flags[0] = 1;
       alive = false;
     }
-    const int n = alive ? min(kG, ksteps4 - ga) : 0;
+    const int nplan = min(kG, gend - ga);
+    const int n = alive ? nplan : 0;
     const size_t soff = (size_t)slot * kG * RC::kBytes;
     if (stage_x && n == kG) {
       // full stage: every address is a per-stage base plus a compile-time offset
@@ -586,13 +599,13 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
-    if (++slot == kStages) slot = 0, phase ^= 1;
-    ga += kG;
-    if (ga >= ksteps4) {
-      // tile finished: merge the consumers' partial sums.  red is double-buffered by tile parity, so
-      // one barrier per tile suffices (a buffer is rewritten only after the next tile's barrier,
-      // which every warp reaches after finishing its part of this merge).  Thread tid sums output
-      // row tid / 16, column tid % 16: the columns of a 1-token chunk spread over all warps.
+    if (++slot == stages) slot = 0, phase ^= 1;
+    ga += nplan;
+    if (ga >= gend) {
+      // tile finished: merge the consumers' partial sums.  red is double-buffered by tile
+      // parity, so one barrier per tile suffices (a buffer is rewritten only after the next
+      // tile's barrier, which every warp reaches after finishing its part of this merge).  Thread
+      // tid sums output row tid / 16, column tid % 16: a 1-token chunk spreads over all warps.
       float* rb = red + (size_t)(tp & 1) * kNC * NT * 4 * 32;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -616,8 +629,9 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         }
       }
       ++tp;
-      ga = 0;
       ++t;
+      ga = 0;
+      gend = (int)lmin(rend - (int64_t)t * ksteps4, ksteps4);
     }
   }
   if (flags[0] && threadIdx.x == 0) report_device_error(err, kErrMnbTimeout, blockIdx.x);
@@ -688,34 +702,54 @@ namespace {
 template <typename T, int BLOCK, int NT, bool PAIR>
 cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
   using RC = Rec<BLOCK>;
-  // activation rows staged in shared memory when they fit in 64 KB (M = 1: K <= 16K)
+  // activation rows staged in shared memory when they fit (M = 1: K <= 16K)
   const int rows = (int)std::min<int64_t>(8 * NT, M);
   const size_t x_bytes = (size_t)(rows + 1) * (p.ksteps4 * 64 * 2 + 16);
   const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
   const int xrows = x_bytes <= kXStageMax && (a16 || pro.kind != kProNone) ? rows : 0;
   if (pro.kind != kProNone && !xrows) return cudaErrorInvalidValue;  // caller checks mnb_prologue_fits
-  const size_t smem = 256 + (size_t)kStages * kG * RC::kBytes + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR>;
+  auto smem_for = [&](int stages) {
+    return 256 + (size_t)stages * kG * RC::kBytes + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
+  };
   static size_t configured = 0;  // per instantiation: the largest dynamic smem set so far
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem_for(kMaxStages) > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(kMaxStages));
     if (e != cudaSuccess) return e;
-    configured = smem;
+    configured = smem_for(kMaxStages);
   }
-  static size_t occ_smem = 0;  // occupancy of the last smem size seen (one query per new size)
-  static int per_sm = 1;
-  if (smem != occ_smem) {
+  // deepest ring that still leaves two CTAs per SM (weights in flight per SM ~ 2 x ring)
+  static size_t occ_key[8] = {};
+  static int occ_val[8] = {};
+  auto per_sm_for = [&](size_t smem, int* out) -> cudaError_t {
+    for (int i = 0; i < 8; ++i)
+      if (occ_key[i] == smem) return (*out = occ_val[i]), cudaSuccess;
     int n = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kNC + 1) * 32, smem);
     if (e != cudaSuccess) return e;
-    per_sm = std::max(1, n);
-    occ_smem = smem;
+    for (int i = 0; i < 8; ++i)
+      if (!occ_key[i]) {
+        occ_key[i] = smem, occ_val[i] = n;
+        break;
+      }
+    return (*out = n), cudaSuccess;
+  };
+  int stages = kMaxStages, per_sm = 0;
+  for (int sg = kMaxStages; sg >= 2; --sg) {
+    int n = 0;
+    if (cudaError_t e = per_sm_for(smem_for(sg), &n)) return e;
+    if (sg == kMaxStages) per_sm = std::max(1, n);
+    if (n >= 2) {
+      stages = sg, per_sm = n;
+      break;
+    }
   }
+  const size_t smem = smem_for(stages);
+  const unsigned gy = (unsigned)((M + 8 * NT - 1) / (8 * NT));
   const int64_t ctas = std::min<int64_t>(p.ntiles, (int64_t)per_sm * num_sms());
-  dim3 grid((unsigned)ctas, (unsigned)((M + 8 * NT - 1) / (8 * NT)));
-  return launch_k(kern, grid, dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
+  return launch_k(kern, dim3((unsigned)ctas, gy), dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                  (int)p.ksteps4, xrows, 0u, pro, device_error_slot());
+                  (int)p.ksteps4, xrows, 0u, stages, pro, device_error_slot());
 }
 
 template <typename T, int BLOCK>

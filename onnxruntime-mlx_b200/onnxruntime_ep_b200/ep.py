@@ -73,6 +73,7 @@ def _lib():
         L.b200ep_compiled_launches_per_run.argtypes = [vp]
         L.b200ep_tp_unique_id.argtypes = [vp]
         L.b200ep_ep_set_tensor_parallel.argtypes = [vp, i32, i32, vp]
+        L.b200ep_tp_shard_preview.argtypes = [vp, i32, i32, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
         _configured = True
     return L
 
@@ -204,6 +205,17 @@ def tp_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     check(_lib().b200ep_tp_unique_id(buf))
     return buf.raw
+
+
+def tp_shard_preview(g: GraphBuilder, rank: int, world: int) -> list:
+    """Host-only view of rank `rank`'s tensor-parallel plan of the whole graph (no GPU needed)."""
+    import json
+
+    need = ctypes.c_size_t(0)
+    check(_lib().b200ep_tp_shard_preview(g.handle, rank, world, None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    check(_lib().b200ep_tp_shard_preview(g.handle, rank, world, buf, need.value, ctypes.byref(need)))
+    return json.loads(buf.value.decode())
 
 
 def _torch_code(t) -> int:
