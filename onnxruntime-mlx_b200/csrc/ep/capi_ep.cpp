@@ -421,6 +421,10 @@ B200EP_API int b200ep_ep_set_tensor_parallel(b200ep_ep* ep, int rank, int world,
   tp->world = world;
   tp->comm = comm;
   tp->owns_comm = true;
+  // decode-sized partial sums (16 rows x 16384 fp16/bf16 per source rank) travel through the
+  // peer mailboxes; larger ones through NCCL
+  if (!truthy(getenv("ONNXRUNTIME_EP_B200_NO_PEER_ALLREDUCE")))
+    if (int rc = tp_mailbox_init(*tp, (size_t)16 * 16384 * 2)) return rc;
   ep->cfg.tp = tp;
   return B200EP_OK;
 #else

@@ -42,6 +42,21 @@ struct Plan::Program {
 };
 
 Plan::~Plan() {
+  if (!prof_ms_.empty()) {
+    double tot = 0;
+    for (auto& kv : prof_ms_) tot += kv.second.second;
+    std::vector<std::pair<double, std::string>> order;
+    for (auto& kv : prof_ms_) order.push_back({-kv.second.second, kv.first});
+    std::sort(order.begin(), order.end());
+    fprintf(stderr, "[b200ep profile] rank %d: %.3f ms over %lld runs\n", cfg_.tp ? cfg_.tp->rank : 0, tot,
+            (long long)stats_.runs);
+    for (auto& [neg, name] : order) {
+      auto& v = prof_ms_[name];
+      fprintf(stderr, "[b200ep profile]   %-48s n=%6lld total=%9.3f ms avg=%8.2f us %5.1f%%\n", name.c_str(),
+              (long long)v.first, v.second, v.second * 1e3 / v.first, 100.0 * v.second / tot);
+    }
+  }
+  for (auto e : prof_ev_) cudaEventDestroy(e);
   programs_.clear();
   if (stream_) cudaStreamDestroy(stream_);
   if (ev_in_) cudaEventDestroy(ev_in_);
@@ -60,6 +75,17 @@ int64_t numel_of(const std::vector<int64_t>& s) {
   int64_t n = 1;
   for (auto d : s) n *= d;
   return n;
+}
+
+MnbAr make_ar(const TpContext& tp) {
+  MnbAr a;
+  a.world = tp.world;
+  a.rank = tp.rank;
+  a.ctrs = static_cast<unsigned*>(tp.ar_ctrs);
+  for (int k = 0; k < tp.world; ++k) a.mbox[k] = static_cast<char*>(tp.ar_peer[k]);
+  a.slot_bytes = tp.ar_slot_bytes;
+  a.region_bytes = (size_t)tp.world * tp.ar_slot_bytes;
+  return a;
 }
 
 bool env_on(const char* name) {
@@ -510,6 +536,7 @@ std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& node
                                     std::string* err) {
   std::unique_ptr<Plan> p(new Plan());
   p->cfg_ = cfg;
+  p->prof_ = env_on("ONNXRUNTIME_EP_B200_PROFILE");
   p->stats_.nodes = (int)nodes.size();
   if (p->lower(g, nodes, err)) return nullptr;
   if (cfg.fuse && !env_on("ONNXRUNTIME_EP_B200_NO_FUSION")) {
@@ -519,7 +546,10 @@ std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& node
   if (cfg.tp && p->shard_for_tp(err)) return nullptr;
   if (cfg.host_only) return p;
   if (p->upload_constants(g, err)) return nullptr;
-  if (cfg.fuse) p->fuse_prologues();
+  if (cfg.fuse) {
+    p->fuse_prologues();
+    p->fuse_peer_allreduce();
+  }
   p->stats_.steps = (int)p->steps_.size();
   if (cfg.verbose) fprintf(stderr, "[b200ep] compiled partition: %s\n", p->describe().c_str());
   return p;
@@ -570,6 +600,47 @@ void Plan::fuse_prologues() {
       steps_.erase(steps_.begin() + ip);
       changed = true;
     }
+  }
+}
+
+bool Plan::ar_fused(int64_t M, int64_t hidden, int cons_block) const {
+  return cfg_.tp && cfg_.tp->ar_ok && M >= 1 && M <= 16 && hidden % 8 == 0 &&
+         (size_t)(M * hidden * 2) <= cfg_.tp->ar_slot_bytes &&
+         mnb_prologue_fits(M, hidden, cons_block);
+}
+
+void Plan::fuse_peer_allreduce() {
+  if (!cfg_.tp || !cfg_.tp->ar_ok) return;
+  Uses u = uses_of(steps_, slots_.size());
+  // readers of a slot, counting the inputs folded into GEMV prologues
+  auto readers = [&](int slot) {
+    std::vector<int> r = u.users[slot];
+    for (int i = 0; i < (int)steps_.size(); ++i)
+      for (int x : {steps_[i].pro_x, steps_[i].pro_skip, steps_[i].pro_gamma})
+        if (x == slot) r.push_back(i);
+    return r;
+  };
+  for (int ai = 0; ai < (int)steps_.size(); ++ai) {
+    Step& a = steps_[ai];
+    if (a.kind != StepKind::kAllReduce) continue;
+    const int ip = u.producer[a.in[0]];
+    if (ip < 0 || steps_[ip].kind != StepKind::kMnb || !steps_[ip].prepacked || steps_[ip].ar_out) continue;
+    const std::vector<int> rd = readers(a.out[0]);
+    if (rd.size() != 1 || slots_[a.out[0]].kind != Slot::kTemp) continue;
+    const int im = rd[0];
+    Step& m = steps_[im];
+    if (m.kind != StepKind::kMnb || !m.prepacked || m.pro != kProSkipRms || m.pro_x != a.out[0] || im < ai) continue;
+    // the consumer pairs with the latest producer: no other mailbox producer in between
+    bool clear = true;
+    for (int k = ip + 1; k < im; ++k) clear &= !steps_[k].ar_out;
+    if (!clear) continue;
+    Step& p = steps_[ip];
+    p.ar_out = true;
+    p.ar_block = m.block;
+    a.ar_skip = true;
+    a.ar_block = m.block;
+    m.pro_ar = true;
+    ++stats_.peer_allreduce;
   }
 }
 
@@ -899,7 +970,18 @@ int Plan::output_shapes(const std::vector<TensorArg>& in, std::vector<std::vecto
 
 // ---- launches -------------------------------------------------------------------------------
 int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  const bool prof = prof_ && cs == cudaStreamCaptureStatusNone;
+  if (prof && prof_ev_.size() < 2 * steps_.size() + 2) {
+    for (auto ev : prof_ev_) cudaEventDestroy(ev);
+    prof_ev_.assign(2 * steps_.size() + 2, nullptr);
+    for (auto& ev : prof_ev_) cudaEventCreate(&ev);
+  }
+  int si = 0;
   for (const Step& s : steps_) {
+    if (prof) cudaEventRecord(prof_ev_[2 * si], st);
+    ++si;
     cudaError_t e = cudaSuccess;
     switch (s.kind) {
       case StepKind::kMnb: {
@@ -908,6 +990,9 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
           MnbPacked pk = mnb_packed_geometry(s.N, s.K, s.block);
           pk.w = s.pk_w->p;
           const int64_t M = a.numel() / s.K;
+          MnbAr oar;
+          if (s.ar_out && ar_fused(M, s.N, s.ar_block)) oar = make_ar(*cfg_.tp);
+          const MnbAr* out_ar = oar.world ? &oar : nullptr;
           if (s.pro) {
             MnbPro pro;
             pro.kind = s.pro;
@@ -916,11 +1001,12 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
             pro.gamma = s.pro_gamma >= 0 ? S[s.pro_gamma].ptr : nullptr;
             pro.residual = s.pro_res >= 0 ? S[s.pro_res].ptr : nullptr;
             pro.eps = s.pro_eps;
+            if (s.pro_ar && ar_fused(M, s.K, s.block)) pro.ar = make_ar(*cfg_.tp);
             bool aligned = true;
             for (const void* q : {pro.x, pro.skip, pro.gamma, (const void*)pro.residual})
               aligned &= (reinterpret_cast<uintptr_t>(q) & 15) == 0;
             if (aligned && mnb_prologue_fits(M, s.K, s.block)) {
-              e = launch_mnb_packed(nullptr, pk, S[s.out[0]].ptr, a.dtype, M, st, &pro);
+              e = launch_mnb_packed(nullptr, pk, S[s.out[0]].ptr, a.dtype, M, st, &pro, out_ar);
               break;
             }
             // rows too large to stage (prefill): the standalone producer, then the plain GEMV
@@ -932,7 +1018,7 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
             }
             if (e != cudaSuccess) break;
           }
-          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st);
+          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st, nullptr, out_ar);
           break;
         }
         MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
@@ -999,7 +1085,7 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
         a.workspace_bytes = (size_t)S[s.ws_slot].numel();
         int rc = launch_gqa(a, st);
         if (rc) return rc;
-        continue;
+        break;
       }
       case StepKind::kRms: {
         const Slot& x = S[s.in[0]];
@@ -1049,12 +1135,37 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
       }
       case StepKind::kAllReduce:
       case StepKind::kAllGather: {
+        if (s.ar_skip) {
+          const Slot& x = S[s.in[0]];
+          const int64_t hidden = x.shape.back();
+          if (ar_fused(x.numel() / hidden, hidden, s.ar_block)) break;  // summed in the consumer's prologue
+        }
         int rc = tp_collective(*cfg_.tp, s, S, st);
         if (rc) return rc;
-        continue;
+        break;
       }
     }
     if (e != cudaSuccess) return cuda_status(e, ("launch " + s.name).c_str());
+    if (prof) cudaEventRecord(prof_ev_[2 * si - 1], st);
+  }
+  if (prof) {
+    cudaStreamSynchronize(st);
+    static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
+                                  "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+    for (int i = 0; i < si; ++i) {
+      const Step& s = steps_[i];
+      std::string key = names[(int)s.kind];
+      if (s.kind == StepKind::kMnb)
+        key += " M=" + std::to_string(S[s.in[0]].numel() / std::max<int64_t>(s.K, 1)) + " N=" + std::to_string(s.N) +
+               " K=" + std::to_string(s.K) + (s.pro ? " +prologue" : "") + (s.ar_out ? " +peer-out" : "");
+      else if (s.kind == StepKind::kGqa)
+        key += " rows=" + std::to_string(S[s.in[0]].numel() / std::max<int64_t>(S[s.in[0]].shape.back(), 1));
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, prof_ev_[2 * i], prof_ev_[2 * i + 1]);
+      auto& v = prof_ms_[key];
+      v.first += 1;
+      v.second += ms;
+    }
   }
   (void)prog;
   return B200EP_OK;
@@ -1270,7 +1381,8 @@ std::string Plan::describe() const {
   std::ostringstream o;
   o << "{\"nodes\":" << stats_.nodes << ",\"steps\":" << steps_.size() << ",\"fused_qkv\":" << stats_.fused_qkv
     << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"fused_norm\":" << stats_.fused_norm
-    << ",\"fused_act\":" << stats_.fused_act << ",\"weight_bytes\":" << stats_.weight_bytes
+    << ",\"fused_act\":" << stats_.fused_act << ",\"peer_allreduce\":" << stats_.peer_allreduce
+    << ",\"weight_bytes\":" << stats_.weight_bytes
     << ",\"runs\":" << stats_.runs << ",\"graph_captures\":" << stats_.graph_captures
     << ",\"graph_replays\":" << stats_.graph_replays;
   int npk = 0;

@@ -110,12 +110,18 @@ struct Step {
   int pro_x = -1, pro_skip = -1, pro_gamma = -1, pro_res = -1;
   float pro_eps = 0.f;
   int64_t pro_n = 0;  // SiLU*up: width of the gate (= K)
+  // tensor parallel, decode sizes: the all-reduce between a row-parallel GEMV (ar_out) and the
+  // GEMV whose skip-norm prologue reads its sum (pro_ar) runs through the peer mailboxes; the
+  // AllReduce step between them (ar_skip) then launches nothing
+  bool ar_out = false, pro_ar = false, ar_skip = false;
+  int ar_block = 0;  // block size of the consuming GEMV (its staging decides the fused path)
 };
 
 struct PlanStats {
   int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0, fused_norm = 0, fused_act = 0;
   int64_t weight_bytes = 0;
   int64_t runs = 0, graph_replays = 0, graph_captures = 0;
+  int peer_allreduce = 0;
 };
 
 class Plan {
@@ -145,6 +151,8 @@ class Plan {
   void fuse_qkv();
   void fuse_swiglu();
   void fuse_prologues();
+  void fuse_peer_allreduce();
+  bool ar_fused(int64_t M, int64_t hidden, int cons_block) const;
   int shard_for_tp(std::string* err);
   int infer(std::vector<Slot>& slots, std::string* err) const;
   int launch_steps(const std::vector<Slot>& slots, Program& prog, cudaStream_t st);
@@ -164,6 +172,11 @@ class Plan {
   cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr;
   // host-side constant data used while lowering / fusing (weights before upload)
   std::map<int, std::shared_ptr<Initializer>> pending_consts_;
+  // ONNXRUNTIME_EP_B200_PROFILE: per-step CUDA-event times of eager runs (no graph), printed on
+  // destruction as totals per step name (steps run serialised, so PDL overlap is not included)
+  bool prof_ = false;
+  std::vector<cudaEvent_t> prof_ev_;
+  std::map<std::string, std::pair<int64_t, double>> prof_ms_;
 };
 
 }  // namespace b200ep

@@ -272,6 +272,51 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+enum { kErrArTimeout = 302 };
+
+// Consumer side of the peer-memory all-reduce: wait until every source rank published `epoch`
+// (bounded; a timeout records an error and proceeds), then x chunks are sums of the slots.
+__device__ bool ar_wait(const MnbAr& ar, unsigned epoch, DeviceErrorSlot* err) {
+  bool ok = true;
+  if ((int)threadIdx.x < ar.world) {
+    const unsigned* flag = reinterpret_cast<const unsigned*>(ar.mbox[ar.rank]) + threadIdx.x;
+    uint32_t it = 0;
+    while ((int)(ld_acquire_sys(flag) - epoch) < 0) {
+      if (++it > (1u << 24)) {  // ~1 s of polling: the peer is gone
+        report_device_error(err, kErrArTimeout, (int)threadIdx.x);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return ok;
+}
+
+template <typename T>
+__device__ __forceinline__ void ar_sum8(const MnbAr& ar, unsigned epoch, size_t elem, float (&f)[8]) {
+  const char* base = ar.mbox[ar.rank] + kArFlagsBytes + (size_t)(epoch & 1) * ar.region_bytes + elem * sizeof(T);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = 0.f;
+  for (int src = 0; src < ar.world; ++src) {
+    float v[8];
+    unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(base + (size_t)src * ar.slot_bytes)), v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] += v[i];
+  }
+  // the all-reduced activation is an I/O-dtype tensor
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f<T>(from_f<T>(f[i]));
+}
+
 // Fused producers of the staged activations (consumer threads only; ends before the caller's
 // barrier).  Arithmetic follows the standalone kernels: SiLU(g) * u as in silu_mul_kernel, and the
 // (skip) RMS norm as in rms_norm_kernel — fp32 sum of squares of the (unrounded) row, y =
@@ -279,7 +324,7 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 // CTAs of column 0 (blockIdx.x == 0).  wsum: kNC floats of scratch for the per-warp partials.
 template <typename T>
 __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride, int kpad, int xrows, int m0,
-                               int M, int K, float* wsum) {
+                               int M, int K, float* wsum, DeviceErrorSlot* err) {
   const int tid = threadIdx.x, nthr = kNC * 32;
   const int cpr = kpad / 8;
   // zero row (index xrows) for lanes without a token
@@ -306,6 +351,20 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
   const T* G = static_cast<const T*>(pro.gamma);
   T* R = blockIdx.x == 0 ? static_cast<T*>(pro.residual) : nullptr;
   const bool skip = pro.kind == kProSkipRms;
+  // x comes from the peer mailboxes (tensor-parallel partial sums) instead of X
+  const bool from_ar = skip && pro.ar.world > 0;
+  unsigned epoch = 0;
+  if (from_ar) {
+    epoch = __ldcg(pro.ar.ctrs);
+    ar_wait(pro.ar, epoch, err);
+    consumer_barrier();
+  }
+  auto load_x = [&](int m, int k, float (&t)[8]) {
+    if (from_ar)
+      ar_sum8<T>(pro.ar, epoch, (size_t)m * K + k, t);
+    else
+      unpack8<T>(*reinterpret_cast<const uint4*>(X + (size_t)m * K + k), t);
+  };
   for (int r = 0; r < xrows; ++r) {
     const int m = m0 + r;
     if (m >= M) {
@@ -315,7 +374,7 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
     float ss = 0.f;
     for (int kc = tid; kc * 8 < K; kc += nthr) {
       float t[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(X + (size_t)m * K + kc * 8), t);
+      load_x(m, kc * 8, t);
       if (skip) {
         float sk[8];
         unpack8<T>(*reinterpret_cast<const uint4*>(S + (size_t)m * K + kc * 8), sk);
@@ -338,7 +397,7 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
       float y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       if (k < K) {
         float t[8], gm[8];
-        unpack8<T>(*reinterpret_cast<const uint4*>(X + (size_t)m * K + k), t);
+        load_x(m, k, t);
         if (skip) {
           float sk[8];
           unpack8<T>(*reinterpret_cast<const uint4*>(S + (size_t)m * K + k), sk);
@@ -435,7 +494,7 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
 template <typename T, int BLOCK, int NT, bool PAIR>
 __global__ void __launch_bounds__((kNC + 1) * 32, 2)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
-               int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro,
+               int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int SPB = BLOCK / 16;          // k-steps per block
@@ -500,6 +559,8 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
 
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
   pdl_wait();
+  // tensor-parallel partial output: this launch publishes epoch + 1 (see MnbAr)
+  const unsigned oepoch = oar.world ? __ldcg(oar.ctrs) + 1 : 0;
   if (stage_x) {
     if (pro.kind == kProNone) {
       // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
@@ -522,7 +583,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         }
       }
     } else {
-      stage_prologue<T>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * kNC * NT * 4 * 32 - kNC);
+      stage_prologue<T>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * kNC * NT * 4 * 32 - kNC, err);
     }
     consumer_barrier();
   }
@@ -635,6 +696,33 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     }
   }
   if (flags[0] && threadIdx.x == 0) report_device_error(err, kErrMnbTimeout, blockIdx.x);
+  if (oar.world) {
+    // publish the partial output: the last CTA to finish pushes Y (M x N, complete once every
+    // CTA's writes are visible) into slot `rank` of every rank's mailbox with 16-byte stores,
+    // fences them at system scope, bumps the epoch and releases the flags
+    __threadfence();
+    consumer_barrier();
+    if (threadIdx.x == 0) flags[1] = atomicAdd(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1;
+    consumer_barrier();
+    if (flags[1]) {
+      __threadfence();
+      const size_t bytes = (size_t)M * N * sizeof(T);  // multiple of 16 (N % 8 == 0)
+      const size_t off = kArFlagsBytes + (size_t)(oepoch & 1) * oar.region_bytes + (size_t)oar.rank * oar.slot_bytes;
+      const uint4* src = reinterpret_cast<const uint4*>(Y);
+      for (int d = 0; d < oar.world; ++d) {
+        uint4* dst = reinterpret_cast<uint4*>(oar.mbox[d] + off);
+        for (size_t i = threadIdx.x; i < bytes / 16; i += kNC * 32) dst[i] = __ldcg(src + i);
+      }
+      __threadfence_system();
+      consumer_barrier();
+      if (threadIdx.x == 0) {
+        oar.ctrs[1] = 0;
+        oar.ctrs[0] = oepoch;
+        for (int d = 0; d < oar.world; ++d)
+          st_release_sys(reinterpret_cast<unsigned*>(oar.mbox[d]) + oar.rank, oepoch);
+      }
+    }
+  }
 }
 
 // ---- host side --------------------------------------------------------------------------------
@@ -700,7 +788,8 @@ DeviceErrorSlot* device_error_slot();
 
 namespace {
 template <typename T, int BLOCK, int NT, bool PAIR>
-cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
+cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
+                         const MnbAr& oar) {
   using RC = Rec<BLOCK>;
   // activation rows staged in shared memory when they fit (M = 1: K <= 16K)
   const int rows = (int)std::min<int64_t>(8 * NT, M);
@@ -749,35 +838,39 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   const int64_t ctas = std::min<int64_t>(p.ntiles, (int64_t)per_sm * num_sms());
   return launch_k(kern, dim3((unsigned)ctas, gy), dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                  (int)p.ksteps4, xrows, 0u, stages, pro, device_error_slot());
+                  (int)p.ksteps4, xrows, 0u, stages, pro, oar, device_error_slot());
 }
 
 template <typename T, int BLOCK>
-cudaError_t launch_nt(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
-  if (M == 1) return launch_tma_t<T, BLOCK, 1, false>(A, p, Y, M, st, pro);
-  return M <= 8 ? launch_tma_t<T, BLOCK, 1, true>(A, p, Y, M, st, pro)
-                : launch_tma_t<T, BLOCK, 2, true>(A, p, Y, M, st, pro);
+cudaError_t launch_nt(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
+                      const MnbAr& oar) {
+  if (M == 1) return launch_tma_t<T, BLOCK, 1, false>(A, p, Y, M, st, pro, oar);
+  return M <= 8 ? launch_tma_t<T, BLOCK, 1, true>(A, p, Y, M, st, pro, oar)
+                : launch_tma_t<T, BLOCK, 2, true>(A, p, Y, M, st, pro, oar);
 }
 
 template <typename T>
-cudaError_t launch_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro) {
+cudaError_t launch_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
+                     const MnbAr& oar) {
   switch (p.block) {
-    case 16: return launch_nt<T, 16>(A, p, Y, M, st, pro);
-    case 32: return launch_nt<T, 32>(A, p, Y, M, st, pro);
-    case 64: return launch_nt<T, 64>(A, p, Y, M, st, pro);
-    case 128: return launch_nt<T, 128>(A, p, Y, M, st, pro);
+    case 16: return launch_nt<T, 16>(A, p, Y, M, st, pro, oar);
+    case 32: return launch_nt<T, 32>(A, p, Y, M, st, pro, oar);
+    case 64: return launch_nt<T, 64>(A, p, Y, M, st, pro, oar);
+    case 128: return launch_nt<T, 128>(A, p, Y, M, st, pro, oar);
   }
   return cudaErrorInvalidValue;
 }
 }  // namespace
 
 cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st,
-                              const MnbPro* pro) {
+                              const MnbPro* pro, const MnbAr* out_ar) {
   if (M == 0) return cudaSuccess;
   const MnbPro none{};
+  const MnbAr no_ar{};
   const MnbPro& pr = pro ? *pro : none;
-  if (dtype == kF16) return launch_b<__half>(A, p, Y, M, st, pr);
-  if (dtype == kBF16) return launch_b<__nv_bfloat16>(A, p, Y, M, st, pr);
+  const MnbAr& oa = out_ar ? *out_ar : no_ar;
+  if (dtype == kF16) return launch_b<__half>(A, p, Y, M, st, pr, oa);
+  if (dtype == kBF16) return launch_b<__nv_bfloat16>(A, p, Y, M, st, pr, oa);
   return cudaErrorInvalidValue;
 }
 

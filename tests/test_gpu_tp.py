@@ -1,6 +1,7 @@
-"""Tensor-parallel decoder on 2 GPUs (one process per GPU, NCCL over NVLink): prefill then decode
-steps of a small decoder sharded by KV head / FFN column / vocabulary, checked against the CPU
-oracle run of the unsharded graph.  Skipped with fewer than 2 GPUs."""
+"""Tensor-parallel decoder on 2 GPUs (one process per GPU): prefill then decode steps of a small
+decoder sharded by KV head / FFN column / vocabulary, checked against the CPU oracle run of the
+unsharded graph.  The prefill's 32-row partial sums go through NCCL all-reduces; the decode steps'
+through the peer-memory mailboxes fused into the GEMVs.  Skipped with fewer than 2 GPUs."""
 
 from __future__ import annotations
 
@@ -12,7 +13,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 CFG = dict(layers=2, hidden=256, heads=8, kv_heads=4, head_dim=32, ffn=512, vocab=1000, max_seq=64)
-B, P, CAP, STEPS = 2, 8, 32, 3
+B, P, CAP, STEPS = 2, 16, 32, 3  # prefill: 32 rows (NCCL all-reduce); decode: 2 rows (peer mailboxes)
 
 
 def _gpus():
@@ -55,6 +56,9 @@ def _rank_main(rank, world, port, q):
         dist.broadcast_object_list(obj2, src=0)
         ep_d.set_tensor_parallel(rank, world, obj2[0])
         sess_d = E.Session(build_decoder(cfg, batch=B, seq=1, cap=CAP), ep_d)
+        import json
+
+        desc = json.loads(sess_d.parts[0].describe())
         hk = cfg.kv_heads // world
         kv = [[torch.zeros(B, hk, CAP, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
               for _ in range(cfg.layers)]
@@ -79,7 +83,8 @@ def _rank_main(rank, world, port, q):
             f, o = feeds(ids_all[t + 1], P + t)
             logits.append(sess_d.run(f, o)["logits"].float().cpu().numpy())
         torch.cuda.synchronize()
-        q.put((rank, logits, ids_all, None))
+        q.put((rank, logits, ids_all, None if desc["peer_allreduce"] == 2 * cfg.layers
+               else f"peer_allreduce sites {desc['peer_allreduce']}"))
     except Exception as e:  # noqa: BLE001
         q.put((rank, None, None, repr(e)))
     finally:
