@@ -137,9 +137,11 @@ inline int div_up(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / 
 // scheduled while its predecessor is still running (its CTAs start once the predecessor's CTAs
 // have all executed pdl_trigger or exited).  Every such kernel calls pdl_wait() before it touches
 // memory an earlier kernel of the stream writes (and before it writes anything an earlier kernel
-// reads); the wait returns once the predecessor grid has completed and its writes are visible, so
-// the ordering stays transitive along the chain.  Work on constant data (weight streams) may run
-// before the wait.  Both are no-ops for a kernel launched without the attribute.
+// reads); the wait returns once the predecessor grid has completed and its writes are visible.
+// pdl_trigger() is only executed after the kernel's own pdl_wait(), so when a kernel starts, every
+// kernel before its predecessor has completed: code before the wait may read data written two or
+// more kernels back (weights, a KV cache row of an earlier step) but nothing the predecessor
+// writes.  Both are no-ops for a kernel launched without the attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -24,6 +24,8 @@
 // does not cover (head_size not a multiple of 32, more than 32 query rows per group, unaligned
 // rows): one CTA per query row, keys in shared memory.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "../common.cuh"
 #include "kernels.h"
@@ -617,6 +619,388 @@ __global__ void __launch_bounds__(128) gqa_generic_kernel(GqaKP kp) {
 }
 
 // ---- host side ------------------------------------------------------------------------------
+
+// ---- tensor-core decode kernel ---------------------------------------------------------------
+// gqa_mma_decode_kernel — one query row per sequence (S == 1), G <= 8 query heads per KV head,
+// head_size 64 or 128, fp16 / bf16.  grid (splits, kv_heads, batch) with the splits of one
+// (batch, kv-head) in one thread-block cluster; 4 warps per CTA.
+//   * The keys [lo, past] are cut into 32-key units spread over the splits x 4 warps of the
+//     cluster.  Each warp streams its units through two shared-memory buffers with 16-byte
+//     cp.async copies (rows XOR-swizzled so ldmatrix reads are conflict-free).
+//   * S = Q K^T and O += P V run on mma.sync.m16n8k16 (fp32 accumulate): the G rotated query rows
+//     are the A operand (rows G..15 zero), K and V reach the B operand through ldmatrix /
+//     ldmatrix.trans, and the probabilities go from the score accumulators straight into the A
+//     fragments of P V.  Online softmax in base 2, fp32.
+//   * The warp that owns the newest key (position past) rotates the new k row, writes k and v into
+//     the KV buffer and patches its shared-memory copy of that unit (the copy it streamed may
+//     predate the append).
+//   * Warps merge in shared memory; the CTAs of the cluster merge through distributed shared memory
+//     into the output (no workspace, no second pass).
+constexpr int kMmaWarps = 4;
+constexpr int kUnit = 32;  // keys per unit
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma_f32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value)
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  T a = from_f<T>(lo), b = from_f<T>(hi);
+  uint16_t ua, ub;
+  memcpy(&ua, &a, 2);
+  memcpy(&ub, &b, 2);
+  return (uint32_t)ua | ((uint32_t)ub << 16);
+}
+
+// byte offset of 16-byte chunk `ch` of row `r` in a swizzled [rows][D] tile
+template <int D>
+__device__ __forceinline__ int swz(int r, int ch) {
+  return r * D * 2 + ((ch ^ (r & 7)) << 4);
+}
+
+template <int D>
+struct MmaSmem {
+  static constexpr int kUnitBytes = kUnit * D * 2;            // one K (or V) unit
+  static constexpr int kBufs = 3;                              // units in flight per warp
+  static constexpr int kWarpBytes = kBufs * 2 * kUnitBytes;    // buffers x (K, V)
+  static constexpr int kQStride = D + 8;                      // halves, padded
+  static constexpr int kQ = kMmaWarps * kWarpBytes;           // [16][kQStride] halves
+  static constexpr int kScratch = kQ + 16 * kQStride * 2;     // [kMmaWarps][D] floats
+  static constexpr int kMerge = kScratch + kMmaWarps * D * 4; // [8][D + 2] floats (CTA result)
+  static constexpr int kTotal = kMerge + 8 * (D + 2) * 4;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMmaWarps * 32)
+gqa_mma_decode_kernel(GqaKP kp) {
+  using L = MmaSmem<D>;
+  constexpr int NB = D / 8;   // 8-wide n-blocks of the output
+  constexpr int KS = D / 16;  // k-steps of q.k
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  uint32_t crank, csize;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+
+  // Before the wait: everything that depends only on data written two or more kernels back —
+  // the positions (seqlens), the KV rows of earlier steps and the rotary tables (see pdl_trigger).
+  const int past = past_len(kp, b);
+  const bool ok = range_ok(kp, past);
+  const int nk = ok ? past + 1 : 0;  // keys [lo, nk)
+  const int lo = kp.local_window > 0 ? max(0, past - kp.local_window + 1) : 0;
+  const int units = nk > lo ? (nk - lo + kUnit - 1) / kUnit : 0;
+  const int nw = (int)csize * kMmaWarps, wid = (int)crank * kMmaWarps + warp;
+  const int u0 = (int)((int64_t)units * wid / nw), u1 = (int)((int64_t)units * (wid + 1) / nw);
+  const int64_t head_base = ((int64_t)b * kp.HK + kvh) * kp.cap;
+  T* kvk = static_cast<T*>(kp.kv_k) + head_base * D;
+  T* kvv = static_cast<T*>(kp.kv_v) + head_base * D;
+
+  unsigned char* wbuf = sm + warp * L::kWarpBytes;  // [buf][K | V]
+  auto issue = [&](int u, int buf) {
+    unsigned char* kb = wbuf + buf * 2 * L::kUnitBytes;
+    unsigned char* vb = kb + L::kUnitBytes;
+    const int key0 = lo + u * kUnit;
+    for (int i = lane; i < kUnit * D / 8; i += 32) {
+      const int r = i / (D / 8), ch = i % (D / 8);
+      const bool v = key0 + r < nk;
+      const int64_t row = v ? key0 + r : 0;
+      cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
+      cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+    }
+    cp_async_commit();
+  };
+  for (int k = 0; k < L::kBufs; ++k)
+    if (u0 + k < u1) issue(u0 + k, k);
+  float cs[4] = {0, 0, 0, 0}, sn[4] = {0, 0, 0, 0};  // rotary pairs i = lane + 32 * e of this position
+  if (ok && kp.do_rotary) {
+    const T* cc = static_cast<const T*>(kp.cos_c) + (int64_t)past * kp.half;
+    const T* sc = static_cast<const T*>(kp.sin_c) + (int64_t)past * kp.half;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (lane + 32 * e < kp.half) cs[e] = to_f<T>(cc[lane + 32 * e]), sn[e] = to_f<T>(sc[lane + 32 * e]);
+  }
+  // one head row (fp32 in shared memory) through the optional per-head RMS norm and RoPE, rounded
+  // through T as stored — the arithmetic of rotate_row_warp with the tables preloaded
+  auto rotate = [&](float* row, const void* normw) {
+    if (kp.has_qk_norm) {
+      float ss = 0.f;
+      for (int i = lane; i < D; i += 32) ss = fmaf(row[i], row[i], ss);
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)D + kp.qk_eps);
+      const T* w = static_cast<const T*>(normw);
+      for (int i = lane; i < D; i += 32) row[i] = row[i] * inv * to_f<T>(w[i]);
+      __syncwarp();
+    }
+    if (kp.do_rotary) {
+      float o0[4], o1[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = lane + 32 * e;
+        if (i < kp.half) {
+          const int i0 = kp.interleaved ? 2 * i : i;
+          const int i1 = kp.interleaved ? 2 * i + 1 : i + kp.half;
+          const float a = row[i0], bb = row[i1];
+          o0[e] = a * cs[e] - bb * sn[e];
+          o1[e] = bb * cs[e] + a * sn[e];
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = lane + 32 * e;
+        if (i < kp.half) {
+          row[kp.interleaved ? 2 * i : i] = o0[e];
+          row[kp.interleaved ? 2 * i + 1 : i + kp.half] = o1[e];
+        }
+      }
+      __syncwarp();
+    }
+    for (int i = lane; i < D; i += 32) row[i] = round_through<T>(row[i]);
+    __syncwarp();
+  };
+
+  pdl_wait();  // q / k / v come from the previous kernel
+  pdl_trigger();
+  if (!ok && threadIdx.x == 0 && crank == 0 && kvh == 0) report_device_error(kp.err, kErrGqaRange, b);
+
+  // rotated query rows (rounded through T, as stored) -> Qs rows 0..G-1; rows G..15 zero
+  T* Qs = reinterpret_cast<T*>(sm + L::kQ);
+  float* scratch = reinterpret_cast<float*>(sm + L::kScratch) + warp * D;
+  for (int i = threadIdx.x; i < (16 - kp.G) * L::kQStride; i += kMmaWarps * 32)
+    Qs[kp.G * L::kQStride + i] = from_f<T>(0.f);
+  if (ok) {
+    const T* qin = static_cast<const T*>(kp.q);
+    for (int gq = warp; gq < kp.G; gq += kMmaWarps) {
+      const T* src = qin + (int64_t)b * kp.qstride + (int64_t)(kvh * kp.G + gq) * D;
+      for (int i = lane; i < D; i += 32) scratch[i] = to_f<T>(src[i]);
+      __syncwarp();
+      rotate(scratch, kp.qn);
+      for (int i = lane; i < D; i += 32) Qs[gq * L::kQStride + i] = from_f<T>(scratch[i]);
+      __syncwarp();
+    }
+  }
+  // the owner of the newest key appends it: rotated k and v into the KV buffer (and, below, into
+  // its streamed copy of that unit, which was read before the append)
+  const int u_new = nk > lo ? (nk - 1 - lo) / kUnit : -1;
+  const bool owner = ok && u_new >= u0 && u_new < u1;
+  T knew[D / 32], vnew[D / 32];
+  if (owner) {
+    const T* kin = static_cast<const T*>(kp.k);
+    const T* vin = static_cast<const T*>(kp.v);
+    const int64_t in_off = (int64_t)b * kp.kstride + (int64_t)kvh * D;
+    for (int i = lane; i < D; i += 32) scratch[i] = to_f<T>(kin[in_off + kp.koff + i]);
+    __syncwarp();
+    rotate(scratch, kp.kn);
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) {
+      const int i = lane + 32 * e;
+      knew[e] = from_f<T>(scratch[i]);
+      vnew[e] = vin[in_off + kp.voff + i];
+      kvk[(int64_t)past * D + i] = knew[e];
+      kvv[(int64_t)past * D + i] = vnew[e];
+    }
+  }
+  __syncthreads();
+
+  // Q as A fragments, one per k-step
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const int row = (lane & 7) + ((lane >> 3) & 1) * 8, col = kk * 16 + (lane >> 4) * 8;
+    ldsm_x4(qa[kk], Qs + row * L::kQStride + col);
+  }
+
+  float m_run = -INFINITY, l_run = 0.f;  // row g (lanes with g < G hold real rows)
+  float o[NB][4];
+#pragma unroll
+  for (int n = 0; n < NB; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  const T* bias = static_cast<const T*>(kp.bias);
+  const int64_t bias_row = kp.bias_batch > 0 ? (int64_t)(kp.bias_batch == 1 ? 0 : b) * kp.bias_total : 0;
+
+  for (int u = u0; u < u1; ++u) {
+    const int buf = (u - u0) % L::kBufs;
+    if (u + 2 < u1) cp_async_wait<2>();
+    else if (u + 1 < u1) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncwarp();
+    unsigned char* kb = wbuf + buf * 2 * L::kUnitBytes;
+    unsigned char* vb = kb + L::kUnitBytes;
+    const int key0 = lo + u * kUnit;
+    if (owner && u == u_new) {
+      const int r = nk - 1 - key0;
+#pragma unroll
+      for (int e = 0; e < D / 32; ++e) {
+        const int i = lane + 32 * e;
+        *reinterpret_cast<T*>(kb + swz<D>(r, i >> 3) + (i & 7) * 2) = knew[e];
+        *reinterpret_cast<T*>(vb + swz<D>(r, i >> 3) + (i & 7) * 2) = vnew[e];
+      }
+      __syncwarp();
+    }
+    // S = Q K^T for the unit's 32 keys: 4 n-blocks of 8 keys
+    float sacc[4][4];
+#pragma unroll
+    for (int nb = 0; nb < 4; ++nb) {
+      sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KS; kk += 2) {
+        uint32_t bfr[4];
+        ldsm_x4(bfr, kb + swz<D>(nb * 8 + (lane & 7), kk * 2 + (lane >> 3)));
+        mma_f32<T>(sacc[nb], qa[kk], bfr[0], bfr[1]);
+        mma_f32<T>(sacc[nb], qa[kk + 1], bfr[2], bfr[3]);
+      }
+    }
+    // scores of row g for keys key0 + nb*8 + 2c (+1); online softmax in base 2
+    float sc[4][2], mx = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 4; ++nb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = key0 + nb * 8 + 2 * c + h;
+        float v = sacc[nb][h] * kp.scale_log2;
+        if (bias && j < kp.bias_total) v += to_f<T>(bias[bias_row + j]) * kLog2e;
+        v = j < nk ? v : -INFINITY;
+        sc[nb][h] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+    float ps = 0.f;
+    uint32_t pa[2][4];  // P as A fragments for the two 16-key k-steps (rows g+8 zero)
+#pragma unroll
+    for (int nb = 0; nb < 4; ++nb) {
+      const float p0 = sc[nb][0] == -INFINITY ? 0.f : exp2f(sc[nb][0] - m_new);
+      const float p1 = sc[nb][1] == -INFINITY ? 0.f : exp2f(sc[nb][1] - m_new);
+      ps += p0 + p1;
+      pa[nb >> 1][(nb & 1) * 2] = pack2<T>(p0, p1);
+      pa[nb >> 1][(nb & 1) * 2 + 1] = 0u;
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l_run = l_run * corr + ps;
+    m_run = m_new;
+    if (!__all_sync(0xffffffffu, corr == 1.f)) {
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        o[n][0] *= corr;
+        o[n][1] *= corr;
+      }
+    }
+    // O += P V
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int n = 0; n < NB; n += 2) {
+        uint32_t bfr[4];
+        const int r = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldsm_x4_t(bfr, vb + swz<D>(r, n + (lane >> 4)));
+        mma_f32<T>(o[n], pa[ks], bfr[0], bfr[1]);
+        mma_f32<T>(o[n + 1], pa[ks], bfr[2], bfr[3]);
+      }
+    __syncwarp();
+    if (u + L::kBufs < u1) issue(u + L::kBufs, buf);
+  }
+
+  // merge the warps: per-warp (m, l, O) rows into shared memory (reusing the stream buffers)
+  __syncthreads();
+  float* wst = reinterpret_cast<float*>(sm);  // [kMmaWarps][8][D + 2]
+  if (g < kp.G) {
+    float* row = wst + ((size_t)warp * 8 + g) * (D + 2);
+#pragma unroll
+    for (int n = 0; n < NB; ++n) {
+      row[n * 8 + 2 * c] = o[n][0];
+      row[n * 8 + 2 * c + 1] = o[n][1];
+    }
+    if (c == 0) {
+      row[D] = m_run;
+      row[D + 1] = l_run;
+    }
+  }
+  __syncthreads();
+  float* res = reinterpret_cast<float*>(sm + L::kMerge);  // [8][D + 2]: this CTA's (O, m, l)
+  for (int i = threadIdx.x; i < kp.G * (D + 2); i += kMmaWarps * 32) {
+    const int gq = i / (D + 2), d = i - gq * (D + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, wst[((size_t)w * 8 + gq) * (D + 2) + D]);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMmaWarps; ++w) {
+      const float* row = wst + ((size_t)w * 8 + gq) * (D + 2);
+      const float f = row[D] == -INFINITY ? 0.f : exp2f(row[D] - M);
+      acc += (d < D ? row[d] : row[D + 1]) * f;
+    }
+    res[i] = d == D ? M : acc;  // O (unnormalised), m, l
+  }
+  // merge the cluster's CTAs through distributed shared memory: rank r writes outputs
+  // [r * per, (r + 1) * per) of the G x D head rows, reading every rank's (O, m, l) for them
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (ok) {
+    T* out = static_cast<T*>(kp.out) + (int64_t)b * kp.H * D + (int64_t)kvh * kp.G * D;
+    const uint32_t local = smem_addr(res);
+    const int total = kp.G * D, per = (total + (int)csize - 1) / (int)csize;
+    for (int i = (int)crank * per + threadIdx.x; i < min(total, ((int)crank + 1) * per); i += kMmaWarps * 32) {
+      const int gq = i / D, d = i - gq * D;
+      const uint32_t row = local + (uint32_t)(gq * (D + 2) * 4);
+      float m[8], l[8], ov[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        m[r] = -INFINITY, l[r] = 0.f, ov[r] = 0.f;
+        if (r < (int)csize) {
+          uint32_t ra;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(row), "r"(r));
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ov[r]) : "r"(ra + (uint32_t)(d * 4)));
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(m[r]) : "r"(ra + (uint32_t)(D * 4)));
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(l[r]) : "r"(ra + (uint32_t)((D + 1) * 4)));
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) M = fmaxf(M, m[r]);
+      float num = 0.f, den = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float f = m[r] == -INFINITY ? 0.f : exp2f(m[r] - M);
+        num += ov[r] * f;
+        den += l[r] * f;
+      }
+      out[(int64_t)gq * D + d] = from_f<T>(den > 0.f ? num / den : 0.f);
+    }
+  }
+  // keep every CTA's shared memory alive until all ranks have read it
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 namespace {
 
 int pow2_at_least(int x) {
@@ -717,6 +1101,47 @@ cudaError_t launch_generic(const GqaKP& kp, cudaStream_t st) {
   return launch_k(kern, dim3(kp.B * kp.S * kp.H), dim3(128), smem, st, kp);
 }
 
+
+bool mma_decode_path(const b200ep_gqa_params& p, int dtype) {
+  const int G = (int)(p.num_heads / p.kv_heads);
+  return p.seq == 1 && (dtype == kF16 || dtype == kBF16) && (p.head_size == 64 || p.head_size == 128) &&
+         G >= 1 && G <= 8 && !getenv("ONNXRUNTIME_EP_B200_GQA_SIMT");
+}
+
+// splits of one (batch, kv-head) = cluster size: enough 32-key units per warp at full capacity
+int mma_splits(const b200ep_gqa_params& p) {
+  const int64_t units = (p.cap + kUnit - 1) / kUnit;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(8, (units + 2 * kMmaWarps - 1) / (2 * kMmaWarps)));
+}
+
+template <typename T, int D>
+cudaError_t launch_mma_decode(const GqaKP& kp, int splits, cudaStream_t st) {
+  using L = MmaSmem<D>;
+  auto kern = gqa_mma_decode_kernel<T, D>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(splits, kp.HK, kp.B);
+  cfg.blockDim = dim3(kMmaWarps * 32);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, kp);
+}
 }  // namespace
 
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
@@ -792,7 +1217,14 @@ int launch_gqa(const GqaArgs& a, cudaStream_t st) {
   const bool aligned = (reinterpret_cast<uintptr_t>(a.kv_key) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(a.kv_value) % 16 == 0);
   cudaError_t e;
-  if (decode_path(p, esz) && aligned) {
+  if (mma_decode_path(p, a.dtype) && aligned) {
+    const int sp = mma_splits(p);
+    if (a.dtype == kF16)
+      e = p.head_size == 64 ? launch_mma_decode<__half, 64>(kp, sp, st) : launch_mma_decode<__half, 128>(kp, sp, st);
+    else
+      e = p.head_size == 64 ? launch_mma_decode<__nv_bfloat16, 64>(kp, sp, st)
+                            : launch_mma_decode<__nv_bfloat16, 128>(kp, sp, st);
+  } else if (decode_path(p, esz) && aligned) {
     switch (a.dtype) {
       case kF32: e = launch_decode<float>(kp, st); break;
       case kF16: e = launch_decode<__half>(kp, st); break;

@@ -531,9 +531,8 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     fence_mbarrier_init();
   }
   __syncthreads();
-  // the next kernel of the stream may be scheduled now; the weight stream reads constants only, the
-  // consumers wait for the previous kernel before they read activations or write outputs
-  pdl_trigger();
+  // the weight stream reads constants only and starts at once; the consumers wait for the previous
+  // kernel before they read activations or write outputs
   if (warp == kNC) {
     if (lane == 0) {
       // the CTA's records in stages of at most kG that never cross a tile boundary
@@ -559,6 +558,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
 
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
   pdl_wait();
+  pdl_trigger();
   // tensor-parallel partial output: this launch publishes epoch + 1 (see MnbAr)
   const unsigned oepoch = oar.world ? __ldcg(oar.ctrs) + 1 : 0;
   if (stage_x) {
