@@ -200,6 +200,24 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
   }
 }
 
+// d = a . b with a zero accumulator (the first k-step of a quantisation block)
+template <typename T>
+__device__ __forceinline__ void mma16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+  } else {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+  }
+}
+
 __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
   if (bf) return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
   __half2 h = *reinterpret_cast<__half2*>(&v);
@@ -371,6 +389,46 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
       for (int kc = tid; kc < cpr; kc += nthr) xs_put(xs + (size_t)r * xstride, kc * 8, make_uint4(0, 0, 0, 0));
       continue;
     }
+    constexpr int kCh = 2;  // chunks of 8 a thread keeps in registers: one pass over x when kpad fits
+    if (kpad <= kCh * 8 * nthr) {
+      float t[kCh][8], gm[kCh][8], ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kCh; ++j) {
+        const int k = (tid + j * nthr) * 8;
+        if (k < K) {
+          load_x(m, k, t[j]);
+          unpack8<T>(*reinterpret_cast<const uint4*>(G + k), gm[j]);
+          if (skip) {
+            float sk[8];
+            unpack8<T>(*reinterpret_cast<const uint4*>(S + (size_t)m * K + k), sk);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[j][i] += sk[i];
+            if (R) *reinterpret_cast<uint4*>(R + (size_t)m * K + k) = pack8<T>(t[j]);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss = fmaf(t[j][i], t[j][i], ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if ((tid & 31) == 0) wsum[tid >> 5] = ss;
+      consumer_barrier();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kNC; ++w) tot += wsum[w];
+      const float inv = rsqrtf(tot / (float)K + pro.eps);
+#pragma unroll
+      for (int j = 0; j < kCh; ++j) {
+        const int k = (tid + j * nthr) * 8;
+        if (k < kpad) {
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = k < K ? t[j][i] * inv * gm[j][i] : 0.f;
+          xs_put(xs + (size_t)r * xstride, k, pack8<T>(y));
+        }
+      }
+      consumer_barrier();  // wsum is reused by the next row
+      continue;
+    }
     float ss = 0.f;
     for (int kc = tid; kc * 8 < K; kc += nthr) {
       float t[8];
@@ -473,8 +531,10 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
       Dq<T>::run(words[j], bias_lo, bias_hi, kq, a);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        if (block_start) cb[nt][0] = cb[nt][1] = cb[nt][2] = cb[nt][3] = 0.f;
-        mma16816<T>(cb[nt], a, b[nt][2 * j], b[nt][2 * j + 1]);
+        if (block_start)
+          mma16816_z<T>(cb[nt], a, b[nt][2 * j], b[nt][2 * j + 1]);
+        else
+          mma16816<T>(cb[nt], a, b[nt][2 * j], b[nt][2 * j + 1]);
       }
       if (block_end) {
 #pragma unroll
