@@ -280,6 +280,55 @@ def dominant_kernel_roofline(batch, peaks, peak_kind, reps=10):
             "algorithmic_bytes_per_launch": alg, "launch_us": round(launch_s * 1e6, 2), "traffic": traffic}
 
 
+def gqa_kernel_timing(batch, ctx, peaks, peak_kind, reps=5):
+    """GroupQueryAttention decode alone (32 q / 8 kv heads, head 128, fp16, shared KV buffer of
+    capacity ctx + 16 holding ctx valid rows): CUDA-event timing over rotating KV buffers larger than
+    L2, replayed from a CUDA graph.  Algorithmic bytes: the K and V rows read plus q / k / v / out."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    H, HK, D = 32, 8, 128
+    cap = ctx + 16
+    per = 2 * batch * HK * cap * D * 2
+    copies = max(2, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kvs = [(torch.randn(batch, HK, cap, D, device="cuda", generator=g).half(),
+            torch.randn(batch, HK, cap, D, device="cuda", generator=g).half()) for _ in range(copies)]
+    q = torch.randn(batch, 1, H * D, device="cuda", generator=g).half()
+    k = torch.randn(batch, 1, HK * D, device="cuda", generator=g).half()
+    v = torch.randn(batch, 1, HK * D, device="cuda", generator=g).half()
+    seq = torch.full((batch,), ctx - 1, dtype=torch.int32, device="cuda")
+    ang = torch.arange(cap + 8, device="cuda", dtype=torch.float64)[:, None] / (
+        10000.0 ** (torch.arange(D // 2, device="cuda", dtype=torch.float64) / (D // 2)))[None, :]
+    cos, sin = ang.cos().half(), ang.sin().half()
+    out = torch.empty(batch, 1, H * D, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            ops.group_query_attention(q, k, v, kvs[i][0], kvs[i][1], seq, cos, sin, num_heads=H, kv_heads=HK, out=out)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                ops.group_query_attention(q, k, v, kvs[i][0], kvs[i][1], seq, cos, sin, num_heads=H, kv_heads=HK,
+                                          out=out)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    alg = 2 * batch * HK * ctx * D * 2 + (q.numel() + k.numel() + v.numel() + out.numel()) * 2
+    peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
+    return {"kernel": "gqa_mma_decode_kernel", "batch": batch, "context": ctx, "launch_us": round(launch_s * 1e6, 2),
+            "algorithmic_bytes_per_launch": alg, "achieved": round(alg / launch_s / 1e9, 1), "unit": "GB/s",
+            "frac": round(alg / launch_s / 1e9 / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -507,8 +556,9 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--kernel-only", action="store_true",
-                    help="time only the dominant kernel (the roofline leg); used for ncu captures")
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa"],
+                    help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
+                         "context 1024 and 8192); used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -528,7 +578,11 @@ def main():
         load_library()
         torch.cuda.set_device(0)
         peaks, peak_kind = measured_peaks()
-        print(json.dumps(dominant_kernel_roofline(args.batch, peaks, peak_kind, reps=2)), flush=True)
+        if args.kernel_only == "gqa":
+            for b, ctx in ((1, 1024), (1, 8192), (8, 8192)):
+                print(json.dumps(gqa_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
+        else:
+            print(json.dumps(dominant_kernel_roofline(args.batch, peaks, peak_kind, reps=2)), flush=True)
         return
 
     rank, world, local = dist_setup(args.gpus)

@@ -1108,10 +1108,11 @@ bool mma_decode_path(const b200ep_gqa_params& p, int dtype) {
          G >= 1 && G <= 8 && !getenv("ONNXRUNTIME_EP_B200_GQA_SIMT");
 }
 
-// splits of one (batch, kv-head) = cluster size: enough 32-key units per warp at full capacity
+// splits of one (batch, kv-head) = cluster size (at most 8, the portable limit): one 32-key unit
+// per warp at full capacity where that fits — decode attention is latency-bound at short contexts
 int mma_splits(const b200ep_gqa_params& p) {
   const int64_t units = (p.cap + kUnit - 1) / kUnit;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(8, (units + 2 * kMmaWarps - 1) / (2 * kMmaWarps)));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(8, (units + kMmaWarps - 1) / kMmaWarps));
 }
 
 template <typename T, int D>
