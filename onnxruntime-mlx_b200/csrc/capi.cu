@@ -196,6 +196,10 @@ B200EP_API int b200ep_matmulnbits_prepacked(const void* A, const void* packed, v
   B200EP_CHECK_ARG(reinterpret_cast<uintptr_t>(packed) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 4 == 0,
                    "MatMulNBits prepacked: packed weights must be 16-byte and A 4-byte aligned");
   p.w = const_cast<void*>(packed);
+  // many rows: the tcgen05 GEMM; decode-sized rows: the streaming GEMV
+  if (mnb_gemm_supported(M, K, A))
+    return cuda_status(launch_mnb_gemm(A, p, Y, dtype, M, static_cast<cudaStream_t>(stream)),
+                       "MatMulNBits prepacked GEMM launch");
   return cuda_status(launch_mnb_packed(A, p, Y, dtype, M, static_cast<cudaStream_t>(stream)),
                      "MatMulNBits prepacked launch");
   B200EP_GUARD_END

@@ -1018,7 +1018,10 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
             }
             if (e != cudaSuccess) break;
           }
-          e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st, nullptr, out_ar);
+          if (!out_ar && mnb_gemm_supported(M, s.K, a.ptr))
+            e = launch_mnb_gemm(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st);  // prefill rows
+          else
+            e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st, nullptr, out_ar);
           break;
         }
         MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,

@@ -63,4 +63,8 @@ cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dt
 // Whether a prologue can run fused for M rows of K activations (they must fit the staging area).
 bool mnb_prologue_fits(int64_t M, int64_t K, int block);
 
+// Many rows (prefill): tcgen05 / TMEM GEMM over the same prepacked records (mnb_gemm.cu).
+bool mnb_gemm_supported(int64_t M, int64_t K, const void* A);
+cudaError_t launch_mnb_gemm(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st);
+
 }  // namespace b200ep
