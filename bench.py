@@ -43,6 +43,7 @@ sys.path.insert(0, ROOT)
 PROMPT = 1024
 GEN = 256
 HBM_FALLBACK = 6553.0
+TENSOR_FALLBACK = 1590.0
 
 
 def measured_peaks():
@@ -329,6 +330,60 @@ def gqa_kernel_timing(batch, ctx, peaks, peak_kind, reps=5):
             "frac": round(alg / launch_s / 1e9 / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
 
 
+GEMM_SHAPES = (("gate/up", 512, 4096, 28672), ("q/k/v", 512, 4096, 6144), ("o_proj", 512, 4096, 4096),
+               ("down", 512, 14336, 4096), ("gate/up", 2048, 4096, 28672))
+
+
+def gemm_kernel_timing(name, M, K, N, peaks, peak_kind, reps=5):
+    """Prefill MatMulNBits alone (the tcgen05 GEMM: int4 block 32, fp16 scales + uint8 zero points,
+    fp16 activations) at a Llama-3-8B prefill shape: CUDA-event timing over rotating weight copies
+    larger than L2, replayed from a CUDA graph.  Algorithmic work: 2 M N K flops (the hi / lo weight
+    split that keeps the dequantised weights exact doubles the tensor-core work actually issued)."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    block = 32
+    nb = K // block
+    per = N * nb * block // 2 + N * nb * 2 + N * nb // 2
+    copies = max(2, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    packs = []
+    for _ in range(copies):
+        Bq = torch.randint(0, 256, (N, nb, block // 2), dtype=torch.uint8, device="cuda", generator=g)
+        S = (torch.rand(N * nb, device="cuda", generator=g) * 0.01 + 0.001).half()
+        Z = torch.randint(0, 256, (N * nb // 2,), dtype=torch.uint8, device="cuda", generator=g)
+        packs.append(ops.matmulnbits_prepack(Bq, S, Z, K=K, N=N, block_size=block))
+        del Bq, S, Z
+    a = torch.randn(M, K, device="cuda", generator=g).half()
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    flops = 2 * M * N * K
+    peak = float(peaks.get("bf16_tflops", TENSOR_FALLBACK))
+    tf = flops / launch_s / 1e12
+    return {"kernel": "mnb_gemm_kernel", "proj": name, "M": M, "K": K, "N": N, "launch_us": round(launch_s * 1e6, 2),
+            "bound": "tensor", "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak,
+            "frac": round(tf / peak, 4), "issued_frac": round(2 * tf / peak, 4),
+            "peak_source": f"{peak_kind} bf16_tflops (burst)"}
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -556,9 +611,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa"],
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm"],
                     help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
-                         "context 1024 and 8192); used for ncu captures")
+                         "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes); "
+                         "used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -581,6 +637,9 @@ def main():
         if args.kernel_only == "gqa":
             for b, ctx in ((1, 1024), (1, 8192), (8, 8192)):
                 print(json.dumps(gqa_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
+        elif args.kernel_only == "gemm":
+            for name, m, k, n in GEMM_SHAPES:
+                print(json.dumps(gemm_kernel_timing(name, m, k, n, peaks, peak_kind)), flush=True)
         else:
             print(json.dumps(dominant_kernel_roofline(args.batch, peaks, peak_kind, reps=2)), flush=True)
         return

@@ -2,9 +2,10 @@
 // the accumulator in tensor memory (reference: the fp16 prefill GEMM of quant.rs:540-601 and the
 // quantised matmul of matmulnbits_op, quant.rs:986-1130).
 //
-// One CTA computes a 128 x 128 tile of Y = A . W^T, looping over K in 64-wide stages:
-//   warp 0 (one lane)  TMA: the A tile [128 rows x 64 k] through a 2-D tensor map with 128-byte
-//                      swizzle into a ring of 3 stages;
+// One CTA computes a (128 or 256) x 128 tile of Y = A . W^T, looping over K in 64-wide stages:
+//   warp 0 (one lane)  TMA: the A tile(s) [128 rows x 64 k] through a 2-D tensor map with 128-byte
+//                      swizzle into a ring of 3 stages (two row sub-tiles share each B tile when
+//                      M > 128, halving the dequantisation per flop);
 //   warp 2 (one lane)  the eight 16-row int4 group records of the W tile for each stage (1-D bulk
 //                      copies from the prepacked stream) into a separate, deeper ring of 8, so the
 //                      HBM latency of the weights is hidden behind several stages of work;
@@ -21,6 +22,7 @@
 // CTAs along x cover the M tiles of one W tile, so the W tile is read from HBM once and the other
 // M tiles find it in L2.  Every mbarrier wait is bounded (timeout -> device error word).
 #include <cuda.h>
+#include <cstdlib>
 
 #include <algorithm>
 
@@ -35,7 +37,6 @@ DeviceErrorSlot* device_error_slot();
 namespace {
 
 constexpr int kGStages = 3;   // A / B tile ring
-constexpr int kRStages = 8;   // weight-record ring
 constexpr int kTM = 128, kTN = 128, kTK = 64;
 constexpr int kDeq = 8;       // dequantising (and epilogue) warps: 3 .. 3 + kDeq - 1
 constexpr int kGThreads = (3 + kDeq) * 32;
@@ -49,14 +50,17 @@ struct GRec {  // the record geometry of mnb_mma.cu (kept in sync by mnb_record_
   static constexpr int kBytes = 512 + ((kSlots * 40 + 15) / 16) * 16;
 };
 
-struct GemmSmem {
-  static constexpr int kA = 0;                                  // [stages][128 x 64] (16 KB each)
-  static constexpr int kB = kA + kGStages * kTM * kTK * 2;     // [stages][hi, lo][128 x 64]
+template <int MSUB>
+struct GemmSmem {  // MSUB 128-row sub-tiles of A share every dequantised B tile
+  static constexpr int kRS = MSUB == 1 ? 8 : 4;                // weight-record ring depth
+  static constexpr int kATile = kTM * kTK * 2;                 // 16 KB
+  static constexpr int kA = 0;                                  // [stages][MSUB][128 x 64]
+  static constexpr int kB = kA + kGStages * MSUB * kATile;     // [stages][hi, lo][128 x 64]
   static constexpr int kBTile = kTN * kTK * 2;
   static constexpr int kRec = kB + kGStages * 2 * kBTile;      // [record stages][8 records]
   static constexpr int kRecStage = 8 * 704;                     // largest record (block 16) x 8
-  static constexpr int kBar = kRec + kRStages * kRecStage;      // full, bready, empty, rfull, rempty, acc
-  static constexpr int kTmemSlot = kBar + (3 * kGStages + 2 * kRStages + 1) * 8;
+  static constexpr int kBar = kRec + kRS * kRecStage;           // full, bready, empty, rfull, rempty, acc
+  static constexpr int kTmemSlot = kBar + (3 * kGStages + 2 * kRS + 1) * 8;
   static constexpr int kTotal = kTmemSlot + 16 + 1024;          // + alignment slack
 };
 
@@ -143,11 +147,13 @@ __device__ __forceinline__ uint32_t sw128(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
 }
 
-template <typename T, int BLOCK>
+template <typename T, int BLOCK, int MSUB>
 __global__ void __launch_bounds__(kGThreads, 1)
 mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restrict__ recs, T* __restrict__ Y,
                 int M, int N, int ntiles, int ksteps4, DeviceErrorSlot* err) {
   using RC = GRec<BLOCK>;
+  using GemmSmem = b200ep::GemmSmem<MSUB>;
+  constexpr int kRStages = GemmSmem::kRS;
   constexpr int SPB = BLOCK / 16;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -161,7 +167,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
   int* flag = reinterpret_cast<int*>(sm + GemmSmem::kTmemSlot + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTM, n0 = blockIdx.y * kTN;
+  const int m0 = blockIdx.x * kTM * MSUB, n0 = blockIdx.y * kTN;
   const int tile0 = n0 / 16;
   const int nst = ksteps4;  // stages: one 64-k group each
 
@@ -181,7 +187,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTN));
+                 "r"(kTN * MSUB));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -199,8 +205,9 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
           *flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(kTM * kTK * 2));
-        tma_load_2d(sm + GemmSmem::kA + s * kTM * kTK * 2, &amap, i * kTK, m0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(MSUB * GemmSmem::kATile));
+        for (int u = 0; u < MSUB; ++u)
+          tma_load_2d(sm + GemmSmem::kA + (s * MSUB + u) * GemmSmem::kATile, &amap, i * kTK, m0 + u * kTM, &full[s]);
       }
     }
   } else if (warp == 2) {
@@ -232,21 +239,24 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(sm + GemmSmem::kA + s * kTM * kTK * 2);
+        const uint32_t a0 = smem_u32(sm + GemmSmem::kA + s * MSUB * GemmSmem::kATile);
         const uint32_t b0 = smem_u32(sm + GemmSmem::kB + s * 2 * GemmSmem::kBTile);
 #pragma unroll
-        for (int kk = 0; kk < kTK / 16; ++kk) {
+        for (int kk = 0; kk < kTK / 16; ++kk)
 #pragma unroll
-          for (int part = 0; part < 2; ++part) {  // B.hi then B.lo
-            const uint64_t ad = umma_desc(a0 + kk * 32), bd = umma_desc(b0 + part * GemmSmem::kBTile + kk * 32);
-            const uint32_t acc = (i > 0 || kk > 0 || part > 0) ? 1u : 0u;
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem),
-                "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u)
-                : "memory");
-          }
-        }
+          for (int u = 0; u < MSUB; ++u)  // row sub-tile u accumulates in TMEM columns [u * 128, u * 128 + 128)
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {  // B.hi then B.lo
+              const uint64_t ad = umma_desc(a0 + u * GemmSmem::kATile + kk * 32);
+              const uint64_t bd = umma_desc(b0 + part * GemmSmem::kBTile + kk * 32);
+              const uint32_t acc = (i > 0 || kk > 0 || part > 0) ? 1u : 0u;
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
+                      tmem + (uint32_t)(u * kTN)),
+                  "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u)
+                  : "memory");
+            }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&empty[s]))
                      : "memory");
@@ -315,13 +325,16 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
     // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (rows of the tile)
     if (!mbar_wait(accbar, 0)) *flag = 1;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    // warp w reads TMEM lanes 32 * (w % 4) .. + 31; the kDeq / 4 warps of a lane quarter split the columns
+    // warp w reads TMEM lanes 32 * (w % 4) .. + 31; the kDeq / 4 warps of a lane quarter split the
+    // (MSUB sub-tiles x 128) accumulator columns
     const int q = warp & 3, part = dw / 4, nparts = kDeq / 4;
-    const int row = m0 + q * 32 + lane;
+    constexpr int kCols = kTN * MSUB;
 #pragma unroll 1
-    for (int cc = part * (kTN / nparts); cc < (part + 1) * (kTN / nparts); cc += 32) {
+    for (int ca = part * (kCols / nparts); ca < (part + 1) * (kCols / nparts); ca += 32) {
+      const int u = ca / kTN, cc = ca % kTN;
+      const int row = m0 + u * kTM + q * 32 + lane;
       uint32_t v[32];
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)ca;
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
           "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -345,7 +358,9 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
             *reinterpret_cast<uint4*>(yr + e) = pk;
           }
         } else {
-          for (int e = 0; e < ncol; ++e) yr[e] = from_f<T>(__uint_as_float(v[e]));
+#pragma unroll
+          for (int e = 0; e < 32; ++e)  // constant indices keep v[] in registers
+            if (e < ncol) yr[e] = from_f<T>(__uint_as_float(v[e]));
         }
       }
     }
@@ -354,7 +369,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN * MSUB));
   }
   if (*flag && threadIdx.x == 0) report_device_error(err, kErrGemmTimeout, blockIdx.x);
 }
@@ -375,7 +390,7 @@ EncodeTiled encode_fn() {
   return fn;
 }
 
-template <typename T, int BLOCK>
+template <typename T, int BLOCK, int MSUB>
 cudaError_t gemm_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
   EncodeTiled enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
@@ -390,26 +405,46 @@ cudaError_t gemm_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaSt
           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  auto kern = mnb_gemm_kernel<T, BLOCK>;
+  auto kern = mnb_gemm_kernel<T, BLOCK, MSUB>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem::kTotal);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<MSUB>::kTotal);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((unsigned)((M + kTM - 1) / kTM), (unsigned)((p.N + kTN - 1) / kTN));
-  return launch_k(kern, grid, dim3(kGThreads), (size_t)GemmSmem::kTotal, st, map,
+  dim3 grid((unsigned)((M + kTM * MSUB - 1) / (kTM * MSUB)), (unsigned)((p.N + kTN - 1) / kTN));
+  return launch_k(kern, grid, dim3(kGThreads), (size_t)GemmSmem<MSUB>::kTotal, st, map,
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.ntiles,
                   (int)p.ksteps4, device_error_slot());
+}
+
+// 256-row CTAs dequantise each weight tile once for twice the MMAs but halve the CTA count.  A
+// 256-row CTA takes ~1.35x the time of a 128-row one (measured on B200 over prefill shapes), so
+// compare whole waves of 148 CTAs at those costs.  ONNXRUNTIME_EP_B200_GEMM_MSUB=1|2 forces one.
+int gemm_msub(int64_t M, int64_t N) {
+  static const int forced = [] {
+    const char* e = std::getenv("ONNXRUNTIME_EP_B200_GEMM_MSUB");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == 1 || forced == 2) return forced;
+  if (M <= kTM) return 1;
+  const int64_t ntn = (N + kTN - 1) / kTN;
+  const int64_t w1 = ((M + kTM - 1) / kTM * ntn + 147) / 148, w2 = ((M + 2 * kTM - 1) / (2 * kTM) * ntn + 147) / 148;
+  return w2 * 135 <= w1 * 100 ? 2 : 1;
+}
+
+template <typename T, int BLOCK>
+cudaError_t gemm_m(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
+  return gemm_msub(M, p.N) == 2 ? gemm_t<T, BLOCK, 2>(A, p, Y, M, st) : gemm_t<T, BLOCK, 1>(A, p, Y, M, st);
 }
 
 template <typename T>
 cudaError_t gemm_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
   switch (p.block) {
-    case 16: return gemm_t<T, 16>(A, p, Y, M, st);
-    case 32: return gemm_t<T, 32>(A, p, Y, M, st);
-    case 64: return gemm_t<T, 64>(A, p, Y, M, st);
-    case 128: return gemm_t<T, 128>(A, p, Y, M, st);
+    case 16: return gemm_m<T, 16>(A, p, Y, M, st);
+    case 32: return gemm_m<T, 32>(A, p, Y, M, st);
+    case 64: return gemm_m<T, 64>(A, p, Y, M, st);
+    case 128: return gemm_m<T, 128>(A, p, Y, M, st);
   }
   return cudaErrorInvalidValue;
 }
