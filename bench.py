@@ -330,6 +330,50 @@ def gqa_kernel_timing(batch, ctx, peaks, peak_kind, reps=5):
             "frac": round(alg / launch_s / 1e9 / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
 
 
+def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
+    """GroupQueryAttention over a whole prompt (32 q / 8 kv heads, head 128, fp16, past 0): the
+    rotate-and-append kernel plus the tensor-core prefill kernel, CUDA-event timed over graph
+    replays.  Algorithmic work: causal q.k and p.v, 4 * H * D * S * (S + 1) / 2 flops."""
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    H, HK, D = 32, 8, 128
+    cap = S + 16
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kc = torch.zeros(1, HK, cap, D, device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    q = torch.randn(1, S, H * D, device="cuda", generator=g).half()
+    k = torch.randn(1, S, HK * D, device="cuda", generator=g).half()
+    v = torch.randn(1, S, HK * D, device="cuda", generator=g).half()
+    seq = torch.full((1,), S - 1, dtype=torch.int32, device="cuda")
+    ang = torch.arange(cap + 8, device="cuda", dtype=torch.float64)[:, None] / (
+        10000.0 ** (torch.arange(D // 2, device="cuda", dtype=torch.float64) / (D // 2)))[None, :]
+    cos, sin = ang.cos().half(), ang.sin().half()
+    out = torch.empty(1, S, H * D, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        ops.group_query_attention(q, k, v, kc, vc, seq, cos, sin, num_heads=H, kv_heads=HK, out=out)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            ops.group_query_attention(q, k, v, kc, vc, seq, cos, sin, num_heads=H, kv_heads=HK, out=out)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / reps
+    flops = 4 * H * D * S * (S + 1) / 2
+    peak = float(peaks.get("bf16_tflops", TENSOR_FALLBACK))
+    tf = flops / launch_s / 1e12
+    return {"kernel": "gqa_append_kernel + gqa_mma_prefill_kernel", "S": S, "launch_us": round(launch_s * 1e6, 2),
+            "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
+            "peak_source": f"{peak_kind} bf16_tflops (burst)"}
+
+
 GEMM_SHAPES = (("gate/up", 512, 4096, 28672), ("q/k/v", 512, 4096, 6144), ("o_proj", 512, 4096, 4096),
                ("down", 512, 14336, 4096), ("gate/up", 2048, 4096, 28672))
 
@@ -637,6 +681,8 @@ def main():
         if args.kernel_only == "gqa":
             for b, ctx in ((1, 1024), (1, 8192), (8, 8192)):
                 print(json.dumps(gqa_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
+            for S in (512, 1024, 4096):
+                print(json.dumps(gqa_prefill_timing(S, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "gemm":
             for name, m, k, n in GEMM_SHAPES:
                 print(json.dumps(gemm_kernel_timing(name, m, k, n, peaks, peak_kind)), flush=True)

@@ -20,8 +20,11 @@
 // past_b = seqlens_k[b] + 1 - S is read on the device, so a launch configuration (and a CUDA
 // graph holding it) serves every decode step.
 //
-// gqa_append_kernel + gqa_generic_kernel — the same semantics for shapes the decode kernel
-// does not cover (head_size not a multiple of 32, more than 32 query rows per group, unaligned
+// gqa_append_kernel + gqa_mma_prefill_kernel — prompt rows (S > 1, fp16 / bf16, head_size 64 or
+// 128): the append kernel rotates and appends, a tensor-core flash-attention kernel attends.
+//
+// gqa_append_kernel + gqa_generic_kernel — the same semantics for shapes the other kernels
+// do not cover (head_size not a multiple of 32, more than 32 query rows per group, unaligned
 // rows): one CTA per query row, keys in shared memory.
 #include <algorithm>
 #include <cstdlib>
@@ -1001,6 +1004,202 @@ gqa_mma_decode_kernel(GqaKP kp) {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---- tensor-core prefill kernel --------------------------------------------------------------
+// gqa_mma_prefill_kernel — S > 1 (prompt) attention after gqa_append_kernel has rotated the query
+// rows into the fp32 workspace (rounded through T) and written the rotated k and v rows into the
+// KV buffer.  grid (ceil(S / 64), num_heads, batch), 4 warps; warp w owns query rows
+// [64 x + 16 w, + 16).  Key tiles of 64 keys x D stream through two shared-memory buffers by
+// 16-byte cp.async (rows XOR-swizzled for conflict-free ldmatrix); S = Q K^T and O += P V run on
+// mma.sync.m16n8k16 with fp32 accumulation and a base-2 online softmax per row; the tile loop
+// stops at the block's last causal key and starts at its first windowed key.  Query i (position
+// past + i) sees keys [lo_i, past + i] — the bottom-right-aligned causal mask of ONNX GQA.
+constexpr int kPfWarps = 4;
+constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
+constexpr int kPfKeys = 64;             // keys per tile
+
+template <int D>
+struct PfSmem {
+  static constexpr int kTile = kPfKeys * D * 2;  // one K or V tile
+  static constexpr int kTotal = 2 * 2 * kTile;   // [buffer][K, V]
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPfWarps * 32)
+gqa_mma_prefill_kernel(GqaKP kp) {
+  using L = PfSmem<D>;
+  constexpr int NB = D / 8;   // 8-wide n-blocks of O
+  constexpr int KS = D / 16;  // k-steps of q.k
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int h = blockIdx.y, b = blockIdx.z, kvh = h / kp.G;
+  const int past = past_len(kp, b);
+  if (!range_ok(kp, past)) return;  // reported by gqa_append_kernel
+  const int i0 = blockIdx.x * kPfRows;
+  const int ilast = min(kp.S, i0 + kPfRows) - 1;  // last query row of the CTA
+  const int win = kp.local_window;
+  const int lo_blk = win > 0 ? max(0, past + i0 - win + 1) : 0;
+  const int hi_blk = past + ilast;  // last key any row of the CTA sees
+  const int t0 = lo_blk / kPfKeys, t1 = hi_blk / kPfKeys;
+  const int64_t head_base = ((int64_t)b * kp.HK + kvh) * kp.cap;
+  const T* kvk = static_cast<const T*>(kp.kv_k) + head_base * D;
+  const T* kvv = static_cast<const T*>(kp.kv_v) + head_base * D;
+
+  pdl_wait();  // the append kernel wrote the rotated q rows and the new k / v rows
+  pdl_trigger();
+  auto issue = [&](int t, int buf) {
+    unsigned char* kb = sm + buf * 2 * L::kTile;
+    unsigned char* vb = kb + L::kTile;
+    const int key0 = t * kPfKeys;
+    for (int i = threadIdx.x; i < kPfKeys * D / 8; i += kPfWarps * 32) {
+      const int r = i / (D / 8), ch = i % (D / 8);
+      const bool v = key0 + r <= hi_blk;
+      const int64_t row = v ? key0 + r : 0;
+      cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
+      cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+    }
+    cp_async_commit();
+  };
+  issue(t0, 0);
+
+  // this lane's query rows ra = g and rb = g + 8 of the warp (index i, position past + i)
+  const int ia = i0 + warp * 16 + g, ib = ia + 8;
+  const bool va = ia < kp.S, vb_ = ib < kp.S;
+  const int qa_pos = past + ia, qb_pos = past + ib;
+  const int lo_a = win > 0 ? max(0, qa_pos - win + 1) : 0, lo_b = win > 0 ? max(0, qb_pos - win + 1) : 0;
+  // Q as A fragments (the fp32 workspace holds values already rounded through T)
+  uint32_t qf[KS][4];
+  {
+    const float* qra = kp.qrot + (((int64_t)b * kp.S + (va ? ia : 0)) * kp.H + h) * D;
+    const float* qrb = kp.qrot + (((int64_t)b * kp.S + (vb_ ? ib : 0)) * kp.H + h) * D;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const float2 a0 = va ? *reinterpret_cast<const float2*>(qra + kk * 16 + 2 * c) : make_float2(0.f, 0.f);
+      const float2 a1 = vb_ ? *reinterpret_cast<const float2*>(qrb + kk * 16 + 2 * c) : make_float2(0.f, 0.f);
+      const float2 a2 = va ? *reinterpret_cast<const float2*>(qra + kk * 16 + 8 + 2 * c) : make_float2(0.f, 0.f);
+      const float2 a3 = vb_ ? *reinterpret_cast<const float2*>(qrb + kk * 16 + 8 + 2 * c) : make_float2(0.f, 0.f);
+      qf[kk][0] = pack2<T>(a0.x, a0.y);
+      qf[kk][1] = pack2<T>(a1.x, a1.y);
+      qf[kk][2] = pack2<T>(a2.x, a2.y);
+      qf[kk][3] = pack2<T>(a3.x, a3.y);
+    }
+  }
+  // rows of this warp: the first and last keys any of them sees
+  const int wi0 = i0 + warp * 16, wi1 = min(kp.S - 1, wi0 + 15);
+  const int w_hi = past + wi1, w_lo = win > 0 ? max(0, past + wi0 - win + 1) : 0;
+
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float o[NB][4];
+#pragma unroll
+  for (int n = 0; n < NB; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  for (int t = t0; t <= t1; ++t) {
+    const int buf = (t - t0) & 1;
+    if (t < t1) {
+      issue(t + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int key0 = t * kPfKeys;
+    // a warp whose rows all end before this tile (or start after it) skips it
+    if (wi0 < kp.S && key0 <= w_hi && key0 + kPfKeys - 1 >= w_lo) {
+      const unsigned char* kb = sm + buf * 2 * L::kTile;
+      const unsigned char* vb = kb + L::kTile;
+      float sacc[8][4];
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < KS; kk += 2) {
+          uint32_t bfr[4];
+          ldsm_x4(bfr, kb + swz<D>(nb * 8 + (lane & 7), kk * 2 + (lane >> 3)));
+          mma_f32<T>(sacc[nb], qf[kk], bfr[0], bfr[1]);
+          mma_f32<T>(sacc[nb], qf[kk + 1], bfr[2], bfr[3]);
+        }
+      }
+      // masks: key j is visible to row i iff lo_i <= j <= past + i
+      const bool full = key0 >= max(lo_a, lo_b) && key0 + kPfKeys - 1 <= min(qa_pos, qb_pos) && va && vb_;
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = key0 + nb * 8 + 2 * c + e;
+          float sa = sacc[nb][e] * kp.scale_log2, sb = sacc[nb][2 + e] * kp.scale_log2;
+          if (!full) {
+            sa = (va && j >= lo_a && j <= qa_pos) ? sa : -INFINITY;
+            sb = (vb_ && j >= lo_b && j <= qb_pos) ? sb : -INFINITY;
+          }
+          sacc[nb][e] = sa;
+          sacc[nb][2 + e] = sb;
+          mxa = fmaxf(mxa, sa);
+          mxb = fmaxf(mxb, sb);
+        }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
+      const float ca = m_a == -INFINITY ? 0.f : exp2f(m_a - mna);
+      const float cb = m_b == -INFINITY ? 0.f : exp2f(m_b - mnb);
+      float psa = 0.f, psb = 0.f;
+      uint32_t pa[4][4];  // P as A fragments for the tile's four 16-key k-steps
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        const float p0 = sacc[nb][0] == -INFINITY ? 0.f : exp2f(sacc[nb][0] - mna);
+        const float p1 = sacc[nb][1] == -INFINITY ? 0.f : exp2f(sacc[nb][1] - mna);
+        const float p2 = sacc[nb][2] == -INFINITY ? 0.f : exp2f(sacc[nb][2] - mnb);
+        const float p3 = sacc[nb][3] == -INFINITY ? 0.f : exp2f(sacc[nb][3] - mnb);
+        psa += p0 + p1;
+        psb += p2 + p3;
+        pa[nb >> 1][(nb & 1) * 2] = pack2<T>(p0, p1);
+        pa[nb >> 1][(nb & 1) * 2 + 1] = pack2<T>(p2, p3);
+      }
+      psa += __shfl_xor_sync(0xffffffffu, psa, 1);
+      psa += __shfl_xor_sync(0xffffffffu, psa, 2);
+      psb += __shfl_xor_sync(0xffffffffu, psb, 1);
+      psb += __shfl_xor_sync(0xffffffffu, psb, 2);
+      l_a = l_a * ca + psa;
+      l_b = l_b * cb + psb;
+      m_a = mna;
+      m_b = mnb;
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        o[n][0] *= ca;
+        o[n][1] *= ca;
+        o[n][2] *= cb;
+        o[n][3] *= cb;
+      }
+      // O += P V
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int n = 0; n < NB; n += 2) {
+          uint32_t bfr[4];
+          const int r = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          ldsm_x4_t(bfr, vb + swz<D>(r, n + (lane >> 4)));
+          mma_f32<T>(o[n], pa[ks], bfr[0], bfr[1]);
+          mma_f32<T>(o[n + 1], pa[ks], bfr[2], bfr[3]);
+        }
+    }
+    __syncthreads();  // the buffer is refilled by the next iteration's prefetch
+  }
+
+  T* out = static_cast<T*>(kp.out);
+  const float ia_inv = l_a > 0.f ? 1.f / l_a : 0.f, ib_inv = l_b > 0.f ? 1.f / l_b : 0.f;
+#pragma unroll
+  for (int n = 0; n < NB; ++n) {
+    if (va)
+      *reinterpret_cast<uint32_t*>(out + (((int64_t)b * kp.S + ia) * kp.H + h) * D + n * 8 + 2 * c) =
+          pack2<T>(o[n][0] * ia_inv, o[n][1] * ia_inv);
+    if (vb_)
+      *reinterpret_cast<uint32_t*>(out + (((int64_t)b * kp.S + ib) * kp.H + h) * D + n * 8 + 2 * c) =
+          pack2<T>(o[n][2] * ib_inv, o[n][3] * ib_inv);
+  }
+}
+
 namespace {
 
 int pow2_at_least(int x) {
@@ -1143,6 +1342,30 @@ cudaError_t launch_mma_decode(const GqaKP& kp, int splits, cudaStream_t st) {
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, kp);
 }
+
+// prompt rows (S > 1) beyond what the split-K decode kernel holds: tensor-core prefill
+bool mma_prefill_path(const b200ep_gqa_params& p, int dtype, int esz) {
+  return p.seq > 1 && (dtype == kF16 || dtype == kBF16) && (p.head_size == 64 || p.head_size == 128) &&
+         p.bias_batch == 0 && !decode_path(p, esz) && !getenv("ONNXRUNTIME_EP_B200_GQA_SIMT");
+}
+
+template <typename T, int D>
+cudaError_t launch_mma_prefill(const GqaKP& kp, cudaStream_t st) {
+  const int warps = 4;
+  const int items = kp.B * kp.S * (kp.H + kp.HK);
+  cudaError_t e = launch_k(gqa_append_kernel<T>, dim3(div_up(items, warps)), dim3(warps * 32),
+                           warps * kp.D * sizeof(float), st, kp);
+  if (e != cudaSuccess) return e;
+  auto kern = gqa_mma_prefill_kernel<T, D>;
+  static bool configured = false;
+  if (!configured) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<D>::kTotal);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_k(kern, dim3(div_up(kp.S, kPfRows), kp.H, kp.B), dim3(kPfWarps * 32), (size_t)PfSmem<D>::kTotal,
+                  st, kp);
+}
 }  // namespace
 
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
@@ -1225,6 +1448,12 @@ int launch_gqa(const GqaArgs& a, cudaStream_t st) {
     else
       e = p.head_size == 64 ? launch_mma_decode<__nv_bfloat16, 64>(kp, sp, st)
                             : launch_mma_decode<__nv_bfloat16, 128>(kp, sp, st);
+  } else if (mma_prefill_path(p, a.dtype, esz) && aligned) {
+    if (a.dtype == kF16)
+      e = p.head_size == 64 ? launch_mma_prefill<__half, 64>(kp, st) : launch_mma_prefill<__half, 128>(kp, st);
+    else
+      e = p.head_size == 64 ? launch_mma_prefill<__nv_bfloat16, 64>(kp, st)
+                            : launch_mma_prefill<__nv_bfloat16, 128>(kp, st);
   } else if (decode_path(p, esz) && aligned) {
     switch (a.dtype) {
       case kF32: e = launch_decode<float>(kp, st); break;

@@ -290,6 +290,44 @@ def test_gqa_variants_fp16(ops, S, H, HK, D, interleaved, window):
     np.testing.assert_array_equal(to_np(tv), wv)
 
 
+@pytest.mark.parametrize("B,S,H,HK,D,past,window,interleaved", [
+    (1, 64, 32, 8, 128, 0, -1, 0), (2, 130, 8, 2, 64, 57, -1, 1), (2, 200, 16, 4, 128, 300, 64, 0),
+    (1, 512, 32, 8, 128, 0, -1, 0), (2, 97, 32, 8, 128, 1000, -1, 0)])
+def test_gqa_prefill_fp16(ops, B, S, H, HK, D, past, window, interleaved):
+    """Prompt rows (S > 1) on the tensor-core prefill kernel: causal bottom-right alignment, GQA
+    head map, local window, ragged batch (the second sequence 40 keys shorter)."""
+    rng = np.random.default_rng(S * 7 + H + D + past)
+    cap = past + S + 3
+    q, k, v, kc, vc, cos, sin, seqlens = make_gqa_inputs(rng, B, S, H, HK, D, past, cap)
+    if B > 1:
+        seqlens[1] -= 40
+    want, wk, wv = oracle.gqa(q, k, v, kc.copy(), vc.copy(), seqlens, cos, sin, num_heads=H, kv_heads=HK,
+                              interleaved=interleaved, shared_buffer=True, local_window=window)
+    tk, tv = cuda(kc), cuda(vc)
+    out = ops.group_query_attention(cuda(q), cuda(k), cuda(v), tk, tv, cuda(seqlens), cuda(cos), cuda(sin),
+                                    num_heads=H, kv_heads=HK, interleaved=interleaved, local_window=window)
+    np.testing.assert_allclose(to_np(out).astype(np.float32), want.astype(np.float32), **TOL["f16"])
+    np.testing.assert_array_equal(to_np(tk), wk)
+    np.testing.assert_array_equal(to_np(tv), wv)
+
+
+def test_gqa_prefill_bf16(ops):
+    rng = np.random.default_rng(12)
+    B, S, H, HK, D, past = 1, 300, 32, 8, 128, 100
+    cap = past + S + 8
+    q, k, v, kc, vc, cos, sin, seqlens = make_gqa_inputs(rng, B, S, H, HK, D, past, cap, dtype=np.float32)
+    bf = oracle.f32_to_bf16_bits
+    args = [bf(x) for x in (q, k, v, kc, vc, cos, sin)]
+    kco, vco = args[3].copy(), args[4].copy()
+    want, wk, _ = oracle.gqa(args[0], args[1], args[2], kco, vco, seqlens, args[5], args[6], num_heads=H,
+                             kv_heads=HK, shared_buffer=True, dtype="bf16")
+    t = [cuda(x).view(torch.bfloat16) for x in args]
+    out = ops.group_query_attention(t[0], t[1], t[2], t[3], t[4], cuda(seqlens), t[5], t[6], num_heads=H,
+                                    kv_heads=HK)
+    np.testing.assert_allclose(to_np(out.float()), oracle.bf16_bits_to_f32(want), **TOL["bf16"])
+    np.testing.assert_array_equal(to_np(t[3].view(torch.int16)).view(np.uint16), wk)
+
+
 def test_gqa_bf16_decode(ops):
     rng = np.random.default_rng(11)
     B, S, H, HK, D, past = 1, 1, 32, 8, 128, 2000
