@@ -428,7 +428,10 @@ def gemm_kernel_timing(name, M, K, N, peaks, peak_kind, reps=5):
             "peak_source": f"{peak_kind} bf16_tflops (burst)"}
 
 
-def run_ours(args, rank, world, local):
+def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
+    """One decode measurement.  tp=False: every rank holds a full model and decodes its own
+    sequences (data-parallel replicas, no collective on the data path; weak scaling).  tp=True: one
+    model sharded over the ranks (tensor parallel), the same tokens on every rank (strong scaling)."""
     import numpy as np
     import torch
 
@@ -438,7 +441,8 @@ def run_ours(args, rank, world, local):
     cfg = LLAMA3_8B
     B = args.batch
     cap = PROMPT + GEN + 64
-    tp = world > 1  # one model sharded over the ranks (tensor parallel), the same tokens on every rank
+    n_steps = steps or args.steps
+    tp = tp and world > 1
     t_build = time.time()
     ep = E.ExecutionProvider(device_id=local)
     if tp:
@@ -494,7 +498,7 @@ def run_ours(args, rank, world, local):
     seqlens = torch.full((B,), PROMPT - 1, dtype=torch.int32, device="cuda")
     total = torch.tensor([PROMPT], dtype=torch.int32, device="cuda")
     logits = torch.empty(B, 1, cfg.vocab, dtype=torch.float16, device="cuda")
-    pool = torch.from_numpy(rng.integers(0, cfg.vocab, size=(max(GEN, args.steps + args.warmup) + 8, B, 1),
+    pool = torch.from_numpy(rng.integers(0, cfg.vocab, size=(max(GEN, n_steps + args.warmup) + 8, B, 1),
                                          dtype=np.int64)).cuda()
     ins, outs = bind(ids, seqlens, total, logits)
     n_step = [0]
@@ -519,14 +523,14 @@ def run_ours(args, rank, world, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(n_steps):
             decode_step()
         e1.record()
         torch.cuda.synchronize()
     barrier(world)
     dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
     seqs = B if tp else world * B  # sequences the whole job decodes per step
-    value = seqs * args.steps / dev_s
+    value = seqs * n_steps / dev_s
 
     # e2e through the C ABI with host buffers: ids / lengths staged H2D, logits read back per step
     h_ids = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
@@ -550,27 +554,27 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e0.record()
-    for t in range(args.steps):
+    for t in range(n_steps):
         e2e_step(t)
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     e2e_s = max_over_ranks(max(e0.elapsed_time(e1) / 1e3, wall), world)
-    e2e = {"value": round(seqs * args.steps / e2e_s, 2), "unit": "tokens/s",
+    e2e = {"value": round(seqs * n_steps / e2e_s, 2), "unit": "tokens/s",
            "h2d_bytes_per_step": B * 8 + B * 4 + 4, "d2h_bytes_per_step": B * cfg.vocab * 2,
            "path": "b200ep_compiled_run with pinned host tensors"}
 
     peaks, peak_kind = measured_peaks()
-    roof = dominant_kernel_roofline(B, peaks, peak_kind)
+    roof = dominant_kernel_roofline(B, peaks, peak_kind) if with_cpu else None
     desc = json.loads(part.describe())
     result = {
         "metric": f"int4 decode tokens/s (Llama-3-8B shape, batch {B})",
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": n_steps,
         "warmup": args.warmup,
-        "ms_per_step": round(dev_s / args.steps * 1e3, 4),
+        "ms_per_step": round(dev_s / n_steps * 1e3, 4),
         "higher_is_better": True,
         "scaling": "strong" if tp else "weak",
         "vs_baseline": None,
@@ -579,11 +583,13 @@ def run_ours(args, rank, world, local):
         "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)",
                    "layers": cfg.layers, "hidden": cfg.hidden, "heads": f"{cfg.heads}/{cfg.kv_heads}",
                    "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B, "global_batch": seqs,
-                   "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + args.steps}",
+                   "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + n_steps}",
                    "kv_capacity": cap,
                    "parallelism": (f"tp{world}: q/k/v, gate/up and lm_head split by output rows (attention by "
-                                   f"KV head), o/down by K blocks + NCCL all-reduce, logits all-gathered")
-                   if tp else "single GPU",
+                                   f"KV head), o/down by K blocks + peer-memory / NCCL all-reduce, logits "
+                                   f"all-gathered")
+                   if tp else (f"dp{world}: data-parallel replicas, a full int4 model and its own sequences "
+                               f"per GPU, no collective on the data path" if world > 1 else "single GPU"),
                    "l2": "weights 4.4 GB/step streamed from HBM (>> 126 MB L2)",
                    "cuda_graph_replays": desc["graph_replays"], "fused_qkv": desc["fused_qkv"],
                    "fused_swiglu": desc["fused_swiglu"], "prefill_s": round(t_pre, 2),
@@ -591,7 +597,7 @@ def run_ours(args, rank, world, local):
         "e2e": e2e,
         "roofline": roof,
         "clocks": clocks.summary(),
-        "gpu_launches": part.launches_per_run() * args.steps,
+        "gpu_launches": part.launches_per_run() * n_steps,
     }
     # release the compiled partition (its CUDA graphs hold NCCL calls) before the process group goes
     del part, sess, ep, ins, outs, ins_h, outs_h
@@ -599,7 +605,7 @@ def run_ours(args, rank, world, local):
 
     gc.collect()
     torch.cuda.synchronize()
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and with_cpu and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline(cfg, B)
     return result
 
@@ -655,6 +661,10 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
+                    help="N > 1: data-parallel replicas (default, weak scaling) or one tensor-parallel model")
+    ap.add_argument("--no-tp-leg", action="store_true",
+                    help="N > 1 with --parallel dp: skip the tensor-parallel measurement reported beside it")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm"],
                     help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
                          "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes); "
@@ -691,7 +701,13 @@ def main():
         return
 
     rank, world, local = dist_setup(args.gpus)
-    res = run_ours(args, rank, world, local)
+    res = run_ours(args, rank, world, local, tp=args.parallel == "tp")
+    if world > 1 and args.parallel == "dp" and not args.no_tp_leg:
+        # the tensor-parallel form of the same decoder, measured beside the replicas
+        t = run_ours(args, rank, world, local, tp=True, with_cpu=False, steps=min(args.steps, 32))
+        res["tp"] = {k: t[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling")}
+        res["tp"]["parallelism"] = t["config"]["parallelism"]
+        res["tp"]["e2e"] = t["e2e"]["value"]
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

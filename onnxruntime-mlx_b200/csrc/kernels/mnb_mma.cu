@@ -225,10 +225,22 @@ __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
 }
 
 // ---- the TMA-fed streaming kernel -------------------------------------------------------------
-constexpr int kNC = 8;        // consumer warps
+// Geometry of the streaming kernel.  The defaults are the measured best on B200; the macros let a
+// build try other splits without editing the kernel.
+#ifndef B200EP_MNB_WARPS
+#define B200EP_MNB_WARPS 8
+#endif
+#ifndef B200EP_MNB_STAGE_RECORDS
+#define B200EP_MNB_STAGE_RECORDS 32
+#endif
+#ifndef B200EP_MNB_CTAS_PER_SM
+#define B200EP_MNB_CTAS_PER_SM 2
+#endif
+constexpr int kNC = B200EP_MNB_WARPS;  // consumer warps
+constexpr int kMinCtas = B200EP_MNB_CTAS_PER_SM;  // CTAs per SM the ring depth is chosen for
 constexpr int kMaxStages = 4; // ring stages (chosen per launch: 2..4)
 constexpr size_t kXStageMax = 64 * 1024;  // bytes of staged activation rows (else read from global)
-constexpr int kG = 32;        // records per stage (one bulk copy, ~19 KB for block 32)
+constexpr int kG = B200EP_MNB_STAGE_RECORDS;  // records per stage (one bulk copy, ~19 KB for 32 x block 32)
 enum { kErrMnbTimeout = 301 };
 
 __device__ __forceinline__ int64_t lmin(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -552,7 +564,7 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
 }
 
 template <typename T, int BLOCK, int NT, bool PAIR>
-__global__ void __launch_bounds__((kNC + 1) * 32, 2)
+__global__ void __launch_bounds__((kNC + 1) * 32, kMinCtas)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
                int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
@@ -867,7 +879,7 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
     if (e != cudaSuccess) return e;
     configured = smem_for(kMaxStages);
   }
-  // deepest ring that still leaves two CTAs per SM (weights in flight per SM ~ 2 x ring)
+  // deepest ring that still leaves kMinCtas CTAs per SM (weights in flight per SM ~ kMinCtas x ring)
   static size_t occ_key[8] = {};
   static int occ_val[8] = {};
   auto per_sm_for = [&](size_t smem, int* out) -> cudaError_t {
@@ -888,7 +900,7 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
     int n = 0;
     if (cudaError_t e = per_sm_for(smem_for(sg), &n)) return e;
     if (sg == kMaxStages) per_sm = std::max(1, n);
-    if (n >= 2) {
+    if (n >= kMinCtas) {
       stages = sg, per_sm = n;
       break;
     }
