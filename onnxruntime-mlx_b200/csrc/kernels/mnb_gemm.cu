@@ -7,18 +7,19 @@
 //                      swizzle into a ring of 3 stages (two row sub-tiles share each B tile when
 //                      M > 128, halving the dequantisation per flop);
 //   warp 2 (one lane)  the eight 16-row int4 group records of the W tile for each stage (1-D bulk
-//                      copies from the prepacked stream) into a separate, deeper ring of 8, so the
-//                      HBM latency of the weights is hidden behind several stages of work;
-//   warps 3..10        dequantise the records (one each) into two B tiles [128 rows x 64 k] of the I/O dtype in
-//                      the same 128-byte swizzled K-major layout: hi = (q - z) * scale rounded
-//                      once, lo = the rounding residual (one fused multiply-add), so hi + lo carries
-//                      the weight to ~22 bits — the accuracy of the fp32-dequantising GEMV; fence
-//                      them to the async proxy and arrive;
-//   warp 1 (one lane)  issues eight tcgen05.mma.kind::f16 (128 x 128 x 16, fp32 in TMEM: A.hi and
-//                      A.lo per 16-k step) per stage and commits them to the stage's "empty"
-//                      barrier, which frees the stage;
-//   warps 3..10        finally read the accumulator with tcgen05.ld (each warp 64 columns of its
-//                      32 TMEM lanes) and store the rows of Y.
+//                      copies from the prepacked stream) into a separate, deeper record ring (8, or
+//                      4 with two sub-tiles), started before the wait for the previous kernel;
+//   warps 3..18        dequantise the records (two warps per record, two 16-k steps each) into
+//                      two B tiles [128 rows x 64 k] of the I/O dtype in the same 128-byte swizzled
+//                      K-major layout, written with stmatrix straight from the fragment registers:
+//                      hi = (q - z) * scale rounded once, lo = the rounding residual (one fused
+//                      multiply-add), so hi + lo is the fp32 dequantised weight; fence them to the
+//                      async proxy and arrive;
+//   warp 1 (one lane)  issues tcgen05.mma.kind::f16 (128 x 128 x 16, fp32 in TMEM: hi and lo per
+//                      16-k step and row sub-tile) and commits them to the stage's "empty" barrier,
+//                      which frees the stage;
+//   warps 3..18        finally read the accumulators with tcgen05.ld (a warp reads its 32 TMEM
+//                      lanes; the four warps of a lane quarter split the columns) and store Y.
 // CTAs along x cover the M tiles of one W tile, so the W tile is read from HBM once and the other
 // M tiles find it in L2.  Every mbarrier wait is bounded (timeout -> device error word).
 #include <cuda.h>
@@ -38,7 +39,7 @@ namespace {
 
 constexpr int kGStages = 3;   // A / B tile ring
 constexpr int kTM = 128, kTN = 128, kTK = 64;
-constexpr int kDeq = 8;       // dequantising (and epilogue) warps: 3 .. 3 + kDeq - 1
+constexpr int kDeq = 16;      // dequantising (and epilogue) warps: 3 .. 3 + kDeq - 1 (8 or 16)
 constexpr int kGThreads = (3 + kDeq) * 32;
 enum { kErrGemmTimeout = 303 };
 
@@ -147,6 +148,14 @@ __device__ __forceinline__ uint32_t sw128(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
 }
 
+// four 8 x 8 b16 matrices from mma fragment registers into shared memory rows (one 16-byte row
+// segment per lane address: lanes 8m .. 8m + 7 give the rows of matrix m)
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
 template <typename T, int BLOCK, int MSUB>
 __global__ void __launch_bounds__(kGThreads, 1)
 mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restrict__ recs, T* __restrict__ Y,
@@ -194,9 +203,13 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();  // A comes from the previous kernel; Y is read by the next one
-  pdl_trigger();
 
+  // Warp 2 streams weights (constants) at once; the other roles wait for the previous kernel
+  // (A is its output; Y may still be read by it)
+  if (warp != 2) {
+    pdl_wait();
+    pdl_trigger();
+  }
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < nst; ++i) {
@@ -267,9 +280,16 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
     }
     __syncwarp();
   } else {
-    // warps 3 .. 3 + kDeq - 1: dequantise one record each per stage, then the epilogue
+    // warps 3 .. 3 + kDeq - 1: kDeq / 8 warps per record, each dequantising 4 / (kDeq / 8) of its
+    // k-steps per stage, then the epilogue
+    constexpr int kDPR = kDeq / 8;  // warps per record
+    constexpr int kSPW = 4 / kDPR;  // k-steps per warp
     const int dw = warp - 3;
-    const int g = lane >> 2, c = lane & 3;
+    const int j = dw / kDPR, st0 = (dw % kDPR) * kSPW;
+    // stmatrix row address of this lane: matrix m = lane / 8 holds rows (m & 1) * 8 .. + 7 of the
+    // record and k (m >> 1) * 8 .. + 7 of the k-step (the order of the mma A fragment registers)
+    const int srow = j * 16 + ((lane >> 3) & 1) * 8 + (lane & 7), skh = (lane >> 4) * 8;
+    const int g = lane >> 2;
     bool alive = true;
     for (int i = 0; i < nst; ++i) {
       const int s = i % kGStages, rr = i % kRStages;
@@ -285,34 +305,36 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
       unsigned char* bt = sm + GemmSmem::kB + s * 2 * GemmSmem::kBTile;
       unsigned char* bl = bt + GemmSmem::kBTile;
       const unsigned char* rs = sm + GemmSmem::kRec + rr * GemmSmem::kRecStage;
+      const bool have = alive && tile0 + j < ntiles;
+      const unsigned char* rec = rs + j * RC::kBytes;
+      uint32_t words[kSPW];
 #pragma unroll
-      for (int jj = 0; jj < 8 / kDeq; ++jj) {
-        const int j = dw * (8 / kDeq) + jj;
-        const bool have = alive && tile0 + j < ntiles;
-        const unsigned char* rec = rs + j * RC::kBytes;
-        uint4 w4 = make_uint4(0, 0, 0, 0);
-        if (have) w4 = *reinterpret_cast<const uint4*>(rec + lane * 16);
-        const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          const int sl = SPB <= 4 ? st / SPB : 0;
-          uint32_t sw = 0, zr = 0;
-          if (have) {
-            sw = *reinterpret_cast<const uint32_t*>(rec + RC::kSOff + (g * RC::kSlots + sl) * 4);
-            zr = __byte_perm((uint32_t)rec[RC::kZOff + g * RC::kSlots + sl], 0, 0x4040);
-          }
-          const uint32_t sg2 = __byte_perm(sw, 0, 0x1010), sh2 = __byte_perm(sw, 0, 0x3232);
-          uint32_t o[4], lo[4];
-          dequant8<T>(words[st], zr, sg2, sh2, o, lo);
-          if (!have) o[0] = o[1] = o[2] = o[3] = lo[0] = lo[1] = lo[2] = lo[3] = 0u;
-          const int r0 = j * 16 + g, r1 = r0 + 8, k0 = st * 16 + 2 * c;
-          const uint32_t off[4] = {sw128(r0, k0), sw128(r1, k0), sw128(r0, k0 + 8), sw128(r1, k0 + 8)};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            *reinterpret_cast<uint32_t*>(bt + off[u]) = o[u];
-            *reinterpret_cast<uint32_t*>(bl + off[u]) = lo[u];
-          }
+      for (int u = 0; u < kSPW; ++u) words[u] = 0u;
+      if (have) {
+        if constexpr (kSPW == 4) {
+          const uint4 w4 = *reinterpret_cast<const uint4*>(rec + lane * 16);
+          words[0] = w4.x, words[1] = w4.y, words[2] = w4.z, words[3] = w4.w;
+        } else {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(rec + lane * 16 + st0 * 4);
+          words[0] = w2.x, words[1] = w2.y;
         }
+      }
+#pragma unroll
+      for (int u = 0; u < kSPW; ++u) {
+        const int st = st0 + u;
+        const int sl = SPB <= 4 ? st / SPB : 0;
+        uint32_t sw = 0, zr = 0;
+        if (have) {
+          sw = *reinterpret_cast<const uint32_t*>(rec + RC::kSOff + (g * RC::kSlots + sl) * 4);
+          zr = __byte_perm((uint32_t)rec[RC::kZOff + g * RC::kSlots + sl], 0, 0x4040);
+        }
+        const uint32_t sg2 = __byte_perm(sw, 0, 0x1010), sh2 = __byte_perm(sw, 0, 0x3232);
+        uint32_t o[4], lo[4];
+        dequant8<T>(words[u], zr, sg2, sh2, o, lo);
+        if (!have) o[0] = o[1] = o[2] = o[3] = lo[0] = lo[1] = lo[2] = lo[3] = 0u;
+        const int kk = st * 16 + skh;
+        stsm_x4(smem_u32(bt + sw128(srow, kk)), o);
+        stsm_x4(smem_u32(bl + sw128(srow, kk)), lo);
       }
       // generic-proxy writes -> visible to the tensor core's (async proxy) reads
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
