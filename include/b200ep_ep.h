@@ -99,6 +99,15 @@ B200EP_API int b200ep_compiled_launches_per_run(const b200ep_compiled* c);
  * the inserted AllReduce / AllGather steps in launch order.  No counterpart in the reference (which
  * has no multi-GPU path); it lets the sharding be checked on a machine without GPUs.  *needed
  * receives the JSON length + 1; out may be NULL to query it. */
+/* Session summary as JSON (reference: MlxTracer::log_summary, rust/src/trace.rs:640-735): claimed
+ * / total nodes and per op type why nodes stayed on CPU, partitions compiled (time, weight bytes),
+ * runs per path (decode / prefill / general) and how they ran (graph replay, capture, eager),
+ * shape-key cache hits, host boundary bytes staged, host time in runs.  Same two-call sizing as
+ * b200ep_tp_shard_preview.  With ONNXRUNTIME_EP_B200_VERBOSE=1 (or provider option verbose=1) the
+ * text form is printed to stderr by b200ep_ep_release, as the reference does with
+ * ONNXRUNTIME_EP_MLX_VERBOSE. */
+B200EP_API int b200ep_ep_summary(const b200ep_ep* ep, char* out, size_t cap, size_t* needed);
+
 B200EP_API int b200ep_tp_shard_preview(const b200ep_graph* g, int rank, int world, char* out, size_t cap,
                                       size_t* needed);
 

@@ -232,6 +232,7 @@ B200EP_API int b200ep_graph_num_nodes(const b200ep_graph* g) { return g ? (int)g
 B200EP_API b200ep_ep* b200ep_ep_create(const char* const* keys, const char* const* values, size_t n) {
   try {
     auto* ep = new b200ep_ep();
+    ep->cfg.summary = std::make_shared<SessionSummary>();
     ep->cfg.cuda_graph = !truthy(getenv("ONNXRUNTIME_EP_B200_NO_GRAPH"));
     ep->cfg.fuse = !truthy(getenv("ONNXRUNTIME_EP_B200_NO_FUSION"));
     ep->cfg.verbose = truthy(getenv("ONNXRUNTIME_EP_B200_VERBOSE"));
@@ -252,7 +253,24 @@ B200EP_API b200ep_ep* b200ep_ep_create(const char* const* keys, const char* cons
   }
 }
 
-B200EP_API void b200ep_ep_release(b200ep_ep* ep) { delete ep; }
+B200EP_API void b200ep_ep_release(b200ep_ep* ep) {
+  if (ep && ep->cfg.verbose && ep->cfg.summary) fprintf(stderr, "%s\n", ep->cfg.summary->text().c_str());
+  delete ep;
+}
+
+B200EP_API int b200ep_ep_summary(const b200ep_ep* ep, char* out, size_t cap, size_t* needed) {
+  GUARD_BEGIN
+  B200EP_CHECK_ARG(ep && ep->cfg.summary, "ep is null");
+  const std::string js = ep->cfg.summary->json();
+  if (needed) *needed = js.size() + 1;
+  if (out && cap > 0) {
+    const size_t n = std::min(cap - 1, js.size());
+    memcpy(out, js.data(), n);
+    out[n] = 0;
+  }
+  return B200EP_OK;
+  GUARD_END
+}
 
 B200EP_API const char* b200ep_ep_name(const b200ep_ep* ep) { return ep ? ep->name.c_str() : ""; }
 
@@ -269,6 +287,19 @@ B200EP_API int b200ep_ep_get_capability(b200ep_ep* ep, const b200ep_graph* g, in
     for (int ni : ep->groups[gi])
       if (node_group) node_group[ni] = (int32_t)gi;
   if (num_groups) *num_groups = (int32_t)ep->groups.size();
+  if (ep->cfg.summary) {
+    SessionSummary& sm = *ep->cfg.summary;
+    std::lock_guard<std::mutex> lk(sm.mu);
+    ++sm.getcap_calls;
+    sm.total_nodes += (int64_t)g->g.nodes.size();
+    sm.partitions += (int64_t)ep->groups.size();
+    for (auto& gr : ep->groups) sm.claimed_nodes += (int64_t)gr.size();
+    for (size_t i = 0; i < ep->last.reasons.size(); ++i)
+      if (!ep->last.reasons[i].empty()) {
+        auto& r = sm.rejected[g->g.nodes[i].op_type];
+        if (r.first++ == 0) r.second = ep->last.reasons[i];
+      }
+  }
   if (ep->cfg.verbose) {
     int claimed = 0;
     for (auto& gr : ep->groups) claimed += (int)gr.size();

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <chrono>
 #include <set>
 #include <sstream>
 #include <unordered_map>
@@ -35,6 +36,7 @@ struct Plan::Program {
   std::vector<Slot> slots;
   std::vector<std::unique_ptr<DevMem>> mems;
   std::map<std::string, cudaGraphExec_t> graphs;
+  int path = 2;  // 0 decode, 1 prefill, 2 general (for the session summary)
   ~Program() {
     for (auto& kv : graphs)
       if (kv.second) cudaGraphExecDestroy(kv.second);
@@ -532,8 +534,68 @@ int Plan::upload_constants(const Graph& g, std::string* err) {
   return B200EP_OK;
 }
 
+std::string SessionSummary::json() const {
+  std::lock_guard<std::mutex> lk(mu);
+  std::ostringstream o;
+  o << "{\"getcap_calls\":" << getcap_calls << ",\"total_nodes\":" << total_nodes
+    << ",\"claimed_nodes\":" << claimed_nodes << ",\"partitions\":" << partitions << ",\"rejected\":{";
+  bool first = true;
+  for (auto& [op, v] : rejected) {
+    o << (first ? "" : ",") << "\"" << op << "\":{\"nodes\":" << v.first << ",\"reason\":\"";
+    for (char ch : v.second) o << (ch == '"' || ch == '\\' ? '\'' : ch);
+    o << "\"}";
+    first = false;
+  }
+  o << "},\"compiles\":" << compiles << ",\"compile_ms\":" << compile_ms << ",\"weight_bytes\":" << weight_bytes
+    << ",\"path_decode\":" << path_decode << ",\"path_prefill\":" << path_prefill
+    << ",\"path_general\":" << path_general << ",\"graph_replays\":" << graph_replays
+    << ",\"graph_captures\":" << graph_captures << ",\"eager_runs\":" << eager_runs
+    << ",\"key_hits\":" << key_hits << ",\"key_misses\":" << key_misses << ",\"h2d_bytes\":" << h2d_bytes
+    << ",\"d2h_bytes\":" << d2h_bytes << ",\"run_ms\":" << run_ms << "}";
+  return o.str();
+}
+
+std::string SessionSummary::text() const {
+  std::lock_guard<std::mutex> lk(mu);
+  std::ostringstream o;
+  const double pct = total_nodes ? 100.0 * (double)claimed_nodes / (double)total_nodes : 0.0;
+  o.setf(std::ios::fixed);
+  o.precision(1);
+  o << "===== B200 EP session summary =====\n"
+    << "  claim:   " << claimed_nodes << "/" << total_nodes << " nodes claimed (" << pct << "%) across "
+    << partitions << " partition(s), " << getcap_calls << " GetCapability call(s)\n";
+  if (!rejected.empty()) {
+    o << "           unclaimed (-> CPU):\n";
+    for (auto& [op, v] : rejected) o << "             - " << op << " x" << v.first << ": " << v.second << "\n";
+  }
+  o << "  compile: " << compiles << " partition(s), " << compile_ms << " ms, "
+    << (double)weight_bytes / (1024.0 * 1024.0) << " MiB of weights in HBM\n"
+    << "  compute: decode=" << path_decode << " prefill=" << path_prefill << " general=" << path_general
+    << "  (graph replay " << graph_replays << ", capture " << graph_captures << ", eager " << eager_runs
+    << "; shape keys " << key_hits << " HIT / " << key_misses << " MISS)\n"
+    << "  memory:  host inputs staged " << (double)h2d_bytes / (1024.0 * 1024.0) << " MiB H2D, host outputs "
+    << (double)d2h_bytes / (1024.0 * 1024.0) << " MiB D2H\n"
+    << "  timing:  compile=" << compile_ms << " ms, run (host)=" << run_ms << " ms\n"
+    << "===================================";
+  return o.str();
+}
+
 std::unique_ptr<Plan> Plan::compile(const Graph& g, const std::vector<int>& nodes, const EpConfig& cfg,
                                     std::string* err) {
+  const auto t0 = std::chrono::steady_clock::now();
+  std::unique_ptr<Plan> p = compile_impl(g, nodes, cfg, err);
+  if (p && cfg.summary && !cfg.host_only) {
+    std::lock_guard<std::mutex> lk(cfg.summary->mu);
+    ++cfg.summary->compiles;
+    cfg.summary->weight_bytes += p->stats_.weight_bytes;
+    cfg.summary->compile_ms +=
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  }
+  return p;
+}
+
+std::unique_ptr<Plan> Plan::compile_impl(const Graph& g, const std::vector<int>& nodes, const EpConfig& cfg,
+                                         std::string* err) {
   std::unique_ptr<Plan> p(new Plan());
   p->cfg_ = cfg;
   p->prof_ = env_on("ONNXRUNTIME_EP_B200_PROFILE");
@@ -1192,7 +1254,12 @@ int Plan::run(const std::vector<TensorArg>& in, const std::vector<TensorArg>& ou
   cudaStream_t st = stream_;
   B200EP_CUDA_RET(cudaEventRecord(ev_in_, caller));
   B200EP_CUDA_RET(cudaStreamWaitEvent(st, ev_in_, 0));
+  const auto t0 = std::chrono::steady_clock::now();
   int rc = run_locked(in, out, st);
+  if (cfg_.summary) {
+    std::lock_guard<std::mutex> sl(cfg_.summary->mu);
+    cfg_.summary->run_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  }
   cudaEventRecord(ev_out_, st);
   cudaStreamWaitEvent(caller, ev_out_, 0);
   return rc;
@@ -1207,6 +1274,11 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
   for (size_t i = 0; i < in.size(); ++i) key += shape_str(in[i].shape) + (in[i].on_device ? "d" : "h") + ";";
   for (size_t i = 0; i < out.size(); ++i) key += shape_str(out[i].shape) + (out[i].on_device ? "d" : "h") + ";";
   auto it = programs_.find(key);
+  SessionSummary* sum = cfg_.summary.get();
+  if (sum) {
+    std::lock_guard<std::mutex> sl(sum->mu);
+    ++(it == programs_.end() ? sum->key_misses : sum->key_hits);
+  }
   if (it == programs_.end()) {
     auto prog = std::make_unique<Program>();
     prog->slots = slots_;
@@ -1268,6 +1340,11 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
         prog->mems.push_back(std::move(mem));
       }
     }
+    for (const Step& stp : steps_)
+      if (stp.kind == StepKind::kGqa) {
+        const int rows = (int)prog->slots[stp.in[0]].shape[1];
+        prog->path = rows > 1 ? 1 : (prog->path == 1 ? 1 : 0);
+      }
     it = programs_.emplace(key, std::move(prog)).first;
   }
   Program& prog = *it->second;
@@ -1283,6 +1360,10 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
         const size_t bytes = (size_t)numel_of(s.shape) * dtype_size(s.dtype);
         if (bytes) B200EP_CUDA_RET(cudaMemcpyAsync(s.ptr, a.data, bytes, cudaMemcpyHostToDevice, st));
         if (!s.host_copy.empty()) memcpy(s.host_copy.data(), a.data, s.host_copy.size());
+        if (sum) {
+          std::lock_guard<std::mutex> sl(sum->mu);
+          sum->h2d_bytes += (int64_t)bytes;
+        }
       }
     } else if (s.kind == Slot::kOutput && out[s.io].on_device) {
       s.ptr = out[s.io].data;
@@ -1295,6 +1376,7 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
   }
   ++stats_.runs;
   const bool use_graph = cfg_.cuda_graph && !env_on("ONNXRUNTIME_EP_B200_NO_GRAPH");
+  const int64_t replays0 = stats_.graph_replays, captures0 = stats_.graph_captures;
   if (use_graph) {
     auto g = prog.graphs.find(ptr_key);
     if (g == prog.graphs.end()) {
@@ -1336,11 +1418,22 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
     if (int rc = launch_steps(S, prog, st)) return rc;
   }
   // host outputs
+  int64_t d2h = 0;
   for (auto& s : S)
     if (s.kind == Slot::kOutput && !out[s.io].on_device) {
       const size_t bytes = (size_t)numel_of(s.shape) * dtype_size(s.dtype);
       if (bytes) B200EP_CUDA_RET(cudaMemcpyAsync(out[s.io].data, s.ptr, bytes, cudaMemcpyDeviceToHost, st));
+      d2h += (int64_t)bytes;
     }
+  if (sum) {
+    std::lock_guard<std::mutex> sl(sum->mu);
+    ++(prog.path == 0 ? sum->path_decode : prog.path == 1 ? sum->path_prefill : sum->path_general);
+    const int64_t rp = stats_.graph_replays - replays0, cp = stats_.graph_captures - captures0;
+    sum->graph_replays += rp;
+    sum->graph_captures += cp;
+    if (!rp) ++sum->eager_runs;
+    sum->d2h_bytes += d2h;
+  }
   bool any_host_out = false;
   for (auto& o : out) any_host_out |= !o.on_device;
   if (any_host_out) B200EP_CUDA_RET(cudaStreamSynchronize(st));

@@ -30,6 +30,28 @@ namespace b200ep {
 
 struct TpContext;  // tensor-parallel communicator (tp.h)
 
+// Session digest of one EP (reference: MlxTracer::log_summary, rust/src/trace.rs:640-735, printed
+// when ONNXRUNTIME_EP_MLX_VERBOSE is set): claim rate and why nodes stayed on CPU, compiled
+// partitions, runs per path and shape-key cache, boundary copies, host time.  Shared by the EP and
+// its compiled partitions; printed to stderr when the EP is released with
+// ONNXRUNTIME_EP_B200_VERBOSE=1, and returned as JSON by b200ep_ep_summary.
+struct SessionSummary {
+  mutable std::mutex mu;
+  int64_t getcap_calls = 0, total_nodes = 0, claimed_nodes = 0, partitions = 0;
+  std::map<std::string, std::pair<int64_t, std::string>> rejected;  // op type -> (nodes, first reason)
+  int64_t compiles = 0, weight_bytes = 0;
+  double compile_ms = 0;
+  // runs by path: decode (every attention step has one query row), prefill (more rows), general
+  // (no attention); how they executed: CUDA-graph replay, graph capture, eager
+  int64_t path_decode = 0, path_prefill = 0, path_general = 0;
+  int64_t graph_replays = 0, graph_captures = 0, eager_runs = 0;
+  int64_t key_hits = 0, key_misses = 0;  // per-shape-key program cache
+  int64_t h2d_bytes = 0, d2h_bytes = 0;  // host boundary tensors staged through the EP
+  double run_ms = 0;                     // host time inside compiled runs
+  std::string json() const;
+  std::string text() const;
+};
+
 struct EpConfig {
   bool cuda_graph = true;
   bool fuse = true;
@@ -37,6 +59,7 @@ struct EpConfig {
   std::string layer_partitions;  // "" = unset
   std::shared_ptr<TpContext> tp;  // null = single GPU
   bool host_only = false;         // lower, fuse and shard on the host only (no upload): preview()
+  std::shared_ptr<SessionSummary> summary;  // null = not recorded
 };
 
 struct TensorArg {
@@ -146,6 +169,8 @@ class Plan {
  private:
   struct Program;  // per-shape-key buffers and captured graphs
   Plan() = default;
+  static std::unique_ptr<Plan> compile_impl(const Graph& g, const std::vector<int>& nodes, const EpConfig& cfg,
+                                            std::string* err);
   int lower(const Graph& g, const std::vector<int>& nodes, std::string* err);
   int upload_constants(const Graph& g, std::string* err);
   void fuse_qkv();

@@ -74,6 +74,7 @@ def _lib():
         L.b200ep_tp_unique_id.argtypes = [vp]
         L.b200ep_ep_set_tensor_parallel.argtypes = [vp, i32, i32, vp]
         L.b200ep_tp_shard_preview.argtypes = [vp, i32, i32, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
+        L.b200ep_ep_summary.argtypes = [vp, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
         _configured = True
     return L
 
@@ -190,6 +191,18 @@ class ExecutionProvider:
 
     def claim_reason(self, node: int) -> str:
         return _lib().b200ep_ep_claim_reason(self._ep, node).decode()
+
+    def summary(self) -> dict:
+        """Session summary: claim rate and unclaimed op types with reasons, compiled partitions,
+        runs per path (decode / prefill / general) and execution (graph replay / capture / eager),
+        shape-key cache, host boundary bytes, host time (printed at release when verbose)."""
+        import json
+
+        need = ctypes.c_size_t(0)
+        check(_lib().b200ep_ep_summary(self._ep, None, 0, ctypes.byref(need)))
+        buf = ctypes.create_string_buffer(need.value)
+        check(_lib().b200ep_ep_summary(self._ep, buf, need.value, ctypes.byref(need)))
+        return json.loads(buf.value.decode())
 
     def compile(self, g: GraphBuilder, group: int) -> "Compiled":
         out = ctypes.c_void_p()

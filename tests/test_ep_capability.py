@@ -182,6 +182,26 @@ def test_convex_clusters_split_around_unclaimed_node():
     assert groups[0] >= 0 and groups[2] >= 0 and groups[0] != groups[2] and num == 2
 
 
+def test_session_summary_counts_claims_and_reasons():
+    """The session summary (reference: MlxTracer::log_summary, rust/src/trace.rs:640-735) counts
+    claimed nodes, partitions and, per op type, why nodes stayed on CPU; no GPU work recorded."""
+    g = GraphBuilder()
+    g.input("x", FLOAT, [4])
+    for n in ("a", "r", "c"):
+        g.tensor(n, FLOAT, [4])
+    g.output("c", FLOAT, [4])
+    g.node("Sigmoid", ["x"], ["a"], name="a")
+    g.node("Relu", ["a"], ["r"], name="relu")
+    g.node("Add", ["a", "r"], ["c"], name="c")
+    ep, _, num = claimed(g)
+    ep.get_capability(g)
+    s = ep.summary()
+    assert s["getcap_calls"] == 2 and s["total_nodes"] == 6 and s["claimed_nodes"] == 4
+    assert s["partitions"] == 2 * num
+    assert s["rejected"]["Relu"]["nodes"] == 2 and "no B200 handler" in s["rejected"]["Relu"]["reason"]
+    assert s["compiles"] == 0 and s["path_decode"] == s["path_prefill"] == s["eager_runs"] == 0
+
+
 def test_convex_cluster_merges_chain():
     g = GraphBuilder()
     g.input("x", FLOAT, [4])

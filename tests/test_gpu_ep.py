@@ -210,3 +210,8 @@ def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
                                    kv_ref[i][0].astype(np.float32)[:, :, :P + steps], rtol=2e-2, atol=2e-2)
     d = json.loads(sess_d.parts[0].describe())
     assert d["graph_replays"] >= steps - 2  # one CUDA graph serves every decode step
+    # the session summaries see the same: a prefill run on one EP, decode runs on the other
+    sp, sd = sess_p.ep.summary(), sess_d.ep.summary()
+    assert sp["path_prefill"] == 1 and sp["path_decode"] == 0 and sp["compiles"] == 1
+    assert sd["path_decode"] == steps and sd["graph_replays"] == d["graph_replays"]
+    assert sd["claimed_nodes"] == sd["total_nodes"] and sd["weight_bytes"] > 0 and sd["key_misses"] == 1
