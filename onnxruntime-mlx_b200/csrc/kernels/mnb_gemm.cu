@@ -26,6 +26,7 @@
 #include <cstdlib>
 
 #include <algorithm>
+#include <string>
 
 #include "../common.cuh"
 #include "kernels.h"
@@ -37,11 +38,11 @@ DeviceErrorSlot* device_error_slot();
 
 namespace {
 
-constexpr int kGStages = 3;   // A / B tile ring
-constexpr int kTM = 128, kTN = 128, kTK = 64;
+constexpr int kTM = 128, kTK = 64;
 constexpr int kDeq = 16;      // dequantising (and epilogue) warps: 3 .. 3 + kDeq - 1 (8 or 16)
 constexpr int kGThreads = (3 + kDeq) * 32;
 enum { kErrGemmTimeout = 303 };
+constexpr int kCost256x256 = 205;  // relative CTA time of a 256 x 256 tile (128 x 128 = 100)
 
 template <int BLOCK>
 struct GRec {  // the record geometry of mnb_mma.cu (kept in sync by mnb_record_bytes)
@@ -51,18 +52,24 @@ struct GRec {  // the record geometry of mnb_mma.cu (kept in sync by mnb_record_
   static constexpr int kBytes = 512 + ((kSlots * 40 + 15) / 16) * 16;
 };
 
-template <int MSUB>
-struct GemmSmem {  // MSUB 128-row sub-tiles of A share every dequantised B tile
-  static constexpr int kRS = MSUB == 1 ? 8 : 4;                // weight-record ring depth
-  static constexpr int kATile = kTM * kTK * 2;                 // 16 KB
+// Tile geometry: MSUB 128-row sub-tiles of A share every dequantised B tile of TN (128 or 256)
+// weight rows; the accumulators take MSUB x TN TMEM columns (at most 512).
+template <int MSUB, int TN>
+struct GemmSmem {
+  static constexpr int kStages = TN == 256 ? 2 : 3;             // A / B tile ring
+  static constexpr int kRPS = TN / 16;                          // weight records per stage
+  static constexpr int kRS = TN == 256 ? 2 : MSUB == 1 ? 8 : 4; // weight-record ring depth
+  static constexpr int kATile = kTM * kTK * 2;                  // 16 KB
   static constexpr int kA = 0;                                  // [stages][MSUB][128 x 64]
-  static constexpr int kB = kA + kGStages * MSUB * kATile;     // [stages][hi, lo][128 x 64]
-  static constexpr int kBTile = kTN * kTK * 2;
-  static constexpr int kRec = kB + kGStages * 2 * kBTile;      // [record stages][8 records]
-  static constexpr int kRecStage = 8 * 704;                     // largest record (block 16) x 8
+  static constexpr int kB = kA + kStages * MSUB * kATile;       // [stages][hi, lo][TN x 64]
+  static constexpr int kBTile = TN * kTK * 2;
+  static constexpr int kRec = kB + kStages * 2 * kBTile;        // [record stages][kRPS records]
+  static constexpr int kRecStage = kRPS * 704;                  // largest record (block 16) x kRPS
   static constexpr int kBar = kRec + kRS * kRecStage;           // full, bready, empty, rfull, rempty, acc
-  static constexpr int kTmemSlot = kBar + (3 * kGStages + 2 * kRS + 1) * 8;
+  static constexpr int kTmemSlot = kBar + (3 * kStages + 2 * kRS + 1) * 8;
   static constexpr int kTotal = kTmemSlot + 16 + 1024;          // + alignment slack
+  static_assert(MSUB * TN <= 512, "TMEM holds 512 fp32 columns");
+  static_assert(kTotal <= 232448, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_byte_addr) {
@@ -76,10 +83,10 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_byte_addr) {
   return d;
 }
 
-template <typename T>
+template <typename T, int TN>
 __device__ __forceinline__ uint32_t idesc_f16() {
   constexpr uint32_t fmt = std::is_same<T, __half>::value ? 0u : 1u;
-  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -156,13 +163,16 @@ __device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
                : "memory");
 }
 
-template <typename T, int BLOCK, int MSUB>
+template <typename T, int BLOCK, int MSUB, int TN>
 __global__ void __launch_bounds__(kGThreads, 1)
 mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restrict__ recs, T* __restrict__ Y,
                 int M, int N, int ntiles, int ksteps4, DeviceErrorSlot* err) {
   using RC = GRec<BLOCK>;
-  using GemmSmem = b200ep::GemmSmem<MSUB>;
+  using GemmSmem = b200ep::GemmSmem<MSUB, TN>;
   constexpr int kRStages = GemmSmem::kRS;
+  constexpr int kGStages = GemmSmem::kStages;
+  constexpr int kTN = TN;
+  constexpr int kRPS = GemmSmem::kRPS;
   constexpr int SPB = BLOCK / 16;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -226,7 +236,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
   } else if (warp == 2) {
     if (lane == 0) {
       int nrec = 0;
-      for (int j = 0; j < 8; ++j) nrec += tile0 + j < ntiles;
+      for (int j = 0; j < kRPS; ++j) nrec += tile0 + j < ntiles;
       for (int i = 0; i < nst; ++i) {
         const int r = i % kRStages;
         if (i >= kRStages && !mbar_wait(&rempty[r], ((i / kRStages) - 1) & 1)) {
@@ -234,7 +244,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
           break;
         }
         mbar_arrive_expect_tx(&rfull[r], (uint32_t)(nrec * RC::kBytes));
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kRPS; ++j)
           if (tile0 + j < ntiles)
             bulk_g2s(sm + GemmSmem::kRec + r * GemmSmem::kRecStage + j * RC::kBytes,
                      recs + ((size_t)(tile0 + j) * ksteps4 + i) * RC::kBytes, RC::kBytes, &rfull[r]);
@@ -242,7 +252,7 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16<T>();
+      const uint32_t idesc = idesc_f16<T, TN>();
       bool alive = true;
       for (int i = 0; i < nst && alive; ++i) {
         const int s = i % kGStages;
@@ -280,9 +290,10 @@ mnb_gemm_kernel(const __grid_constant__ CUtensorMap amap, const uint8_t* __restr
     }
     __syncwarp();
   } else {
-    // warps 3 .. 3 + kDeq - 1: kDeq / 8 warps per record, each dequantising 4 / (kDeq / 8) of its
-    // k-steps per stage, then the epilogue
-    constexpr int kDPR = kDeq / 8;  // warps per record
+    // warps 3 .. 3 + kDeq - 1: kDeq / kRPS warps per record, each dequantising 4 / (kDeq / kRPS)
+    // of its k-steps per stage, then the epilogue
+    constexpr int kDPR = kDeq / kRPS;  // warps per record
+    static_assert(kDPR == 1 || kDPR == 2, "one or two dequantising warps per record");
     constexpr int kSPW = 4 / kDPR;  // k-steps per warp
     const int dw = warp - 3;
     const int j = dw / kDPR, st0 = (dw % kDPR) * kSPW;
@@ -412,7 +423,7 @@ EncodeTiled encode_fn() {
   return fn;
 }
 
-template <typename T, int BLOCK, int MSUB>
+template <typename T, int BLOCK, int MSUB, int TN>
 cudaError_t gemm_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
   EncodeTiled enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
@@ -427,37 +438,48 @@ cudaError_t gemm_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaSt
           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  auto kern = mnb_gemm_kernel<T, BLOCK, MSUB>;
+  auto kern = mnb_gemm_kernel<T, BLOCK, MSUB, TN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<MSUB>::kTotal);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<MSUB, TN>::kTotal);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((unsigned)((M + kTM * MSUB - 1) / (kTM * MSUB)), (unsigned)((p.N + kTN - 1) / kTN));
-  return launch_k(kern, grid, dim3(kGThreads), (size_t)GemmSmem<MSUB>::kTotal, st, map,
+  dim3 grid((unsigned)((M + kTM * MSUB - 1) / (kTM * MSUB)), (unsigned)((p.N + TN - 1) / TN));
+  return launch_k(kern, grid, dim3(kGThreads), (size_t)GemmSmem<MSUB, TN>::kTotal, st, map,
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.ntiles,
                   (int)p.ksteps4, device_error_slot());
 }
 
-// 256-row CTAs dequantise each weight tile once for twice the MMAs but halve the CTA count.  A
-// 256-row CTA takes ~1.35x the time of a 128-row one (measured on B200 over prefill shapes), so
-// compare whole waves of 148 CTAs at those costs.  ONNXRUNTIME_EP_B200_GEMM_MSUB=1|2 forces one.
-int gemm_msub(int64_t M, int64_t N) {
+// Tile shape per launch.  256-row CTAs dequantise each weight tile once for twice the MMAs; 256-
+// column weight tiles halve the A-operand shared-memory reads per flop (a 128 x 128 x 16 MMA
+// needs the whole shared-memory bandwidth; 128 x 256 x 16 leaves a quarter for the dequantised
+// writes).  Relative CTA times measured on B200 over prefill shapes: 128x128 : 256x128 : 256x256 =
+// 1 : 1.35 : 2.05; the choice minimises whole waves of 148 CTAs times that cost.
+// ONNXRUNTIME_EP_B200_GEMM_TILE=128x128|256x128|256x256 forces one.
+int gemm_tile(int64_t M, int64_t N) {
   static const int forced = [] {
-    const char* e = std::getenv("ONNXRUNTIME_EP_B200_GEMM_MSUB");
-    return e ? std::atoi(e) : 0;
+    const char* e = std::getenv("ONNXRUNTIME_EP_B200_GEMM_TILE");
+    if (!e) return 0;
+    const std::string v(e);
+    return v == "128x128" ? 1 : v == "256x128" ? 2 : v == "256x256" ? 3 : 0;
   }();
-  if (forced == 1 || forced == 2) return forced;
+  if (forced) return forced;
   if (M <= kTM) return 1;
-  const int64_t ntn = (N + kTN - 1) / kTN;
-  const int64_t w1 = ((M + kTM - 1) / kTM * ntn + 147) / 148, w2 = ((M + 2 * kTM - 1) / (2 * kTM) * ntn + 147) / 148;
-  return w2 * 135 <= w1 * 100 ? 2 : 1;
+  auto waves = [&](int64_t rows, int64_t cols) {
+    return ((M + rows - 1) / rows * ((N + cols - 1) / cols) + 147) / 148;
+  };
+  const int64_t c1 = waves(128, 128) * 100, c2 = waves(256, 128) * 135, c3 = waves(256, 256) * kCost256x256;
+  return c3 <= c2 && c3 <= c1 ? 3 : c2 <= c1 ? 2 : 1;
 }
 
 template <typename T, int BLOCK>
 cudaError_t gemm_m(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st) {
-  return gemm_msub(M, p.N) == 2 ? gemm_t<T, BLOCK, 2>(A, p, Y, M, st) : gemm_t<T, BLOCK, 1>(A, p, Y, M, st);
+  switch (gemm_tile(M, p.N)) {
+    case 3: return gemm_t<T, BLOCK, 2, 256>(A, p, Y, M, st);
+    case 2: return gemm_t<T, BLOCK, 2, 128>(A, p, Y, M, st);
+    default: return gemm_t<T, BLOCK, 1, 128>(A, p, Y, M, st);
+  }
 }
 
 template <typename T>

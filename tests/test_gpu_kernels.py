@@ -395,7 +395,8 @@ def test_matmulnbits_prepacked_vs_oracle(ops, block, M, asym):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (1, 14336, 4096), (1, 4096, 28672), (16, 4096, 4096),
-                                   (512, 4096, 1024), (1, 1168, 96), (200, 1024, 18944), (300, 4096, 20480)])
+                                   (512, 4096, 1024), (1, 1168, 96), (200, 1024, 18944), (300, 4096, 20480),
+                                   (1000, 256, 28672)])
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_matmulnbits_prepacked_llama_shapes(ops, M, K, N, dt):
     rng = np.random.default_rng(M + K * 3 + N)
