@@ -1013,6 +1013,9 @@ gqa_mma_decode_kernel(GqaKP kp) {
 // mma.sync.m16n8k16 with fp32 accumulation and a base-2 online softmax per row; the tile loop
 // stops at the block's last causal key and starts at its first windowed key.  Query i (position
 // past + i) sees keys [lo_i, past + i] — the bottom-right-aligned causal mask of ONNX GQA.
+// (Measured alternatives, slower on B200 except at prompts of 4K and more: 8 warps per CTA sharing
+// each K / V tile, and 32-key tiles with the Q fragments re-read from shared memory for four CTAs
+// per SM.  mma.sync bounds this kernel; the tcgen05 form is the next step.)
 constexpr int kPfWarps = 4;
 constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
 constexpr int kPfKeys = 64;             // keys per tile

@@ -292,7 +292,7 @@ def test_gqa_variants_fp16(ops, S, H, HK, D, interleaved, window):
 
 @pytest.mark.parametrize("B,S,H,HK,D,past,window,interleaved", [
     (1, 64, 32, 8, 128, 0, -1, 0), (2, 130, 8, 2, 64, 57, -1, 1), (2, 200, 16, 4, 128, 300, 64, 0),
-    (1, 512, 32, 8, 128, 0, -1, 0), (2, 97, 32, 8, 128, 1000, -1, 0)])
+    (1, 512, 32, 8, 128, 0, -1, 0), (2, 97, 32, 8, 128, 1000, -1, 0), (2, 1200, 32, 8, 128, 40, -1, 0)])
 def test_gqa_prefill_fp16(ops, B, S, H, HK, D, past, window, interleaved):
     """Prompt rows (S > 1) on the tensor-core prefill kernel: causal bottom-right alignment, GQA
     head map, local window, ragged batch (the second sequence 40 keys shorter)."""
