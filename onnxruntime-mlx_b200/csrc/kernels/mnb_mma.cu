@@ -569,9 +569,6 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
                int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
-  constexpr int SPB = BLOCK / 16;          // k-steps per block
-  constexpr int SL = RC::kSlots;
-  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr int UNIT = RC::kUnit;
   constexpr int PER = kG / (kNC * UNIT);   // units per warp per full stage
   static_assert(kG % (kNC * UNIT) == 0, "stage must split evenly");
