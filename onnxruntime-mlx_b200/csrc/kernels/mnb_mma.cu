@@ -239,7 +239,10 @@ __device__ __forceinline__ float2 s2_to_f2(uint32_t v, bool bf) {
 constexpr int kNC = B200EP_MNB_WARPS;  // consumer warps
 constexpr int kMinCtas = B200EP_MNB_CTAS_PER_SM;  // CTAs per SM the ring depth is chosen for
 constexpr int kMaxStages = 4; // ring stages (chosen per launch: 2..4)
-constexpr size_t kXStageMax = 64 * 1024;  // bytes of staged activation rows (else read from global)
+// bytes of staged activation rows (else fragments are read from global memory, which costs several
+// times the weight stream at 8-16 rows): up to 16 rows at K = 4096 or 4 rows at K = 14336 (the
+// launch then runs one CTA per SM when two no longer fit)
+constexpr size_t kXStageMax = 144 * 1024;
 constexpr int kG = B200EP_MNB_STAGE_RECORDS;  // records per stage (one bulk copy, ~19 KB for 32 x block 32)
 enum { kErrMnbTimeout = 301 };
 
