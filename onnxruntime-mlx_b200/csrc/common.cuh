@@ -147,6 +147,18 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();  // false when ONNXRUNTIME_EP_B200_NO_PDL is set
 
+// SMs of the current device (cached; every GPU of a node is the same part)
+inline int num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms = n > 0 ? n : 148;
+  }
+  return sms;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg{};

@@ -1312,9 +1312,13 @@ bool mma_decode_path(const b200ep_gqa_params& p, int dtype) {
 
 // splits of one (batch, kv-head) = cluster size (at most 8, the portable limit): one 32-key unit
 // per warp at full capacity where that fits — decode attention is latency-bound at short contexts
+// — but no more than two waves of CTAs over the SMs need (one CTA per SM: 207 KB of shared
+// memory), so that many sequences (batch x kv heads >= 148) stream longer runs per CTA.
 int mma_splits(const b200ep_gqa_params& p) {
   const int64_t units = (p.cap + kUnit - 1) / kUnit;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(8, (units + kMmaWarps - 1) / kMmaWarps));
+  const int64_t heads = std::max<int64_t>(1, p.batch * p.kv_heads);
+  const int64_t by_sms = std::max<int64_t>(1, (2 * num_sms() + heads - 1) / heads);
+  return (int)std::max<int64_t>(1, std::min<int64_t>({8, (units + kMmaWarps - 1) / kMmaWarps, by_sms}));
 }
 
 template <typename T, int D>

@@ -354,16 +354,6 @@ mnb_tile_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
 // ---- host launchers -------------------------------------------------------------------------
 namespace {
 
-int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  return sms;
-}
 
 template <typename T, int BITS, int BLOCK, int MT, bool HAS_ZP>
 cudaError_t launch_gemv_t(const MnbArgs& a, cudaStream_t st) {

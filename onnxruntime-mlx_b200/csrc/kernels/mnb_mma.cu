@@ -842,16 +842,6 @@ cudaError_t prepack_b(const uint8_t* B, const void* scales, const uint8_t* zp, c
   return cudaErrorInvalidValue;
 }
 
-int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  return sms;
-}
 }  // namespace
 
 cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8_t* zp, int scale_dtype,
@@ -954,7 +944,8 @@ cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dt
 bool mnb_prologue_fits(int64_t M, int64_t K, int block) {
   const MnbPacked g = mnb_packed_geometry(1, K, block);
   const int64_t rows = std::min<int64_t>(M <= 8 ? 8 : 16, M);
-  return M > 0 && K % 8 == 0 && (size_t)(rows + 1) * (g.ksteps4 * 64 * 2 + 16) <= kXStageMax;
+  // more than 16 rows run the tensor-core GEMM (the GEMV would re-stream the weights per 16 rows)
+  return M > 0 && M <= 16 && K % 8 == 0 && (size_t)(rows + 1) * (g.ksteps4 * 64 * 2 + 16) <= kXStageMax;
 }
 
 }  // namespace b200ep
