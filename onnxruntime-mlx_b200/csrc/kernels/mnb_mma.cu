@@ -944,8 +944,11 @@ cudaError_t launch_mnb_packed(const void* A, const MnbPacked& p, void* Y, int dt
 bool mnb_prologue_fits(int64_t M, int64_t K, int block) {
   const MnbPacked g = mnb_packed_geometry(1, K, block);
   const int64_t rows = std::min<int64_t>(M <= 8 ? 8 : 16, M);
-  // more than 16 rows run the tensor-core GEMM (the GEMV would re-stream the weights per 16 rows)
-  return M > 0 && M <= 16 && K % 8 == 0 && (size_t)(rows + 1) * (g.ksteps4 * 64 * 2 + 16) <= kXStageMax;
+  // every CTA of the GEMV recomputes the fused producer over all rows from L2, which pays for one
+  // or two rows (measured on B200: batch 4 decodes faster with the standalone producer kernel and
+  // plain staging); more than 16 rows run the tensor-core GEMM
+  return M > 0 && M <= 2 && K % 8 == 0 && (size_t)M * K * 2 <= 32 * 1024 &&
+         (size_t)(rows + 1) * (g.ksteps4 * 64 * 2 + 16) <= kXStageMax;
 }
 
 }  // namespace b200ep
