@@ -244,6 +244,7 @@ constexpr int kMaxStages = 4; // ring stages (chosen per launch: 2..4)
 // launch then runs one CTA per SM when two no longer fit)
 constexpr size_t kXStageMax = 144 * 1024;
 constexpr int kG = B200EP_MNB_STAGE_RECORDS;  // records per stage (one bulk copy, ~19 KB for 32 x block 32)
+constexpr int kXcStride = kG * 64 * 2 + 16;  // bytes per activation row of a stage chunk (padded)
 enum { kErrMnbTimeout = 301 };
 
 __device__ __forceinline__ int64_t lmin(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -492,11 +493,11 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
 //   xp: staged activation fragments of the first record (STAGED) — else ag/live/gi0 address the
 //   activation rows in global memory.  PAIR = false when only even token columns exist (M == 1):
 //   the odd-column accumulators are then left alone.
-template <typename T, int BLOCK, int NT, bool STAGED, bool PAIR>
+template <typename T, int BLOCK, int NT, int XM, bool PAIR>
 __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned char* pq,
                                          const unsigned char* const (&xp)[NT], const uint32_t* const (&ag)[NT],
                                          const uint32_t (&live)[NT], int gi0, int ksteps, int g,
-                                         const DqConst& kq, float (&acc)[NT][4]) {
+                                         const DqConst& kq, float (&acc)[NT][4], uint32_t xc = 0) {
   using RC = Rec<BLOCK>;
   constexpr int SPB = BLOCK / 16;
   constexpr int SL = RC::kSlots;
@@ -507,7 +508,28 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
     uint32_t b[NT][8];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      if constexpr (STAGED) {
+      if constexpr (XM == 2) {
+        // row-major chunk of this stage: ldmatrix per k-step (matrices: tokens 0-7 / 8-15 x k 0-7 / 8-15)
+        if (nt == 0) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = xc + (uint32_t)(r * 128 + j * 32);
+            if constexpr (NT == 2) {
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(b[0][2 * j]), "=r"(b[0][2 * j + 1]), "=r"(b[1][2 * j]), "=r"(b[1][2 * j + 1])
+                           : "r"(a));
+            } else {
+              asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                           : "=r"(b[0][2 * j]), "=r"(b[0][2 * j + 1])
+                           : "r"(a));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < NT; ++q)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) b[q][e] &= live[q];
+        }
+      } else if constexpr (XM == 1) {
         const uint4 lo = *reinterpret_cast<const uint4*>(xp[nt] + r * 128);
         const uint4 hi = *reinterpret_cast<const uint4*>(xp[nt] + r * 128 + 16);
         b[nt][0] = lo.x, b[nt][1] = lo.y, b[nt][2] = lo.z, b[nt][3] = lo.w;
@@ -569,7 +591,7 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
 template <typename T, int BLOCK, int NT, bool PAIR>
 __global__ void __launch_bounds__((kNC + 1) * 32, kMinCtas)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
-               int ntiles, int ksteps4, int xrows, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
+               int ntiles, int ksteps4, int xrows, int xmode, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int UNIT = RC::kUnit;
@@ -580,18 +602,23 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   uint64_t* empty = full + kMaxStages;
   int* flags = reinterpret_cast<int*>(empty + kMaxStages);
   unsigned char* buf = smem + 256;
-  float* red = reinterpret_cast<float*>(buf + (size_t)stages * kG * RC::kBytes);  // [2][kNC][NT][4][32]
+  // ring stage: kG records, then (xmode 2) the stage's k-range of the 8 NT activation rows,
+  // row-major with rows kXcStride bytes apart (bulk-copied beside the records)
+  const size_t rec_bytes = (size_t)kG * RC::kBytes;
+  const size_t stage_bytes = rec_bytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
+  float* red = reinterpret_cast<float*>(buf + (size_t)stages * stage_bytes);  // [2][kNC][NT][4][32]
   // staged activation rows (xrows > 0): xrows + 1 rows (the last one zero) of kpad halves,
   // 16 bytes apart in bank order so the 8 row groups of a fragment load use all 32 banks
   unsigned char* xs = reinterpret_cast<unsigned char*>(red + 2 * kNC * NT * 4 * 32);
   const int kpad = ksteps4 * 64;
   const int xstride = kpad * 2 + 16;
-  const bool stage_x = xrows > 0;
+  const bool stage_x = xmode == 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const RecSplit part{(int64_t)ntiles * ksteps4, (int)gridDim.x, ksteps4};
   const int64_t rbeg = part.beg(blockIdx.x), rend = part.beg(blockIdx.x + 1);
   const int m0 = blockIdx.y * 8 * NT;
+  const int vrows = min(8 * NT, M - m0);  // activation rows of this column chunk
   const int ksteps = K / 16;
 
   if (threadIdx.x == 0) {
@@ -619,8 +646,18 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         const int64_t tile_end = (r / ksteps4 + 1) * ksteps4;
         const int n = (int)lmin(kG, lmin(rend, tile_end) - r);
         const uint32_t bytes = (uint32_t)(n * RC::kBytes);
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(buf + (size_t)slot * kG * RC::kBytes, recs + (size_t)r * RC::kBytes, bytes, &full[slot]);
+        unsigned char* sbuf = buf + (size_t)slot * stage_bytes;
+        if (xmode == 2) {
+          // the activation rows of this stage's k-range (64 k per record), beside the records
+          const int kr = (int)(r - (r / ksteps4) * ksteps4);
+          mbar_arrive_expect_tx(&full[slot], bytes + (uint32_t)(vrows * n * 128));
+          for (int row = 0; row < vrows; ++row)
+            bulk_g2s(sbuf + rec_bytes + (size_t)row * kXcStride, A + (size_t)(m0 + row) * K + (size_t)kr * 64,
+                     (uint32_t)(n * 128), &full[slot]);
+        } else {
+          mbar_arrive_expect_tx(&full[slot], bytes);
+        }
+        bulk_g2s(sbuf, recs + (size_t)r * RC::kBytes, bytes, &full[slot]);
         r += n;
         if (++slot == stages) slot = 0, phase ^= 1;
       }
@@ -657,6 +694,14 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     } else {
       stage_prologue<T>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * kNC * NT * 4 * 32 - kNC, err);
     }
+    consumer_barrier();
+  } else if (xmode == 2 && vrows < 8 * NT) {
+    // rows without a token read zeros (the copies only ever write rows < vrows)
+    const int per_row = kXcStride / 16;
+    for (int s = 0; s < stages; ++s)
+      for (int i = threadIdx.x; i < (8 * NT - vrows) * per_row; i += kNC * 32)
+        *reinterpret_cast<uint4*>(buf + (size_t)s * stage_bytes + rec_bytes +
+                                  (size_t)(vrows + i / per_row) * kXcStride + (i % per_row) * 16) = make_uint4(0, 0, 0, 0);
     consumer_barrier();
   }
   const int g = lane >> 2, c = lane & 3;
@@ -695,8 +740,28 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     }
     const int nplan = min(kG, gend - ga);
     const int n = alive ? nplan : 0;
-    const size_t soff = (size_t)slot * kG * RC::kBytes;
-    if (stage_x && n == kG) {
+    const size_t soff = (size_t)slot * stage_bytes;
+    if (xmode == 2) {
+      // activation chunk of this stage: ldmatrix rows (token (lane / 16) * 8 + lane % 8, k half
+      // (lane / 8) % 2) of the unit's records
+      const uint32_t xc0 = smem_u32(buf + soff + rec_bytes) +
+                           (uint32_t)((((lane >> 4) * 8 + (lane & 7)) * kXcStride) + ((lane >> 3) & 1) * 16);
+#pragma unroll
+      for (int pu = 0; pu < PER; ++pu) {
+        const int q0 = (pu * kNC + warp) * UNIT;
+        const bool valid = q0 < n;
+        const int q = valid ? q0 : 0;
+        uint32_t live[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) live[nt] = valid ? 0xffffffffu : 0u;
+        const unsigned char* xp[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) xp[nt] = nullptr;
+        const unsigned char* r0 = buf + soff + (size_t)q * RC::kBytes;
+        mnb_unit<T, BLOCK, NT, 2, PAIR>(r0 + lane * 16, r0, xp, arow, live, 0, ksteps, g, kq, acc,
+                                        xc0 + (uint32_t)(q * 128));
+      }
+    } else if (stage_x && n == kG) {
       // full stage: every address is a per-stage base plus a compile-time offset
       const int xoff = (ga + warp * UNIT) * 128;
 #pragma unroll
@@ -705,7 +770,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         const unsigned char* xp[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) xp[nt] = xrow[nt] + xoff + qoff * 128;
-        mnb_unit<T, BLOCK, NT, true, PAIR>(wrec + soff + qoff * RC::kBytes, wparam + soff + qoff * RC::kBytes, xp,
+        mnb_unit<T, BLOCK, NT, 1, PAIR>(wrec + soff + qoff * RC::kBytes, wparam + soff + qoff * RC::kBytes, xp,
                                      arow, amask, 0, ksteps, g, kq, acc);
       }
     } else {
@@ -725,9 +790,9 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         }
         const unsigned char* r0 = buf + soff + (size_t)q * RC::kBytes;
         if (stage_x)
-          mnb_unit<T, BLOCK, NT, true, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
+          mnb_unit<T, BLOCK, NT, 1, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
         else
-          mnb_unit<T, BLOCK, NT, false, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
+          mnb_unit<T, BLOCK, NT, 0, PAIR>(r0 + lane * 16, r0, xp, arow, live, ga + q, ksteps, g, kq, acc);
       }
     }
     __syncwarp();
@@ -864,23 +929,31 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
   const int xrows = x_bytes <= kXStageMax && (a16 || pro.kind != kProNone) ? rows : 0;
   if (pro.kind != kProNone && !xrows) return cudaErrorInvalidValue;  // caller checks mnb_prologue_fits
+  // activation modes: 1 = all rows staged once per CTA; 2 = each stage's k-range bulk-copied beside
+  // its records (rows too long to stage whole, e.g. 16 rows at K 14336); 0 = read from global memory
+  const int xmode = xrows ? 1 : (a16 && p.K % 64 == 0 && p.ksteps4 * 64 == p.K) ? 2 : 0;
   auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR>;
   auto smem_for = [&](int stages) {
-    return 256 + (size_t)stages * kG * RC::kBytes + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
+    const size_t stage = (size_t)kG * RC::kBytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
+    return 256 + (size_t)stages * stage + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   };
-  static size_t configured = 0;  // per instantiation: the largest dynamic smem set so far
-  if (smem_for(kMaxStages) > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(kMaxStages));
-    if (e != cudaSuccess) return e;
-    configured = smem_for(kMaxStages);
-  }
-  // deepest ring that still leaves kMinCtas CTAs per SM (weights in flight per SM ~ kMinCtas x ring)
+  constexpr size_t kSmemCap = 232448;  // dynamic shared memory per CTA on sm_100
+  static size_t configured = 0;        // per instantiation: the largest dynamic smem set so far
+  auto configure = [&](size_t smem) -> cudaError_t {
+    if (smem <= configured) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) configured = smem;
+    return e;
+  };
+  // deepest ring that still leaves kMinCtas CTAs per SM (weights in flight per SM ~ kMinCtas x ring),
+  // else the deepest ring that fits one CTA
   static size_t occ_key[8] = {};
   static int occ_val[8] = {};
   auto per_sm_for = [&](size_t smem, int* out) -> cudaError_t {
     for (int i = 0; i < 8; ++i)
       if (occ_key[i] == smem) return (*out = occ_val[i]), cudaSuccess;
     int n = 0;
+    if (cudaError_t e = configure(smem)) return e;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kNC + 1) * 32, smem);
     if (e != cudaSuccess) return e;
     for (int i = 0; i < 8; ++i)
@@ -890,22 +963,28 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
       }
     return (*out = n), cudaSuccess;
   };
-  int stages = kMaxStages, per_sm = 0;
+  int stages = 0, per_sm = 0, fallback = 0, fallback_n = 0;
   for (int sg = kMaxStages; sg >= 2; --sg) {
+    if (smem_for(sg) > kSmemCap) continue;
     int n = 0;
     if (cudaError_t e = per_sm_for(smem_for(sg), &n)) return e;
-    if (sg == kMaxStages) per_sm = std::max(1, n);
+    if (n >= 1 && !fallback) fallback = sg, fallback_n = n;
     if (n >= kMinCtas) {
       stages = sg, per_sm = n;
       break;
     }
   }
+  if (!stages) {
+    if (!fallback) return cudaErrorInvalidValue;  // not even a 2-stage ring fits
+    stages = fallback, per_sm = fallback_n;
+  }
+  if (cudaError_t e = configure(smem_for(stages))) return e;
   const size_t smem = smem_for(stages);
   const unsigned gy = (unsigned)((M + 8 * NT - 1) / (8 * NT));
   const int64_t ctas = std::min<int64_t>(p.ntiles, (int64_t)per_sm * num_sms());
   return launch_k(kern, dim3((unsigned)ctas, gy), dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
-                  (int)p.ksteps4, xrows, 0u, stages, pro, oar, device_error_slot());
+                  (int)p.ksteps4, xrows, xmode, 0u, stages, pro, oar, device_error_slot());
 }
 
 template <typename T, int BLOCK>

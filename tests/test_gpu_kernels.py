@@ -396,7 +396,7 @@ def test_matmulnbits_prepacked_vs_oracle(ops, block, M, asym):
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (1, 14336, 4096), (1, 4096, 28672), (16, 4096, 4096),
                                    (512, 4096, 1024), (1, 1168, 96), (200, 1024, 18944), (300, 4096, 20480),
-                                   (1000, 256, 28672)])
+                                   (1000, 256, 28672), (16, 14336, 4096), (5, 14336, 200)])
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_matmulnbits_prepacked_llama_shapes(ops, M, K, N, dt):
     rng = np.random.default_rng(M + K * 3 + N)
@@ -412,6 +412,20 @@ def test_matmulnbits_prepacked_llama_shapes(ops, M, K, N, dt):
         packed = ops.matmulnbits_prepack(cuda(b), cuda(sb).view(torch.bfloat16), cuda(zp), K=K, N=N)
         got = ops.matmulnbits_prepacked(cuda(ab).view(torch.bfloat16), packed, K=K, N=N)
     np.testing.assert_allclose(got.float().cpu().numpy(), want, **TOL[dt])
+
+
+@pytest.mark.parametrize("block", [32, 64, 128])
+@pytest.mark.parametrize("M", [3, 12])
+def test_matmulnbits_prepacked_long_rows_stream_activation_chunks(ops, block, M):
+    """Rows too long to stage whole (M x K = 12 x 14336): each weight stage brings its k-range of
+    the activation rows by bulk copy; rows beyond M read zeros."""
+    rng = np.random.default_rng(block * 7 + M)
+    K, N = 14336, 72
+    a, b, s, zp = make_mnb(rng, M, K, N, block=block, dtype=np.float16)
+    packed = ops.matmulnbits_prepack(cuda(b), cuda(s), cuda(zp), K=K, N=N, block_size=block)
+    got = ops.matmulnbits_prepacked(cuda(a), packed, K=K, N=N, block_size=block).float().cpu().numpy()
+    want = oracle.matmulnbits(a, b, s, zp, N=N, K=K, block_size=block).astype(np.float32)
+    np.testing.assert_allclose(got, want, **TOL["f16"])
 
 
 def test_matmulnbits_prepacked_matches_ort_layout_kernel(ops):
