@@ -22,6 +22,10 @@
 //                      lanes; the four warps of a lane quarter split the columns) and store Y.
 // CTAs along x cover the M tiles of one W tile, so the W tile is read from HBM once and the other
 // M tiles find it in L2.  Every mbarrier wait is bounded (timeout -> device error word).
+// (A persistent stream-K form — one CTA per SM sharing the (tile, 64-k stage) units, cut tiles
+// summed from fp32 partials by their last contributor — measured slower on B200 at every prefill
+// shape tried: the per-piece epilogue serialises the TMEM accumulator and the weight slabs lose
+// their L2 reuse across concurrent CTAs.)
 #include <cuda.h>
 #include <cstdlib>
 
