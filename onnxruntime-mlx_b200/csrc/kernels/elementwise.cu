@@ -89,6 +89,44 @@ __global__ void gbq_kernel(const uint8_t* __restrict__ data, const T* __restrict
   }
 }
 
+// rows whose width is a multiple of 8 (and blocks of at least 8): one thread per 8 values — one
+// 4-byte load of nibbles, one scale and zero point, one 16-byte (fp16 / bf16) store; grid (rows,
+// dim / 2048)
+template <typename T, typename TI>
+__global__ void gbq8_kernel(const uint8_t* __restrict__ data, const T* __restrict__ scales,
+                            const uint8_t* __restrict__ zp, const TI* __restrict__ idx, T* __restrict__ out,
+                            int64_t n_idx, int64_t rows, int64_t dim, int block, DeviceErrorSlot* err) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t w = blockIdx.x;
+  const int64_t j0 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (w >= n_idx || j0 >= dim) return;
+  int64_t r = (int64_t)idx[w];
+  if (r < 0) r += rows;
+  if (r < 0 || r >= rows) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) report_device_error(err, 201, (int)w);
+    return;
+  }
+  const int64_t nblocks = dim / block;
+  const uint32_t q8 = *reinterpret_cast<const uint32_t*>(data + r * (dim / 2) + j0 / 2);
+  const int64_t blk = j0 / block;
+  int z = 8;
+  if (zp) {
+    const uint8_t zb = zp[r * ((nblocks + 1) / 2) + (blk >> 1)];
+    z = (blk & 1) ? (zb >> 4) : (zb & 0x0f);
+  }
+  const float sc = to_f<T>(scales[r * nblocks + blk]);
+  T v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = from_f<T>((float)((int)((q8 >> (4 * i)) & 15u) - z) * sc);
+  if constexpr (sizeof(T) == 2) {
+    *reinterpret_cast<uint4*>(out + w * dim + j0) = *reinterpret_cast<const uint4*>(v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[w * dim + j0 + i] = v[i];
+  }
+}
+
 namespace {
 int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
 
@@ -145,6 +183,21 @@ cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n
 
 cudaError_t launch_gather_block_quantized(const GbqArgs& a, cudaStream_t st) {
   if (a.n_idx == 0) return cudaSuccess;
+  const bool wide = a.dim % 8 == 0 && a.block % 8 == 0 && (reinterpret_cast<uintptr_t>(a.data) & 3) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && a.n_idx <= 65535 * 64;
+  if (wide) {
+    return by_dtype(a.dtype, [&](auto tag) {
+      using T = decltype(tag);
+      const dim3 grid((unsigned)a.n_idx, (unsigned)((a.dim / 8 + 255) / 256));
+      if (a.idx_dtype == kI64)
+        return launch_k(gbq8_kernel<T, int64_t>, grid, dim3(256), 0, st, a.data, static_cast<const T*>(a.scales),
+                        a.zp, static_cast<const int64_t*>(a.indices), static_cast<T*>(a.out), a.n_idx, a.rows,
+                        a.dim, a.block, a.err);
+      return launch_k(gbq8_kernel<T, int32_t>, grid, dim3(256), 0, st, a.data, static_cast<const T*>(a.scales),
+                      a.zp, static_cast<const int32_t*>(a.indices), static_cast<T*>(a.out), a.n_idx, a.rows, a.dim,
+                      a.block, a.err);
+    });
+  }
   const int blocks = (int)((a.n_idx * 32 + 255) / 256);
   return by_dtype(a.dtype, [&](auto tag) {
     using T = decltype(tag);

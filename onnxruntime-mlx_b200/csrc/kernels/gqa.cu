@@ -800,34 +800,53 @@ gqa_mma_decode_kernel(GqaKP kp) {
   float* scratch = reinterpret_cast<float*>(sm + L::kScratch) + warp * D;
   for (int i = threadIdx.x; i < (16 - kp.G) * L::kQStride; i += kMmaWarps * 32)
     Qs[kp.G * L::kQStride + i] = from_f<T>(0.f);
+  // the owner of the newest key appends it: rotated k and v into the KV buffer (and, below, into
+  // its streamed copy of that unit, which was read before the append).  Its k / v loads are issued
+  // together with the query loads, so the two round trips overlap.
+  const int u_new = nk > lo ? (nk - 1 - lo) / kUnit : -1;
+  const bool owner = ok && u_new >= u0 && u_new < u1;
+  T knew[D / 32], vnew[D / 32], kraw[D / 32];
+  const int64_t in_off = (int64_t)b * kp.kstride + (int64_t)kvh * D;
+  if (owner) {
+    const T* kin = static_cast<const T*>(kp.k);
+    const T* vin = static_cast<const T*>(kp.v);
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) {
+      kraw[e] = kin[in_off + kp.koff + lane + 32 * e];
+      vnew[e] = vin[in_off + kp.voff + lane + 32 * e];
+    }
+  }
   if (ok) {
     const T* qin = static_cast<const T*>(kp.q);
     for (int gq = warp; gq < kp.G; gq += kMmaWarps) {
       const T* src = qin + (int64_t)b * kp.qstride + (int64_t)(kvh * kp.G + gq) * D;
-      for (int i = lane; i < D; i += 32) scratch[i] = to_f<T>(src[i]);
+      // D / 32 consecutive values per lane in one load
+      if constexpr (D == 128) {
+        const uint2 w = *reinterpret_cast<const uint2*>(src + lane * 4);
+        const T* h = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) scratch[lane * 4 + e] = to_f<T>(h[e]);
+      } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + lane * 2);
+        const T* h = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) scratch[lane * 2 + e] = to_f<T>(h[e]);
+      }
       __syncwarp();
       rotate(scratch, kp.qn);
       for (int i = lane; i < D; i += 32) Qs[gq * L::kQStride + i] = from_f<T>(scratch[i]);
       __syncwarp();
     }
   }
-  // the owner of the newest key appends it: rotated k and v into the KV buffer (and, below, into
-  // its streamed copy of that unit, which was read before the append)
-  const int u_new = nk > lo ? (nk - 1 - lo) / kUnit : -1;
-  const bool owner = ok && u_new >= u0 && u_new < u1;
-  T knew[D / 32], vnew[D / 32];
   if (owner) {
-    const T* kin = static_cast<const T*>(kp.k);
-    const T* vin = static_cast<const T*>(kp.v);
-    const int64_t in_off = (int64_t)b * kp.kstride + (int64_t)kvh * D;
-    for (int i = lane; i < D; i += 32) scratch[i] = to_f<T>(kin[in_off + kp.koff + i]);
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) scratch[lane + 32 * e] = to_f<T>(kraw[e]);
     __syncwarp();
     rotate(scratch, kp.kn);
 #pragma unroll
     for (int e = 0; e < D / 32; ++e) {
       const int i = lane + 32 * e;
       knew[e] = from_f<T>(scratch[i]);
-      vnew[e] = vin[in_off + kp.voff + i];
       kvk[(int64_t)past * D + i] = knew[e];
       kvv[(int64_t)past * D + i] = vnew[e];
     }
