@@ -195,6 +195,11 @@ class Plan {
   PlanStats stats_;
   cudaStream_t stream_ = nullptr;
   cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr;
+  // repeated calls with the same boundary tensors (a decode loop): the signature (pointer,
+  // residency, shape of every boundary tensor) of the last call, its program and graph
+  std::vector<int64_t> last_sig_;
+  Program* last_prog_ = nullptr;
+  cudaGraphExec_t last_exec_ = nullptr;
   // host-side constant data used while lowering / fusing (weights before upload)
   std::map<int, std::shared_ptr<Initializer>> pending_consts_;
   // ONNXRUNTIME_EP_B200_PROFILE: per-step CUDA-event times of eager runs (no graph), printed on
