@@ -72,15 +72,24 @@ Node* node_at(b200ep_graph* g, int i) {
   return &g->g.nodes[i];
 }
 
+void fill_args(const b200ep_tensor* t, size_t n, std::vector<TensorArg>& v);
+
 std::vector<TensorArg> to_args(const b200ep_tensor* t, size_t n) {
   std::vector<TensorArg> v(n);
+  fill_args(t, n, v);
+  return v;
+}
+
+// the same into a caller-kept vector whose shape buffers are reused (no allocation per call in a
+// decode loop)
+void fill_args(const b200ep_tensor* t, size_t n, std::vector<TensorArg>& v) {
+  v.resize(n);
   for (size_t i = 0; i < n; ++i) {
     v[i].data = t[i].data;
     v[i].dtype = t[i].dtype;
-    v[i].shape = dims_of(t[i].rank, t[i].dims);
+    v[i].shape.assign(t[i].dims, t[i].dims + std::max(0, (int)t[i].rank));
     v[i].on_device = t[i].on_device != 0;
   }
-  return v;
 }
 
 bool truthy(const char* v) { return v && *v && strcmp(v, "0") != 0 && strcmp(v, "false") != 0; }
@@ -375,7 +384,10 @@ B200EP_API int b200ep_compiled_run(b200ep_compiled* c, const b200ep_tensor* inpu
   GUARD_BEGIN
   B200EP_CHECK_ARG(c && (n_inputs == 0 || inputs) && (n_outputs == 0 || outputs), "null argument");
   B200EP_CUDA_RET(cudaSetDevice(c->device));
-  return c->plan->run(to_args(inputs, n_inputs), to_args(outputs, n_outputs), static_cast<cudaStream_t>(stream));
+  static thread_local std::vector<TensorArg> ins, outs;
+  fill_args(inputs, n_inputs, ins);
+  fill_args(outputs, n_outputs, outs);
+  return c->plan->run(ins, outs, static_cast<cudaStream_t>(stream));
   GUARD_END
 }
 
