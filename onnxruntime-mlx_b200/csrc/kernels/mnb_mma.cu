@@ -257,8 +257,9 @@ struct RecSplit {
   __device__ __forceinline__ int64_t beg(int c) const { return c >= G ? R : ((R / ks) * c / G) * ks; }
 };
 
+template <int NC>
 __device__ __forceinline__ void consumer_barrier() {
-  asm volatile("bar.sync 1, %0;" ::"r"(kNC * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
 }
 
 template <int N>
@@ -356,10 +357,10 @@ __device__ __forceinline__ void ar_sum8(const MnbAr& ar, unsigned epoch, size_t 
 // (skip) RMS norm as in rms_norm_kernel — fp32 sum of squares of the (unrounded) row, y =
 // (t * inv) * gamma rounded once; the skip form writes the rounded sum t to pro.residual from the
 // CTAs of column 0 (blockIdx.x == 0).  wsum: kNC floats of scratch for the per-warp partials.
-template <typename T>
+template <typename T, int NC>
 __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride, int kpad, int xrows, int m0,
                                int M, int K, float* wsum, DeviceErrorSlot* err) {
-  const int tid = threadIdx.x, nthr = kNC * 32;
+  const int tid = threadIdx.x, nthr = NC * 32;
   const int cpr = kpad / 8;
   // zero row (index xrows) for lanes without a token
   for (int kc = tid; kc < cpr; kc += nthr) xs_put(xs + (size_t)xrows * xstride, kc * 8, make_uint4(0, 0, 0, 0));
@@ -391,7 +392,7 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
   if (from_ar) {
     epoch = __ldcg(pro.ar.ctrs);
     ar_wait(pro.ar, epoch, err);
-    consumer_barrier();
+    consumer_barrier<NC>();
   }
   auto load_x = [&](int m, int k, float (&t)[8]) {
     if (from_ar)
@@ -427,10 +428,10 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
       }
       ss = warp_sum(ss);
       if ((tid & 31) == 0) wsum[tid >> 5] = ss;
-      consumer_barrier();
+      consumer_barrier<NC>();
       float tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < kNC; ++w) tot += wsum[w];
+      for (int w = 0; w < NC; ++w) tot += wsum[w];
       const float inv = rsqrtf(tot / (float)K + pro.eps);
 #pragma unroll
       for (int j = 0; j < kCh; ++j) {
@@ -442,7 +443,7 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
           xs_put(xs + (size_t)r * xstride, k, pack8<T>(y));
         }
       }
-      consumer_barrier();  // wsum is reused by the next row
+      consumer_barrier<NC>();  // wsum is reused by the next row
       continue;
     }
     float ss = 0.f;
@@ -461,10 +462,10 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) wsum[tid >> 5] = ss;
-    consumer_barrier();
+    consumer_barrier<NC>();
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kNC; ++w) tot += wsum[w];
+    for (int w = 0; w < NC; ++w) tot += wsum[w];
     const float inv = rsqrtf(tot / (float)K + pro.eps);
     for (int kc = tid; kc < cpr; kc += nthr) {
       const int k = kc * 8;
@@ -484,7 +485,7 @@ __device__ void stage_prologue(const MnbPro& pro, unsigned char* xs, int xstride
       }
       xs_put(xs + (size_t)r * xstride, k, pack8<T>(y));
     }
-    consumer_barrier();  // wsum is reused by the next row
+    consumer_barrier<NC>();  // wsum is reused by the next row
   }
 }
 
@@ -588,15 +589,15 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
   }
 }
 
-template <typename T, int BLOCK, int NT, bool PAIR>
-__global__ void __launch_bounds__((kNC + 1) * 32, kMinCtas)
+template <typename T, int BLOCK, int NT, bool PAIR, int NC>
+__global__ void __launch_bounds__((NC + 1) * 32, NC > kNC ? 1 : kMinCtas)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
                int ntiles, int ksteps4, int xrows, int xmode, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int UNIT = RC::kUnit;
-  constexpr int PER = kG / (kNC * UNIT);   // units per warp per full stage
-  static_assert(kG % (kNC * UNIT) == 0, "stage must split evenly");
+  constexpr int PER = kG / (NC * UNIT);   // units per warp per full stage
+  static_assert(kG % (NC * UNIT) == 0, "stage must split evenly");
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
@@ -606,10 +607,10 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   // row-major with rows kXcStride bytes apart (bulk-copied beside the records)
   const size_t rec_bytes = (size_t)kG * RC::kBytes;
   const size_t stage_bytes = rec_bytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
-  float* red = reinterpret_cast<float*>(buf + (size_t)stages * stage_bytes);  // [2][kNC][NT][4][32]
+  float* red = reinterpret_cast<float*>(buf + (size_t)stages * stage_bytes);  // [2][NC][NT][4][32]
   // staged activation rows (xrows > 0): xrows + 1 rows (the last one zero) of kpad halves,
   // 16 bytes apart in bank order so the 8 row groups of a fragment load use all 32 banks
-  unsigned char* xs = reinterpret_cast<unsigned char*>(red + 2 * kNC * NT * 4 * 32);
+  unsigned char* xs = reinterpret_cast<unsigned char*>(red + 2 * NC * NT * 4 * 32);
   const int kpad = ksteps4 * 64;
   const int xstride = kpad * 2 + 16;
   const bool stage_x = xmode == 1;
@@ -625,14 +626,14 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     flags[0] = 0;
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kNC);
+      mbar_init(&empty[s], NC);
     }
     fence_mbarrier_init();
   }
   __syncthreads();
   // the weight stream reads constants only and starts at once; the consumers wait for the previous
   // kernel before they read activations or write outputs
-  if (warp == kNC) {
+  if (warp == NC) {
     if (lane == 0) {
       // the CTA's records in stages of at most kG that never cross a tile boundary
       int slot = 0;
@@ -675,11 +676,11 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
       const int cpr = kpad / 8;  // 16-byte chunks per row
       const int chunks = (xrows + 1) * cpr;
-      for (int base = threadIdx.x; base < chunks; base += 4 * kNC * 32) {
+      for (int base = threadIdx.x; base < chunks; base += 4 * NC * 32) {
         uint4 v[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int idx = base + u * kNC * 32;
+          const int idx = base + u * NC * 32;
           const int r = idx / cpr, k = (idx - r * cpr) * 8;
           const int m = m0 + r;
           v[u] = make_uint4(0, 0, 0, 0);
@@ -687,22 +688,22 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int idx = base + u * kNC * 32;
+          const int idx = base + u * NC * 32;
           if (idx < chunks) xs_put(xs + (size_t)(idx / cpr) * xstride, (idx % cpr) * 8, v[u]);
         }
       }
     } else {
-      stage_prologue<T>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * kNC * NT * 4 * 32 - kNC, err);
+      stage_prologue<T, NC>(pro, xs, xstride, kpad, xrows, m0, M, K, red + 2 * NC * NT * 4 * 32 - NC, err);
     }
-    consumer_barrier();
+    consumer_barrier<NC>();
   } else if (xmode == 2 && vrows < 8 * NT) {
     // rows without a token read zeros (the copies only ever write rows < vrows)
     const int per_row = kXcStride / 16;
     for (int s = 0; s < stages; ++s)
-      for (int i = threadIdx.x; i < (8 * NT - vrows) * per_row; i += kNC * 32)
+      for (int i = threadIdx.x; i < (8 * NT - vrows) * per_row; i += NC * 32)
         *reinterpret_cast<uint4*>(buf + (size_t)s * stage_bytes + rec_bytes +
                                   (size_t)(vrows + i / per_row) * kXcStride + (i % per_row) * 16) = make_uint4(0, 0, 0, 0);
-    consumer_barrier();
+    consumer_barrier<NC>();
   }
   const int g = lane >> 2, c = lane & 3;
   const unsigned char* xrow[NT];
@@ -748,7 +749,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
                            (uint32_t)((((lane >> 4) * 8 + (lane & 7)) * kXcStride) + ((lane >> 3) & 1) * 16);
 #pragma unroll
       for (int pu = 0; pu < PER; ++pu) {
-        const int q0 = (pu * kNC + warp) * UNIT;
+        const int q0 = (pu * NC + warp) * UNIT;
         const bool valid = q0 < n;
         const int q = valid ? q0 : 0;
         uint32_t live[NT];
@@ -766,7 +767,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       const int xoff = (ga + warp * UNIT) * 128;
 #pragma unroll
       for (int pu = 0; pu < PER; ++pu) {
-        const int qoff = pu * kNC * UNIT;
+        const int qoff = pu * NC * UNIT;
         const unsigned char* xp[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) xp[nt] = xrow[nt] + xoff + qoff * 128;
@@ -778,7 +779,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       // stage's first unit against zero activations (finite parameters, contribution exactly 0)
 #pragma unroll
       for (int pu = 0; pu < PER; ++pu) {
-        const int q0 = (pu * kNC + warp) * UNIT;
+        const int q0 = (pu * NC + warp) * UNIT;
         const bool valid = q0 < n;
         const int q = valid ? q0 : 0;
         const unsigned char* xp[NT];
@@ -809,7 +810,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       // thread-block clusters with cut tiles summed through distributed shared memory — a
       // cluster launches only when a GPC frees enough slots at once, defeating the overlap with
       // the previous kernel.)
-      float* rb = red + (size_t)(tp & 1) * kNC * NT * 4 * 32;
+      float* rb = red + (size_t)(tp & 1) * NC * NT * 4 * 32;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -817,8 +818,8 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           if (PAIR || !(e & 1)) rb[((warp * NT + nt) * 4 + e) * 32 + lane] = acc[nt][e];
           acc[nt][e] = 0.f;
         }
-      consumer_barrier();
-      for (int tid = threadIdx.x; tid < 256; tid += kNC * 32) {
+      consumer_barrier<NC>();
+      for (int tid = threadIdx.x; tid < 256; tid += NC * 32) {
         const int row = tid >> 4, col = tid & 15;
         const int m = m0 + col, n = t * 16 + row;
         if (col < 8 * NT && m < M && n < N) {
@@ -827,7 +828,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           const int ln = (row & 7) * 4 + (cc >> 1);
           float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < kNC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
+          for (int w = 0; w < NC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
           Y[(size_t)m * N + n] = from_f<T>(v);
         }
       }
@@ -843,9 +844,9 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
     // CTA's writes are visible) into slot `rank` of every rank's mailbox with 16-byte stores,
     // fences them at system scope, bumps the epoch and releases the flags
     __threadfence();
-    consumer_barrier();
+    consumer_barrier<NC>();
     if (threadIdx.x == 0) flags[1] = atomicAdd(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1;
-    consumer_barrier();
+    consumer_barrier<NC>();
     if (flags[1]) {
       __threadfence();
       const size_t bytes = (size_t)M * N * sizeof(T);  // multiple of 16 (N % 8 == 0)
@@ -853,10 +854,10 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       const uint4* src = reinterpret_cast<const uint4*>(Y);
       for (int d = 0; d < oar.world; ++d) {
         uint4* dst = reinterpret_cast<uint4*>(oar.mbox[d] + off);
-        for (size_t i = threadIdx.x; i < bytes / 16; i += kNC * 32) dst[i] = __ldcg(src + i);
+        for (size_t i = threadIdx.x; i < bytes / 16; i += NC * 32) dst[i] = __ldcg(src + i);
       }
       __threadfence_system();
-      consumer_barrier();
+      consumer_barrier<NC>();
       if (threadIdx.x == 0) {
         oar.ctrs[1] = 0;
         oar.ctrs[0] = oepoch;
@@ -932,10 +933,13 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   // activation modes: 1 = all rows staged once per CTA; 2 = each stage's k-range bulk-copied beside
   // its records (rows too long to stage whole, e.g. 16 rows at K 14336); 0 = read from global memory
   const int xmode = xrows ? 1 : (a16 && p.K % 64 == 0 && p.ksteps4 * 64 == p.K) ? 2 : 0;
-  auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR>;
+  // 16-token chunks stage 16 activation rows: one CTA per SM, so it gets twice the consumer warps
+  constexpr int NC = NT == 2 ? 2 * kNC : kNC;
+  constexpr int kMinC = NC > kNC ? 1 : kMinCtas;
+  auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR, NC>;
   auto smem_for = [&](int stages) {
     const size_t stage = (size_t)kG * RC::kBytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
-    return 256 + (size_t)stages * stage + (size_t)2 * kNC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
+    return 256 + (size_t)stages * stage + (size_t)2 * NC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   };
   constexpr size_t kSmemCap = 232448;  // dynamic shared memory per CTA on sm_100
   static size_t configured = 0;        // per instantiation: the largest dynamic smem set so far
@@ -954,7 +958,7 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
       if (occ_key[i] == smem) return (*out = occ_val[i]), cudaSuccess;
     int n = 0;
     if (cudaError_t e = configure(smem)) return e;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (kNC + 1) * 32, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, (NC + 1) * 32, smem);
     if (e != cudaSuccess) return e;
     for (int i = 0; i < 8; ++i)
       if (!occ_key[i]) {
@@ -969,7 +973,7 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
     int n = 0;
     if (cudaError_t e = per_sm_for(smem_for(sg), &n)) return e;
     if (n >= 1 && !fallback) fallback = sg, fallback_n = n;
-    if (n >= kMinCtas) {
+    if (n >= kMinC) {
       stages = sg, per_sm = n;
       break;
     }
@@ -982,7 +986,7 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   const size_t smem = smem_for(stages);
   const unsigned gy = (unsigned)((M + 8 * NT - 1) / (8 * NT));
   const int64_t ctas = std::min<int64_t>(p.ntiles, (int64_t)per_sm * num_sms());
-  return launch_k(kern, dim3((unsigned)ctas, gy), dim3((kNC + 1) * 32), smem, st, static_cast<const T*>(A),
+  return launch_k(kern, dim3((unsigned)ctas, gy), dim3((NC + 1) * 32), smem, st, static_cast<const T*>(A),
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
                   (int)p.ksteps4, xrows, xmode, 0u, stages, pro, oar, device_error_slot());
 }
