@@ -330,6 +330,64 @@ def gqa_kernel_timing(batch, ctx, peaks, peak_kind, reps=5):
             "frac": round(alg / launch_s / 1e9 / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
 
 
+def paged_kernel_timing(batch, ctx, peaks, peak_kind, reps=5, block=16):
+    """PagedAttention decode alone (32 q / 8 kv heads, head 128, fp16, 16-row blocks scattered by a
+    random block table): each sequence appends one token after ctx - 1 cached ones.  CUDA-event
+    timing of the append + attention launches over rotating cache pairs larger than L2, replayed
+    from a CUDA graph.  Algorithmic bytes: the K and V rows read plus q / k / v / out."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    H, HK, D = 32, 8, 128
+    nblk = (ctx + block - 1) // block
+    nb = batch * nblk
+    per = 2 * nb * block * HK * D * 2
+    copies = max(2, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    caches = [(torch.randn(nb, block, HK, D, device="cuda", generator=g).half(),
+               torch.randn(nb, block, HK, D, device="cuda", generator=g).half()) for _ in range(copies)]
+    bt = torch.randperm(nb, device="cuda", generator=g).to(torch.int32).reshape(batch, nblk)
+    q = torch.randn(batch, H * D, device="cuda", generator=g).half()
+    k = torch.randn(batch, HK * D, device="cuda", generator=g).half()
+    v = torch.randn(batch, HK * D, device="cuda", generator=g).half()
+    cum = torch.arange(batch + 1, dtype=torch.int32, device="cuda")
+    past = torch.full((batch,), ctx - 1, dtype=torch.int32, device="cuda")
+    ang = torch.arange(ctx + 8, device="cuda", dtype=torch.float64)[:, None] / (
+        10000.0 ** (torch.arange(D // 2, device="cuda", dtype=torch.float64) / (D // 2)))[None, :]
+    cos, sin = ang.cos().half(), ang.sin().half()
+    out = torch.empty(batch, H * D, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+
+    def step(i):
+        ops.paged_attention(q, k, v, caches[i][0], caches[i][1], cum, past, bt, cos, sin, num_heads=H,
+                            kv_heads=HK, out=out)
+
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            step(i)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                step(i)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    alg = 2 * batch * HK * ctx * D * 2 + (q.numel() + k.numel() + v.numel() + out.numel()) * 2
+    peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
+    return {"kernel": "paged_append_kernel + paged_attn_kernel", "batch": batch, "context": ctx, "block": block,
+            "launch_us": round(launch_s * 1e6, 2), "algorithmic_bytes_per_launch": alg,
+            "achieved": round(alg / launch_s / 1e9, 1), "unit": "GB/s", "frac": round(alg / launch_s / 1e9 / peak, 4),
+            "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
+
+
 def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
     """GroupQueryAttention over a whole prompt (32 q / 8 kv heads, head 128, fp16, past 0): the
     rotate-and-append kernel plus the tensor-core prefill kernel, CUDA-event timed over graph
@@ -668,9 +726,10 @@ def main():
                     help="N > 1: data-parallel replicas (default, weak scaling) or one tensor-parallel model")
     ap.add_argument("--no-tp-leg", action="store_true",
                     help="N > 1 with --parallel dp: skip the tensor-parallel measurement reported beside it")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm"],
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm", "paged"],
                     help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
-                         "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes); "
+                         "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes; "
+                         "paged: PagedAttention decode); "
                          "used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -696,6 +755,9 @@ def main():
                 print(json.dumps(gqa_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
             for S in (512, 1024, 4096):
                 print(json.dumps(gqa_prefill_timing(S, peaks, peak_kind)), flush=True)
+        elif args.kernel_only == "paged":
+            for b, ctx in ((1, 1024), (8, 1024), (8, 8192), (32, 2048)):
+                print(json.dumps(paged_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "gemm":
             for name, m, k, n in GEMM_SHAPES:
                 print(json.dumps(gemm_kernel_timing(name, m, k, n, peaks, peak_kind)), flush=True)

@@ -174,6 +174,35 @@ B200EP_API int b200ep_group_query_attention_noalloc(
     void* out, int dtype, void* stream);
 B200EP_API size_t b200ep_gqa_noalloc_max_workspace(void);
 
+/* PagedAttention (com.microsoft; reference: paged_attention_op, rust/src/ops/attention.rs:2495-2746,
+ * claim 2748-2900).  Tokens of `batch` sequences are packed row after row: sequence b owns query /
+ * key / value rows [cumulative_seqlens[b], cumulative_seqlens[b + 1]) and continues after
+ * past_seqlens[b] cached tokens.  Its logical position p lives in physical block
+ * block_table[b * max_blocks + p / block_size] at row p % block_size of the caches
+ * [num_blocks, block_size, kv_heads, head_size].  The new k (RoPE'd at positions past_b + j when
+ * do_rotary) and v rows are written into their slots in place; query row j attends keys
+ * 0 .. past_b + j causally (fp32 softmax, scale = attr or 1/sqrt(head_size)) and writes
+ * out[num_tokens, num_heads * head_size].  Rotated q and k are rounded to the I/O dtype, as the
+ * reference computes RoPE in that dtype.  The control tensors are read on the device; a slot
+ * outside the caches or the block table, or a position outside the cos/sin rows, skips that
+ * write (its output row is zeros) and sets the device error word.  fp16 / bf16, head_size 64 or
+ * 128; separate K / V caches (the LATENT layout, slot_mapping, head_sink and q/k norms are
+ * declined by the claim). */
+typedef struct b200ep_paged_params {
+  int32_t batch;       /* sequences: cumulative_seqlens has batch + 1 entries */
+  int32_t num_tokens;  /* packed rows (= cumulative_seqlens[batch]) */
+  int32_t num_heads, kv_heads, head_size;
+  int32_t num_blocks, block_size, max_blocks; /* caches' blocks, rows per block; block_table row */
+  int32_t max_seq, rotary_half;               /* cos/sin cache rows and columns (do_rotary) */
+  int32_t do_rotary, interleaved;
+  float scale;                                /* 0: 1/sqrt(head_size) */
+} b200ep_paged_params;
+B200EP_API int b200ep_paged_attention(const b200ep_paged_params* p, const void* query, const void* key,
+                                      const void* value, void* key_cache, void* value_cache,
+                                      const int32_t* cumulative_seqlens, const int32_t* past_seqlens,
+                                      const int32_t* block_table, const void* cos_cache,
+                                      const void* sin_cache, void* out, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

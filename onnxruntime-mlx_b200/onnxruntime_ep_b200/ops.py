@@ -25,6 +25,16 @@ class GqaParams(ctypes.Structure):
     ]
 
 
+class PagedParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("num_tokens", ctypes.c_int32), ("num_heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32), ("head_size", ctypes.c_int32), ("num_blocks", ctypes.c_int32),
+        ("block_size", ctypes.c_int32), ("max_blocks", ctypes.c_int32), ("max_seq", ctypes.c_int32),
+        ("rotary_half", ctypes.c_int32), ("do_rotary", ctypes.c_int32), ("interleaved", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+    ]
+
+
 _configured = False
 
 
@@ -45,6 +55,7 @@ def _lib():
         L.b200ep_matmulnbits_prepack.argtypes = [vp, vp, vp, i32, i64, i64, i32, i32, vp, vp]
         L.b200ep_matmulnbits_prepacked.argtypes = [vp, vp, vp, i32, i64, i64, i64, i32, i32, vp]
         L.b200ep_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), i32]
+        L.b200ep_paged_attention.argtypes = [ctypes.POINTER(PagedParams)] + [vp] * 11 + [i32, vp]
         _configured = True
     return L
 
@@ -178,3 +189,29 @@ def group_query_attention(query, key, value, kv_key, kv_value, seqlens_k, cos_ca
 
 def gqa_workspace_size(**kw) -> int:
     return int(_lib().b200ep_gqa_workspace_size(ctypes.byref(gqa_params(**kw))))
+
+
+def paged_attention(query, key, value, key_cache, value_cache, cumulative_seqlens, past_seqlens, block_table,
+                    cos_cache=None, sin_cache=None, *, num_heads, kv_heads, scale=0.0, interleaved=0, out=None):
+    """com.microsoft PagedAttention: packed rows [num_tokens, H*D]; caches [num_blocks, block_size, HK, D]
+    updated in place; control tensors int32 on the device."""
+    import torch
+
+    T, W = query.shape
+    D = W // num_heads
+    batch = cumulative_seqlens.numel() - 1
+    p = PagedParams()
+    p.batch, p.num_tokens, p.num_heads, p.kv_heads, p.head_size = batch, T, num_heads, kv_heads, D
+    p.num_blocks, p.block_size = key_cache.shape[0], key_cache.shape[1]
+    p.max_blocks = block_table.numel() // batch
+    p.do_rotary = int(cos_cache is not None)
+    p.max_seq = 0 if cos_cache is None else cos_cache.shape[0]
+    p.rotary_half = 0 if cos_cache is None else cos_cache.shape[1]
+    p.interleaved, p.scale = int(interleaved), float(scale)
+    if out is None:
+        out = torch.empty(T, num_heads * D, dtype=query.dtype, device=query.device)
+    check(_lib().b200ep_paged_attention(
+        ctypes.byref(p), _p(query), _p(key), _p(value), _p(key_cache), _p(value_cache), _p(cumulative_seqlens),
+        _p(past_seqlens), _p(block_table), _p(cos_cache), _p(sin_cache), _p(out), _dt(query),
+        _stream(query.device)))
+    return out

@@ -9,6 +9,7 @@
  *   - com.microsoft GroupQueryAttention  (rust/src/ops/attention.rs:556-952)
  *   - SimplifiedLayerNormalization / RMSNormalization /
  *     SkipSimplifiedLayerNormalization    (rust/src/ops/norm.rs:163-246)
+ *   - com.microsoft PagedAttention       (rust/src/ops/attention.rs:2495-2746)
  *
  * It is the checker for the CUDA kernels (tests, smoke(), and the timed CPU
  * baseline of bench.py).  The product library never links or calls it.
@@ -449,6 +450,117 @@ int oracle_gqa(const oracle_gqa_params* p, const void* q, const void* k, const v
         }
         free(sc);
       }
+  free(qr);
+  return OR_OK;
+}
+
+/* ---- PagedAttention (com.microsoft) ---------------------------------------
+ * paged_attention_op, attention.rs:2495-2746 (SEPARATE K / V caches, no
+ * slot_mapping / head_sink / q-k norm, rotary_offset 0):
+ *   sequence b owns packed rows [cum[b], cum[b+1]) and follows past[b] cached
+ *   tokens; row j sits at position p = past[b] + j (2588-2596);
+ *   RoPE of the new q and k at those positions, in the I/O dtype (2619-2624);
+ *   the new k / v rows are scattered into physical block bt[b][p / bs], row
+ *   p % bs of the caches [num_blocks, bs, kv_heads, D] (2632-2675);
+ *   keys 0 .. past[b]-1 are gathered from the cache through the block table and
+ *   the new rows appended (2678-2700); query j attends keys <= past[b] + j with
+ *   an fp32 softmax (causal_mask_topleft with offset past, 2703-2711);
+ *   scale = attr or 1/sqrt(D) (attr_scale).  Output [num_tokens, H * D].
+ * Rotated q / k are rounded to the I/O dtype before use. */
+typedef struct {
+  int64_t batch, num_tokens, num_heads, kv_heads, head_size;
+  int64_t num_blocks, block_size, max_blocks;
+  int64_t max_seq, rotary_half;
+  int32_t do_rotary, interleaved;
+  float scale;
+} oracle_paged_params;
+
+static int64_t paged_slot(const oracle_paged_params* p, const int32_t* bt, int64_t b, int64_t pos) {
+  int64_t blk = pos / p->block_size;
+  if (pos < 0 || blk >= p->max_blocks) return -1;
+  int64_t phys = bt[b * p->max_blocks + blk];
+  if (phys < 0 || phys >= p->num_blocks) return -1;
+  return phys * p->block_size + pos % p->block_size;
+}
+
+int oracle_paged_attention(const oracle_paged_params* p, const void* q, const void* k,
+                           const void* v, void* kc, void* vc, const int32_t* cum,
+                           const int32_t* past, const int32_t* bt, const void* cos_c,
+                           const void* sin_c, void* out, int dt, int nthreads) {
+  if (!p || !q || !k || !v || !kc || !vc || !cum || !past || !bt || !out || !is_float_dt(dt))
+    return OR_EINVAL;
+  const int64_t B = p->batch, T = p->num_tokens, H = p->num_heads, HK = p->kv_heads,
+                D = p->head_size;
+  if (B <= 0 || T < 0 || H <= 0 || HK <= 0 || D <= 0 || D > 1024 || H % HK) return OR_EINVAL;
+  if (p->block_size <= 0 || p->num_blocks <= 0 || p->max_blocks <= 0) return OR_EINVAL;
+  if (p->do_rotary && (!cos_c || !sin_c || p->rotary_half <= 0 || 2 * p->rotary_half > D))
+    return OR_EINVAL;
+  if (cum[0] != 0 || cum[B] != T) return OR_EINVAL;
+  for (int64_t b = 0; b < B; ++b) {
+    if (cum[b + 1] < cum[b] || past[b] < 0) return OR_EINVAL;
+    int64_t total = (int64_t)past[b] + (cum[b + 1] - cum[b]);
+    for (int64_t pos = 0; pos < total; ++pos)
+      if (paged_slot(p, bt, b, pos) < 0) return OR_ERANGE;
+    if (p->do_rotary && cum[b + 1] > cum[b] && total > p->max_seq) return OR_ERANGE;
+  }
+  const int64_t G = H / HK, row = HK * D;
+  const float scale = p->scale != 0.0f ? p->scale : (float)(1.0 / sqrt((double)D));
+
+  /* 1. rotate q into scratch; rotate k and scatter k / v into the caches. */
+  float* qr = (float*)malloc((size_t)((T > 0 ? T : 1) * H * D) * sizeof(float));
+  if (!qr) return OR_EINVAL;
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t t = cum[b]; t < cum[b + 1]; ++t) {
+      int64_t pos = (int64_t)past[b] + (t - cum[b]);
+      float vec[1024];
+      for (int64_t h = 0; h < H; ++h) {
+        for (int64_t i = 0; i < D; ++i) vec[i] = load_f(q, t * H * D + h * D + i, dt);
+        if (p->do_rotary) rope_vec(vec, D, p->rotary_half, pos, cos_c, sin_c, dt, p->interleaved);
+        for (int64_t i = 0; i < D; ++i) qr[(t * H + h) * D + i] = round_to(vec[i], dt);
+      }
+      int64_t slot = paged_slot(p, bt, b, pos);
+      for (int64_t h = 0; h < HK; ++h) {
+        for (int64_t i = 0; i < D; ++i) vec[i] = load_f(k, t * row + h * D + i, dt);
+        if (p->do_rotary) rope_vec(vec, D, p->rotary_half, pos, cos_c, sin_c, dt, p->interleaved);
+        for (int64_t i = 0; i < D; ++i) {
+          store_f(kc, slot * row + h * D + i, dt, vec[i]);
+          store_f(vc, slot * row + h * D + i, dt, load_f(v, t * row + h * D + i, dt));
+        }
+      }
+    }
+
+  /* 2. causal attention of every packed row over its sequence's keys. */
+  set_threads(nthreads);
+#pragma omp parallel for schedule(dynamic) collapse(2)
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t h = 0; h < H; ++h) {
+      int64_t b = 0;
+      while (b + 1 < B && cum[b + 1] <= t) ++b;
+      int64_t qpos = (int64_t)past[b] + (t - cum[b]);
+      int64_t hk = h / G, n = qpos + 1;
+      double* sc = (double*)malloc((size_t)n * sizeof(double));
+      const float* qv = qr + (t * H + h) * D;
+      double mx = -INFINITY;
+      for (int64_t j = 0; j < n; ++j) {
+        int64_t slot = paged_slot(p, bt, b, j);
+        double dot = 0.0;
+        for (int64_t i = 0; i < D; ++i) dot += (double)qv[i] * load_f(kc, slot * row + hk * D + i, dt);
+        sc[j] = dot * (double)scale;
+        if (sc[j] > mx) mx = sc[j];
+      }
+      double den = 0.0;
+      for (int64_t j = 0; j < n; ++j) {
+        sc[j] = exp(sc[j] - mx);
+        den += sc[j];
+      }
+      for (int64_t i = 0; i < D; ++i) {
+        double acc = 0.0;
+        for (int64_t j = 0; j < n; ++j)
+          acc += sc[j] * load_f(vc, paged_slot(p, bt, b, j) * row + hk * D + i, dt);
+        store_f(out, (t * H + h) * D + i, dt, acc / den);
+      }
+      free(sc);
+    }
   free(qr);
   return OR_OK;
 }

@@ -241,6 +241,56 @@ def gqa(query, key, value, past_key, past_value, seqlens_k, cos_cache=None, sin_
     return out, pk, pv
 
 
+class PagedParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int64),
+        ("num_heads", ctypes.c_int64),
+        ("kv_heads", ctypes.c_int64),
+        ("head_size", ctypes.c_int64),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int64),
+        ("max_blocks", ctypes.c_int64),
+        ("max_seq", ctypes.c_int64),
+        ("rotary_half", ctypes.c_int64),
+        ("do_rotary", ctypes.c_int32),
+        ("interleaved", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+    ]
+
+
+def paged_attention(query, key, value, key_cache, value_cache, cum_seqlens, past_seqlens, block_table,
+                    cos_cache=None, sin_cache=None, *, num_heads, kv_heads, scale=0.0, interleaved=0,
+                    dtype=None, threads=0):
+    """PagedAttention with the reference's semantics (attention.rs:2495-2746).
+
+    Returns (output [num_tokens, H*D], key_cache, value_cache); the caches are copies with the
+    new rows scattered in.
+    """
+    query = np.ascontiguousarray(query)
+    code = _dtype_code(query, dtype)
+    T, width = query.shape
+    D = width // num_heads
+    kc, vc = np.array(key_cache, copy=True, order="C"), np.array(value_cache, copy=True, order="C")
+    cum = np.ascontiguousarray(cum_seqlens, dtype=np.int32)
+    past = np.ascontiguousarray(past_seqlens, dtype=np.int32)
+    bt = np.ascontiguousarray(block_table, dtype=np.int32)
+    p = PagedParams()
+    p.batch, p.num_tokens, p.num_heads, p.kv_heads, p.head_size = len(cum) - 1, T, num_heads, kv_heads, D
+    p.num_blocks, p.block_size, p.max_blocks = kc.shape[0], kc.shape[1], bt.size // (len(cum) - 1)
+    p.do_rotary = int(cos_cache is not None)
+    p.max_seq = 0 if cos_cache is None else cos_cache.shape[0]
+    p.rotary_half = 0 if cos_cache is None else cos_cache.shape[1]
+    p.interleaved, p.scale = int(interleaved), float(scale)
+    out = np.empty((T, num_heads * D), dtype=_np_dtype(code))
+    args = [query, np.ascontiguousarray(key), np.ascontiguousarray(value), kc, vc, cum, past, bt,
+            None if cos_cache is None else np.ascontiguousarray(cos_cache),
+            None if sin_cache is None else np.ascontiguousarray(sin_cache), out]
+    rc = lib().oracle_paged_attention(ctypes.byref(p), *[_ptr(x) for x in args], code, threads)
+    _check(rc, "oracle_paged_attention")
+    return out, kc, vc
+
+
 def gather_block_quantized(data, scales, indices, *, block_size, zero_points=None, dtype=None):
     data = np.ascontiguousarray(data, dtype=np.uint8)
     scales = np.ascontiguousarray(scales)

@@ -13,7 +13,8 @@ onnxruntime nor onnx_ir is installable here, so this script:
    ``gather_block_quantized_model``; ``test_matmulnbits_asym.py``:
    ``_pack_int4_last``, ``_matmulnbits_model``; ``test_gqa11.py``:
    ``_attention_bias``, ``_gqa11_model`` and the qk-norm test's inline numpy
-   reference; ``test_mlx_ops.py``: the module-level RMS inputs) and runs them with
+   reference; ``test_mlx_ops.py``: the module-level RMS inputs; ``test_paged_attention.py``:
+   ``_inputs`` and ``_paged_ref``, its numpy port of ORT's PagedAttention reference) and runs them with
    stand-ins for the ONNX-building calls, so the fixtures carry exactly the inputs
    the reference's tests feed;
 2. computes the expected outputs in float64 numpy — with the reference's numpy
@@ -402,6 +403,45 @@ def gen_gbq(m, out, manifest):
     manifest["gbq"] = dict(family="gbq", block_size=block, source="tests/ops/_models.py:gather_block_quantized_model")
 
 
+def gen_paged(out, manifest):
+    """PagedAttention: the inputs and expected outputs of the reference's own test parameter sets
+    (test_paged_attention.py ``_inputs`` and its numpy port of ORT's reference ``_paged_ref``),
+    plus the caches after the scatter of the new rows."""
+    import math
+
+    path = os.path.join(REF, "tests/ops/test_paged_attention.py")
+    ns = _load_functions(path, ["_rotate_half", "_apply_rope", "_paged_ref", "_inputs"], {"np": np, "math": math})
+    src = "tests/ops/test_paged_attention.py"
+    cases = []
+    for H, KV in ((4, 2), (4, 4), (8, 2), (2, 1)):  # test_paged_attention_core
+        for batch in (1, 3):
+            cases.append((f"core-h{H}kv{KV}-b{batch}", H, KV, 16, 8 * batch, 4, batch, 0, 0, H * 10 + KV + batch))
+    for blk in (2, 8):  # test_paged_attention_multiblock
+        cases.append((f"multiblock-blk{blk}", 8, 2, 32, 16, blk, 2, 0, 0, blk + 7))
+    for inter in (0, 1):  # test_paged_attention_rotary
+        for H, KV, d in ((4, 2, 16), (2, 1, 64)):
+            cases.append((f"rotary-{'gptj' if inter else 'neox'}-h{H}d{d}", H, KV, d, 16, 4, 2, 1, inter,
+                           H + d + inter))
+    for name, H, KV, d, nb, blk, batch, rot, inter, seed in cases:
+        feeds, ref = ns["_inputs"](H, KV, d, nb, blk, batch, rot, inter, seed)
+        cos, sin = feeds.get("cos_cache"), feeds.get("sin_cache")
+        _, kc, vc = ns["_paged_ref"](feeds["query"], feeds["key"], feeds["value"], feeds["key_cache"],
+                                     feeds["value_cache"], feeds["cumulative_sequence_length"],
+                                     feeds["past_seqlens"], feeds["block_table"], H, KV, d,
+                                     cos=None if cos is None else cos.astype(np.float32),
+                                     sin=None if sin is None else sin.astype(np.float32), interleaved=inter,
+                                     return_cache=True)
+        key = f"paged/{name}"
+        for fname, val in feeds.items():
+            out[f"{key}/{fname}"] = val
+        out[f"{key}/expected"] = ref.astype(np.float32)
+        out[f"{key}/expected_key_cache"] = kc
+        out[f"{key}/expected_value_cache"] = vc
+        manifest[key] = {"family": "paged", "source": f"{src}:_inputs/_paged_ref",
+                         "attrs": {"num_heads": H, "kv_num_heads": KV, "do_rotary": rot, "rotary_interleaved": inter},
+                         "tolerance": {"rtol": 2e-2, "atol": 2e-2}}
+
+
 def main() -> None:
     if os.environ.get("PYTHONHASHSEED") != "0":
         os.environ["PYTHONHASHSEED"] = "0"
@@ -415,10 +455,13 @@ def main() -> None:
     gen_gqa(m, g11, captured, gq, manifest)
     gen_norms(m, ops, nm, manifest)
     gen_gbq(m, gb, manifest)
+    pa: dict = {}
+    gen_paged(pa, manifest)
     np.savez_compressed(os.path.join(HERE, "matmulnbits.npz"), **mnb)
     np.savez_compressed(os.path.join(HERE, "gqa.npz"), **gq)
     np.savez_compressed(os.path.join(HERE, "norms.npz"), **nm)
     np.savez_compressed(os.path.join(HERE, "gather_block_quantized.npz"), **gb)
+    np.savez_compressed(os.path.join(HERE, "paged_attention.npz"), **pa)
     with open(os.path.join(HERE, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=1, sort_keys=True)
     print(f"wrote {len(manifest)} golden cases")

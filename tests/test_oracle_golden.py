@@ -23,9 +23,11 @@ MNB = load_golden("matmulnbits.npz")
 GQA = load_golden("gqa.npz")
 NORMS = load_golden("norms.npz")
 GBQ = load_golden("gather_block_quantized.npz")
+PAGED = load_golden("paged_attention.npz")
 
 MNB_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "matmulnbits")
 GQA_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "gqa")
+PAGED_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "paged")
 
 
 @pytest.mark.parametrize("name", MNB_CASES)
@@ -95,6 +97,35 @@ def test_oracle_skip_rms_norm():
     y, r = oracle.skip_rms_norm(c["x"], c["skip"], c["gamma"], 1e-6)
     np.testing.assert_allclose(y, c["y"], rtol=1e-6, atol=1e-6)
     np.testing.assert_array_equal(r, c["residual"])
+
+
+@pytest.mark.parametrize("name", PAGED_CASES)
+def test_oracle_paged_attention(name):
+    """The reference's PagedAttention cases (test_paged_attention.py): the scattered caches match
+    bit for bit (the same fp32 RoPE rounded once to fp16); the output matches the reference's
+    fp32 numpy port within 2e-3 — the oracle, like the reference op, attends with q / k rounded to
+    fp16 after RoPE, the numpy port with unrounded fp32 values (its own test allows 2e-2)."""
+    a, c = MANIFEST[name]["attrs"], golden_case(PAGED, name)
+    out, kc, vc = oracle.paged_attention(
+        c["query"], c["key"], c["value"], c["key_cache"], c["value_cache"], c["cumulative_sequence_length"],
+        c["past_seqlens"], c["block_table"], c.get("cos_cache"), c.get("sin_cache"), num_heads=a["num_heads"],
+        kv_heads=a["kv_num_heads"], interleaved=a["rotary_interleaved"])
+    np.testing.assert_array_equal(kc, c["expected_key_cache"])
+    np.testing.assert_array_equal(vc, c["expected_value_cache"])
+    np.testing.assert_allclose(out.astype(np.float32), c["expected"], rtol=2e-3, atol=2e-3)
+
+
+def test_oracle_paged_attention_rejects_slots_outside_the_caches():
+    c = golden_case(PAGED, PAGED_CASES[0])
+    a = MANIFEST[PAGED_CASES[0]]["attrs"]
+    bt = c["block_table"].copy()
+    bt[0, 0] = c["key_cache"].shape[0]  # one past the last physical block
+    past = c["past_seqlens"].copy()
+    past[0] = max(int(past[0]), 1)
+    with pytest.raises(oracle.OracleError):
+        oracle.paged_attention(c["query"], c["key"], c["value"], c["key_cache"], c["value_cache"],
+                               c["cumulative_sequence_length"], past, bt, num_heads=a["num_heads"],
+                               kv_heads=a["kv_num_heads"])
 
 
 def test_oracle_gather_block_quantized():
