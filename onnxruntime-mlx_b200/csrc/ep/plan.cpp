@@ -203,6 +203,20 @@ int Plan::lower(const Graph& g, const std::vector<int>& nodes, std::string* err)
         }
         break;
       }
+      case OpKind::kPagedAttention: {
+        // inputs: q, k, v, key_cache, value_cache, cumulative lengths, past lengths, block table,
+        // cos, sin; outputs: attention, key_cache / value_cache (the inputs updated in place)
+        st.kind = StepKind::kPaged;
+        st.num_heads = (int)n.int_attr("num_heads", 0);
+        st.kv_heads = (int)n.int_attr("kv_num_heads", 0);
+        st.head_size = (int)(view.input_info(0)->shape[1] / st.num_heads);
+        st.do_rotary = (int)(n.int_attr("do_rotary", 0) != 0);
+        st.interleaved = (int)n.int_attr("rotary_interleaved", 0);
+        st.scale = n.float_attr("scale", 0.f);
+        st.in.resize(10, -1);
+        st.out.resize(3, -1);
+        break;
+      }
       case OpKind::kRmsNorm:
       case OpKind::kSimplifiedLayerNorm:
         st.kind = StepKind::kRms;
@@ -770,6 +784,8 @@ int Plan::shard_for_tp(std::string* err) {
     *err = "tensor parallel (" + std::to_string(W) + " ranks): " + m;
     return B200EP_EUNSUPPORTED;
   };
+  for (const Step& s : steps_)
+    if (s.kind == StepKind::kPaged) return fail(s.name + ": PagedAttention caches are not sharded");
   auto replace_const = [&](int id, std::shared_ptr<Initializer> init) {
     const int nid = slot_of(init->name);
     slots_[nid].kind = Slot::kConst;
@@ -955,6 +971,15 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
         for (int o : {1, 2})
           if (st.out[o] >= 0 && S[st.out[o]].shape.empty())
             S[st.out[o]].shape = {pk.shape[0], pk.shape[1], cap, pk.shape[3]};
+        break;
+      }
+      case StepKind::kPaged: {
+        const Slot& q = S[st.in[0]];
+        if (q.shape.size() != 2 || S[st.in[3]].shape.size() != 4)
+          return fail("PagedAttention " + st.name + ": query must be rank 2 and key_cache rank 4");
+        S[st.out[0]].shape = {q.shape[0], (int64_t)st.num_heads * st.head_size};
+        for (int o : {1, 2})
+          if (st.out[o] >= 0) S[st.out[o]].shape = S[st.in[o + 2]].shape;
         break;
       }
       case StepKind::kRms:
@@ -1152,6 +1177,42 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
         if (rc) return rc;
         break;
       }
+      case StepKind::kPaged: {
+        const Slot& q = S[s.in[0]];
+        const Slot& kc_in = S[s.in[3]];
+        const Slot& vc_in = S[s.in[4]];
+        // the caches are updated where the outputs live: copied there first when ORT bound the
+        // outputs apart from the inputs, else the inputs themselves (the reference's write-back)
+        void* kc = s.out[1] >= 0 ? S[s.out[1]].ptr : kc_in.ptr;
+        void* vc = s.out[2] >= 0 ? S[s.out[2]].ptr : vc_in.ptr;
+        for (auto [dst, src] : {std::pair<void*, const Slot*>{kc, &kc_in}, {vc, &vc_in}})
+          if (dst != src->ptr) {
+            e = cudaMemcpyAsync(dst, src->ptr, (size_t)src->numel() * dtype_size(src->dtype), cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) return cuda_status(e, "PagedAttention cache copy");
+          }
+        b200ep_paged_params p{};
+        p.batch = (int32_t)(S[s.in[5]].numel() - 1);
+        p.num_tokens = (int32_t)q.shape[0];
+        p.num_heads = s.num_heads;
+        p.kv_heads = s.kv_heads;
+        p.head_size = s.head_size;
+        p.num_blocks = (int32_t)kc_in.shape[0];
+        p.block_size = (int32_t)kc_in.shape[1];
+        p.max_blocks = p.batch > 0 ? (int32_t)(S[s.in[7]].numel() / p.batch) : 0;
+        const Slot* cos = s.do_rotary && s.in[8] >= 0 ? &S[s.in[8]] : nullptr;
+        p.do_rotary = cos != nullptr;
+        p.max_seq = cos ? (int32_t)cos->shape[0] : 0;
+        p.rotary_half = cos ? (int32_t)cos->shape[1] : 0;
+        p.interleaved = s.interleaved;
+        p.scale = s.scale;
+        int rc = b200ep_paged_attention(&p, q.ptr, S[s.in[1]].ptr, S[s.in[2]].ptr, kc, vc,
+                                        static_cast<const int32_t*>(S[s.in[5]].ptr),
+                                        static_cast<const int32_t*>(S[s.in[6]].ptr),
+                                        static_cast<const int32_t*>(S[s.in[7]].ptr), cos ? cos->ptr : nullptr,
+                                        cos ? S[s.in[9]].ptr : nullptr, S[s.out[0]].ptr, q.dtype, st);
+        if (rc) return rc;
+        break;
+      }
       case StepKind::kRms: {
         const Slot& x = S[s.in[0]];
         const int64_t hidden = x.shape.back();
@@ -1216,7 +1277,8 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
   if (prof) {
     cudaStreamSynchronize(st);
     static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                  "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+                                  "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
+                                "PagedAttention"};
     for (int i = 0; i < si; ++i) {
       const Step& s = steps_[i];
       std::string key = names[(int)s.kind];
@@ -1238,7 +1300,7 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
 
 int Plan::launches_per_run() const {
   int n = 0;
-  for (auto& s : steps_) n += s.kind != StepKind::kAllReduce && s.kind != StepKind::kAllGather;
+  for (auto& s : steps_) n += (s.kind != StepKind::kAllReduce && s.kind != StepKind::kAllGather) + (s.kind == StepKind::kPaged);
   return n;
 }
 
@@ -1496,7 +1558,8 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
 
 std::string Plan::preview() const {
   static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
+                                "PagedAttention"};
   auto fnv = [](const std::vector<uint8_t>& b) {
     uint64_t h = 1469598103934665603ull;
     for (uint8_t c : b) h = (h ^ c) * 1099511628211ull;
@@ -1539,7 +1602,8 @@ std::string Plan::describe() const {
   for (auto& st : steps_) npk += st.prepacked;
   o << ",\"prepacked_matmulnbits\":" << npk << ",\"ops\":[";
   static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather"};
+                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
+                                "PagedAttention"};
   for (size_t i = 0; i < steps_.size(); ++i) o << (i ? "," : "") << "\"" << names[(int)steps_[i].kind] << "\"";
   o << "]}";
   return o.str();

@@ -97,7 +97,7 @@ struct Slot {
   }
 };
 
-enum class StepKind { kMnb, kGqa, kRms, kBinary, kSigmoid, kSiluMul, kCast, kGbq, kAllReduce, kAllGather };
+enum class StepKind { kMnb, kGqa, kRms, kBinary, kSigmoid, kSiluMul, kCast, kGbq, kAllReduce, kAllGather, kPaged };
 
 struct Step {
   StepKind kind;

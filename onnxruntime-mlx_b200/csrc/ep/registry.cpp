@@ -258,9 +258,64 @@ ClaimResult cast_claim(const NodeView& v) {
   return ClaimResult::yes();
 }
 
+// ---- PagedAttention: rust/src/ops/attention.rs:2748-2900 ------------------------------------
+// The reference's checks for the forms this EP runs (separate K / V caches, causal, optional RoPE
+// from structured cos / sin caches); slot_mapping, head_sink, q/k norms, rotary_offset and the
+// LATENT layout are declined here (they stay with the next provider).
+ClaimResult paged_claim(const NodeView& v) {
+  REQUIRE(v.num_outputs() >= 1, "PagedAttention requires at least 1 output");
+  const int o = out_dt(v, 0);
+  REQUIRE(o == kF16 || o == kBF16, "PagedAttention is only supported for fp16/bf16 (T), got %s", dtype_name(o));
+  const size_t nin = v.num_inputs();
+  REQUIRE(nin >= 8 && nin <= 17, "expects 8 required inputs plus optional rotary inputs, got %zu", nin);
+  REQUIRE(v.string_attr("kv_cache_layout", "SEPARATE") == "SEPARATE", "only the SEPARATE kv_cache_layout is implemented");
+  for (size_t i : {0, 1, 2, 3, 4}) {
+    REQUIRE(v.input_info(i), "input %zu (Q/K/V/cache) must be present with a float dtype", i);
+    REQUIRE(in_dt(v, i) == o, "input %zu must share the output float dtype", i);
+  }
+  for (size_t i : {5, 6, 7}) {
+    REQUIRE(v.input_info(i), "input %zu (positional) must be present", i);
+    REQUIRE(in_dt(v, i) == kI32, "input %zu must be int32", i);
+  }
+  for (size_t i : {10, 11, 12, 13})
+    REQUIRE(!v.input_present(i), "input %zu (slot_mapping / head_sink / q-k norm) is not implemented", i);
+  const int64_t nh = v.int_attr("num_heads", 0), kvh = v.int_attr("kv_num_heads", 0);
+  REQUIRE(nh > 0 && kvh > 0 && nh % kvh == 0, "num_heads (%lld) must be a positive multiple of kv_num_heads (%lld)",
+          (long long)nh, (long long)kvh);
+  auto* q = v.input_info(0);
+  REQUIRE(q->shape.size() == 2 && q->shape[1] > 0 && q->shape[1] % nh == 0, "query must be [num_tokens,num_heads*head_size]");
+  const int64_t head = q->shape[1] / nh;
+  REQUIRE(head == 32 || head == 64 || head == 128, "head_size %lld is not 32, 64 or 128", (long long)head);
+  const int64_t vh = v.int_attr("v_head_size", 0);
+  REQUIRE(vh == 0 || vh == head, "v_head_size different from head_size is not implemented");
+  REQUIRE(v.int_attr("rotary_offset", 0) == 0, "rotary_offset is not implemented");
+  for (size_t i : {1, 2}) {
+    auto* t = v.input_info(i);
+    REQUIRE(t->shape.size() == 2 && t->shape[1] == kvh * head, "input %zu must be [num_tokens,kv_num_heads*head_size]", i);
+  }
+  for (size_t i : {3, 4}) {
+    auto* t = v.input_info(i);
+    REQUIRE(t->shape.size() == 4 && t->shape[1] > 0 && t->shape[2] == kvh && t->shape[3] == head,
+            "input %zu must be [num_blocks,block_size,kv_num_heads,head_size] with a static block_size", i);
+  }
+  REQUIRE(v.int_attr("local_window_size", -1) == -1, "sliding-window attention (local_window_size) is not supported");
+  REQUIRE(v.float_attr("softcap", 0.f) == 0.f, "attention softcap is not supported");
+  for (size_t i = 1; i < v.num_outputs() && i < 3; ++i)
+    if (v.output_present(i)) REQUIRE(out_dt(v, i) == o, "output %zu must share the output float dtype", i);
+  if (v.int_attr("do_rotary", 0) != 0) {
+    REQUIRE(v.input_present(8) && v.input_present(9), "do_rotary=1 requires cos_cache and sin_cache inputs");
+    REQUIRE(in_dt(v, 8) == o && in_dt(v, 9) == o, "cos_cache/sin_cache must share the output float dtype");
+    auto* c = v.input_info(8);
+    REQUIRE(c->shape.size() == 2 && c->shape[1] > 0 && 2 * c->shape[1] <= head,
+            "cos_cache must be [max_seq, rotary_dim/2] with rotary_dim <= head_size");
+  }
+  return ClaimResult::yes();
+}
+
 const OpEntry kTable[] = {
     {"com.microsoft", "MatMulNBits", -1, -1, OpKind::kMatMulNBits, matmulnbits_claim},
     {"com.microsoft", "GroupQueryAttention", -1, -1, OpKind::kGroupQueryAttention, gqa_claim},
+    {"com.microsoft", "PagedAttention", -1, -1, OpKind::kPagedAttention, paged_claim},
     {"", "RMSNormalization", 23, -1, OpKind::kRmsNorm, rms_norm_claim},
     {"com.microsoft", "SimplifiedLayerNormalization", -1, -1, OpKind::kSimplifiedLayerNorm,
      simplified_layer_norm_claim},
@@ -284,6 +339,7 @@ const char* op_kind_name(OpKind k) {
   switch (k) {
     case OpKind::kMatMulNBits: return "MatMulNBits";
     case OpKind::kGroupQueryAttention: return "GroupQueryAttention";
+    case OpKind::kPagedAttention: return "PagedAttention";
     case OpKind::kRmsNorm: return "RMSNormalization";
     case OpKind::kSimplifiedLayerNorm: return "SimplifiedLayerNormalization";
     case OpKind::kSkipSimplifiedLayerNorm: return "SkipSimplifiedLayerNormalization";

@@ -13,6 +13,7 @@ namespace b200ep {
 enum class OpKind {
   kMatMulNBits,
   kGroupQueryAttention,
+  kPagedAttention,
   kRmsNorm,                // ai.onnx RMSNormalization (eps default 1e-6)
   kSimplifiedLayerNorm,    // com.microsoft / mis-stamped default domain (eps default 1e-5)
   kSkipSimplifiedLayerNorm,

@@ -267,3 +267,60 @@ def test_layer_boundaries_follow_metadata():
 def test_unset_layer_partitions_keep_one_partition():
     _, _, num = claimed(layered_graph(24))
     assert num == 1
+
+
+def paged_graph(*, H=4, KV=2, D=64, dtype=FLOAT16, do_rotary=1, layout=None, extra=(), rotary_offset=0,
+                local_window=None, cos_dtype=None):
+    g = GraphBuilder()
+    nb, blk, batch, maxb = 16, 8, 2, 8
+    g.input("q", dtype, [-1, H * D])
+    g.input("k", dtype, [-1, KV * D])
+    g.input("v", dtype, [-1, KV * D])
+    g.input("kc", dtype, [nb, blk, KV, D])
+    g.input("vc", dtype, [nb, blk, KV, D])
+    g.input("cum", INT32, [batch + 1])
+    g.input("past", INT32, [batch])
+    g.input("bt", INT32, [batch, maxb])
+    ins = ["q", "k", "v", "kc", "vc", "cum", "past", "bt"]
+    if do_rotary:
+        cd = cos_dtype or dtype
+        npd = np.float16 if cd == FLOAT16 else np.float32
+        g.initializer("cos", np.ones((64, D // 2), npd), cd)
+        g.initializer("sin", np.zeros((64, D // 2), npd), cd)
+        ins += ["cos", "sin"]
+    for name in extra:  # optional inputs 10.. (slot_mapping, head_sink, ...)
+        while len(ins) < 10:
+            ins.append("")
+        g.input(name, INT32, [-1])
+        ins.append(name)
+    g.output("out", dtype, [-1, H * D])
+    attrs = dict(num_heads=H, kv_num_heads=KV, do_rotary=do_rotary)
+    if layout:
+        attrs["kv_cache_layout"] = layout
+    if rotary_offset:
+        attrs["rotary_offset"] = rotary_offset
+    if local_window is not None:
+        attrs["local_window_size"] = local_window
+    g.node("PagedAttention", ins, ["out"], domain="com.microsoft", **attrs)
+    return g
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(do_rotary=0), dict(H=8, KV=8, D=32), dict(H=32, KV=8, D=128)])
+def test_paged_attention_claims(kw):
+    _, groups, _ = claimed(paged_graph(**kw))
+    assert groups == [0]
+
+
+@pytest.mark.parametrize("kw,reason", [
+    (dict(dtype=FLOAT), "fp16/bf16"),
+    (dict(D=16), "head_size 16"),
+    (dict(layout="LATENT"), "SEPARATE"),
+    (dict(extra=("slot_mapping",)), "slot_mapping"),
+    (dict(rotary_offset=8), "rotary_offset"),
+    (dict(local_window=16), "local_window_size"),
+    (dict(cos_dtype=FLOAT), "cos_cache/sin_cache"),
+])
+def test_paged_attention_declines_with_reason(kw, reason):
+    ep, groups, _ = claimed(paged_graph(**kw))
+    assert groups == [-1]
+    assert reason in ep.claim_reason(0)

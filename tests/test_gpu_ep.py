@@ -107,6 +107,60 @@ def test_gqa_through_ep_both_kv_contracts(ep_mod, shared):
     np.testing.assert_array_equal(res["prv"].cpu().numpy()[:, :, :valid], wv[:, :, :valid])
 
 
+@pytest.mark.parametrize("cache_outputs", [False, True], ids=["in-place", "bound-outputs"])
+def test_paged_attention_through_ep(ep_mod, cache_outputs):
+    """PagedAttention claimed and compiled: a decode row and a 5-token prompt chunk in one packed
+    batch over a shuffled block table; the caches are updated in place, or copied into separately
+    bound cache outputs first."""
+    rng = np.random.default_rng(3)
+    H, KV, D, nb, blk = 32, 8, 128, 40, 16
+    new_lens, pasts = [1, 5], [300, 17]
+    batch = len(new_lens)
+    maxb = 20
+    cum = np.concatenate([[0], np.cumsum(new_lens)]).astype(np.int32)
+    bt = rng.permutation(nb)[: batch * maxb].astype(np.int32).reshape(batch, maxb)
+    T = int(cum[-1])
+    q = (rng.standard_normal((T, H * D)) * 0.5).astype(np.float16)
+    k = (rng.standard_normal((T, KV * D)) * 0.5).astype(np.float16)
+    v = rng.standard_normal((T, KV * D)).astype(np.float16)
+    kc = (rng.standard_normal((nb, blk, KV, D)) * 0.5).astype(np.float16)
+    vc = rng.standard_normal((nb, blk, KV, D)).astype(np.float16)
+    half = D // 2
+    ang = np.arange(512)[:, None] * (1.0 / (10000.0 ** (np.arange(half) / half)))[None, :]
+    cos, sin = np.cos(ang).astype(np.float16), np.sin(ang).astype(np.float16)
+    g = ep_mod.GraphBuilder()
+    F16 = ep_mod.FLOAT16
+    g.input("q", F16, [-1, H * D])
+    g.input("k", F16, [-1, KV * D])
+    g.input("v", F16, [-1, KV * D])
+    g.input("kc", F16, [nb, blk, KV, D])
+    g.input("vc", F16, [nb, blk, KV, D])
+    g.input("cum", ep_mod.INT32, [batch + 1])
+    g.input("past", ep_mod.INT32, [batch])
+    g.input("bt", ep_mod.INT32, [batch, maxb])
+    g.initializer("cos", cos, F16)
+    g.initializer("sin", sin, F16)
+    g.output("out", F16, [-1, H * D])
+    outs = ["out"]
+    if cache_outputs:
+        g.output("kco", F16, [nb, blk, KV, D])
+        g.output("vco", F16, [nb, blk, KV, D])
+        outs += ["kco", "vco"]
+    g.node("PagedAttention", ["q", "k", "v", "kc", "vc", "cum", "past", "bt", "cos", "sin"], outs,
+           domain="com.microsoft", num_heads=H, kv_num_heads=KV, do_rotary=1)
+    sess = ep_mod.Session(g)
+    tkc, tvc = cuda(kc), cuda(vc)
+    res = sess.run({"q": cuda(q), "k": cuda(k), "v": cuda(v), "kc": tkc, "vc": tvc, "cum": cuda(cum),
+                    "past": cuda(np.array(pasts, np.int32)), "bt": cuda(bt)})
+    want, wk, wv = oracle.paged_attention(q, k, v, kc, vc, cum, pasts, bt, cos, sin, num_heads=H, kv_heads=KV)
+    np.testing.assert_allclose(res["out"].float().cpu().numpy(), want.astype(np.float32), rtol=1e-2, atol=1e-3)
+    got_k, got_v = (res["kco"], res["vco"]) if cache_outputs else (tkc, tvc)
+    np.testing.assert_array_equal(got_k.cpu().numpy(), wk)
+    np.testing.assert_array_equal(got_v.cpu().numpy(), wv)
+    if cache_outputs:  # the bound inputs keep their contents
+        np.testing.assert_array_equal(tkc.cpu().numpy(), kc)
+
+
 SMALL = dict(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000, max_seq=256)
 
 
