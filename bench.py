@@ -720,6 +720,8 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--context", type=int, default=0,
+                    help="--kernel-only paged: time this one (batch, context) case instead of the default set")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
@@ -756,7 +758,8 @@ def main():
             for S in (512, 1024, 4096):
                 print(json.dumps(gqa_prefill_timing(S, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "paged":
-            for b, ctx in ((1, 1024), (8, 1024), (8, 8192), (32, 2048)):
+            cases = ((args.batch, args.context),) if args.context else ((1, 1024), (8, 1024), (8, 8192), (32, 2048))
+            for b, ctx in cases:
                 print(json.dumps(paged_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "gemm":
             for name, m, k, n in GEMM_SHAPES:

@@ -130,7 +130,7 @@ __device__ __forceinline__ void unpack8f(uint4 w, float (&f)[8]) {
 }
 
 template <typename T, int DPL, int GM>
-__global__ void __launch_bounds__(kPagedWarps * 32, 1) paged_attn_kernel(PagedKP kp) {
+__global__ void __launch_bounds__(kPagedWarps * 32, 2) paged_attn_kernel(PagedKP kp) {
   constexpr int D = DPL * 32, NW = kPagedWarps;
   __shared__ __align__(16) float qs[GM][D];  // rotated, rounded, scaled query rows
   __shared__ float wm[NW][GM], wl[NW][GM];
@@ -345,10 +345,11 @@ cudaError_t launch_paged_t(const PagedKP& kp, cudaStream_t st) {
   if (app_smem > 48 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = launch_k(paged_append_kernel<T>, dim3((unsigned)kp.ntok), dim3(128), app_smem, st, kp))
     return e;
-  // key splits per (token, kv head, query-head chunk): enough CTAs for two per SM, at most a
-  // portable cluster of 8
+  // key splits per (token, kv head, query-head chunk): as many as fit one wave of the two CTAs
+  // per SM (a partial second wave would double the time of its keys), at most a portable cluster
+  // of 8
   const int64_t items = (int64_t)kp.ntok * kp.HK * kp.gchunks;
-  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>(8, (2 * num_sms() + items - 1) / items));
+  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>(8, 2 * num_sms() / items));
   switch (kp.D) {
     case 32: return launch_attn_g<T, 1>(kp, splits, st);
     case 64: return launch_attn_g<T, 2>(kp, splits, st);
