@@ -63,6 +63,13 @@ struct GqaKP {
   float scale_log2;  // scale * log2(e)
   float qk_eps;
   int has_qk_norm;
+  // PagedAttention through gqa_mma_decode_kernel<..., true>: blockIdx.z is a packed row of
+  // p_batch sequences (cumulative lengths p_cum, past lengths p_past); key j of its sequence lives
+  // at cache row p_bt[seq][j / p_bs] * p_bs + j % p_bs of kv_k / kv_v [p_nblocks, p_bs, HK, D]
+  const int32_t* p_cum;
+  const int32_t* p_past;
+  const int32_t* p_bt;
+  int p_batch, p_nblocks, p_bs, p_maxb;
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -700,7 +707,27 @@ struct MmaSmem {
   static constexpr int kTotal = kMerge + 8 * (D + 2) * 4;
 };
 
-template <typename T, int D>
+// The sequence of packed row i (cum[b] <= i < cum[b + 1]) or -1, and the cache row of its key j or -1.
+__device__ __forceinline__ int paged_seq(const GqaKP& kp, int i) {
+  int lo = 0, hi = kp.p_batch;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(kp.p_cum + mid) <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  if (lo >= kp.p_batch || __ldg(kp.p_cum + lo) > i || i >= __ldg(kp.p_cum + lo + 1)) return -1;
+  return lo;
+}
+__device__ __forceinline__ int paged_row(const GqaKP& kp, int seq, int j) {
+  const int blk = j / kp.p_bs;
+  if (j < 0 || blk >= kp.p_maxb) return -1;
+  const int phys = __ldg(kp.p_bt + (size_t)seq * kp.p_maxb + blk);
+  return phys < 0 || phys >= kp.p_nblocks ? -1 : phys * kp.p_bs + j % kp.p_bs;
+}
+
+// PAGED: the PagedAttention form (see GqaKP); the new rows were appended by a preceding launch, so
+// the K / V stream starts after the wait for it and no warp appends.
+template <typename T, int D, bool PAGED = false>
 __global__ void __launch_bounds__(kMmaWarps * 32)
 gqa_mma_decode_kernel(GqaKP kp) {
   using L = MmaSmem<D>;
@@ -716,8 +743,17 @@ gqa_mma_decode_kernel(GqaKP kp) {
 
   // Before the wait: everything that depends only on data written two or more kernels back —
   // the positions (seqlens), the KV rows of earlier steps and the rotary tables (see pdl_trigger).
-  const int past = past_len(kp, b);
-  const bool ok = range_ok(kp, past);
+  int past;
+  bool ok;
+  int pseq = -1;  // PAGED: the row's sequence
+  if constexpr (PAGED) {
+    pseq = paged_seq(kp, b);
+    past = pseq >= 0 ? __ldg(kp.p_past + pseq) + (b - __ldg(kp.p_cum + pseq)) : -1;
+    ok = past >= 0 && (!kp.do_rotary || past < kp.max_seq);
+  } else {
+    past = past_len(kp, b);
+    ok = range_ok(kp, past);
+  }
   const int nk = ok ? past + 1 : 0;  // keys [lo, nk)
   const int lo = kp.local_window > 0 ? max(0, past - kp.local_window + 1) : 0;
   const int units = nk > lo ? (nk - lo + kUnit - 1) / kUnit : 0;
@@ -728,21 +764,50 @@ gqa_mma_decode_kernel(GqaKP kp) {
   T* kvv = static_cast<T*>(kp.kv_v) + head_base * D;
 
   unsigned char* wbuf = sm + warp * L::kWarpBytes;  // [buf][K | V]
+  bool bad_row = false;  // PAGED: a key row outside the caches (read as zeros, reported)
+  // PAGED: lane l holds the cache row of key l of the next unit to issue; each issue uses it and
+  // starts the block-table load of the unit after, so that lookup overlaps a whole unit.  (The
+  // block table is not written by the kernels before this one, so the first lookup may precede
+  // the programmatic-launch wait.)
+  auto lookup = [&](int u) {
+    const int j = lo + u * kUnit + lane;
+    return j < nk ? paged_row(kp, pseq, j) : -1;
+  };
+  int prow_next = 0;
+  if constexpr (PAGED) prow_next = lookup(u0);
   auto issue = [&](int u, int buf) {
     unsigned char* kb = wbuf + buf * 2 * L::kUnitBytes;
     unsigned char* vb = kb + L::kUnitBytes;
     const int key0 = lo + u * kUnit;
-    for (int i = lane; i < kUnit * D / 8; i += 32) {
-      const int r = i / (D / 8), ch = i % (D / 8);
-      const bool v = key0 + r < nk;
-      const int64_t row = v ? key0 + r : 0;
-      cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
-      cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+    if constexpr (PAGED) {
+      // lane l looked up the cache row of key key0 + l; the copies take it by shuffle
+      const int prow = prow_next;
+      prow_next = lookup(u + 1);
+      bad_row |= key0 + lane < nk && prow < 0;
+      const T* kc = static_cast<const T*>(kp.kv_k);
+      const T* vc = static_cast<const T*>(kp.kv_v);
+      for (int i = lane; i < kUnit * D / 8; i += 32) {
+        const int r = i / (D / 8), ch = i % (D / 8);
+        const int pr = __shfl_sync(0xffffffffu, prow, r);
+        const bool v = pr >= 0;
+        const int64_t off = v ? ((int64_t)pr * kp.HK + kvh) * D + ch * 8 : 0;
+        cp_async16(kb + swz<D>(r, ch), kc + off, v);
+        cp_async16(vb + swz<D>(r, ch), vc + off, v);
+      }
+    } else {
+      for (int i = lane; i < kUnit * D / 8; i += 32) {
+        const int r = i / (D / 8), ch = i % (D / 8);
+        const bool v = key0 + r < nk;
+        const int64_t row = v ? key0 + r : 0;
+        cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
+        cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+      }
     }
     cp_async_commit();
   };
-  for (int k = 0; k < L::kBufs; ++k)
-    if (u0 + k < u1) issue(u0 + k, k);
+  if constexpr (!PAGED)
+    for (int k = 0; k < L::kBufs; ++k)
+      if (u0 + k < u1) issue(u0 + k, k);
   float cs[4] = {0, 0, 0, 0}, sn[4] = {0, 0, 0, 0};  // rotary pairs i = lane + 32 * e of this position
   if (ok && kp.do_rotary) {
     const T* cc = static_cast<const T*>(kp.cos_c) + (int64_t)past * kp.half;
@@ -793,6 +858,9 @@ gqa_mma_decode_kernel(GqaKP kp) {
 
   pdl_wait();  // q / k / v come from the previous kernel
   pdl_trigger();
+  if constexpr (PAGED)  // the previous launch appended this step's rows
+    for (int k = 0; k < L::kBufs; ++k)
+      if (u0 + k < u1) issue(u0 + k, k);
   if (!ok && threadIdx.x == 0 && crank == 0 && kvh == 0) report_device_error(kp.err, kErrGqaRange, b);
 
   // rotated query rows (rounded through T, as stored) -> Qs rows 0..G-1; rows G..15 zero
@@ -804,7 +872,7 @@ gqa_mma_decode_kernel(GqaKP kp) {
   // its streamed copy of that unit, which was read before the append).  Its k / v loads are issued
   // together with the query loads, so the two round trips overlap.
   const int u_new = nk > lo ? (nk - 1 - lo) / kUnit : -1;
-  const bool owner = ok && u_new >= u0 && u_new < u1;
+  const bool owner = !PAGED && ok && u_new >= u0 && u_new < u1;
   T knew[D / 32], vnew[D / 32], kraw[D / 32];
   const int64_t in_off = (int64_t)b * kp.kstride + (int64_t)kvh * D;
   if (owner) {
@@ -919,6 +987,10 @@ gqa_mma_decode_kernel(GqaKP kp) {
     const float corr = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
     float ps = 0.f;
     uint32_t pa[2][4];  // P as A fragments for the two 16-key k-steps (rows g+8 zero)
+    // PagedAttention in bf16: P as hi + lo bf16 parts (two P.V MMAs), since its rows with few keys
+    // have large probabilities whose 8-bit rounding would show in the output
+    constexpr bool kPSplit = PAGED && std::is_same<T, __nv_bfloat16>::value;
+    uint32_t pl[2][4];
 #pragma unroll
     for (int nb = 0; nb < 4; ++nb) {
       const float p0 = sc[nb][0] == -INFINITY ? 0.f : exp2f(sc[nb][0] - m_new);
@@ -926,6 +998,10 @@ gqa_mma_decode_kernel(GqaKP kp) {
       ps += p0 + p1;
       pa[nb >> 1][(nb & 1) * 2] = pack2<T>(p0, p1);
       pa[nb >> 1][(nb & 1) * 2 + 1] = 0u;
+      if constexpr (kPSplit) {
+        pl[nb >> 1][(nb & 1) * 2] = pack2<T>(p0 - round_through<T>(p0), p1 - round_through<T>(p1));
+        pl[nb >> 1][(nb & 1) * 2 + 1] = 0u;
+      }
     }
     ps += __shfl_xor_sync(0xffffffffu, ps, 1);
     ps += __shfl_xor_sync(0xffffffffu, ps, 2);
@@ -948,11 +1024,17 @@ gqa_mma_decode_kernel(GqaKP kp) {
         ldsm_x4_t(bfr, vb + swz<D>(r, n + (lane >> 4)));
         mma_f32<T>(o[n], pa[ks], bfr[0], bfr[1]);
         mma_f32<T>(o[n + 1], pa[ks], bfr[2], bfr[3]);
+        if constexpr (kPSplit) {
+          mma_f32<T>(o[n], pl[ks], bfr[0], bfr[1]);
+          mma_f32<T>(o[n + 1], pl[ks], bfr[2], bfr[3]);
+        }
       }
     __syncwarp();
     if (u + L::kBufs < u1) issue(u + L::kBufs, buf);
   }
 
+  if constexpr (PAGED)
+    if (__any_sync(0xffffffffu, bad_row) && lane == 0) report_device_error(kp.err, kErrGqaRange, b);
   // merge the warps: per-warp (m, l, O) rows into shared memory (reusing the stream buffers)
   __syncthreads();
   float* wst = reinterpret_cast<float*>(sm);  // [kMmaWarps][8][D + 2]
@@ -1340,10 +1422,10 @@ int mma_splits(const b200ep_gqa_params& p) {
   return (int)std::max<int64_t>(1, std::min<int64_t>({8, (units + kMmaWarps - 1) / kMmaWarps, by_sms}));
 }
 
-template <typename T, int D>
+template <typename T, int D, bool PAGED = false>
 cudaError_t launch_mma_decode(const GqaKP& kp, int splits, cudaStream_t st) {
   using L = MmaSmem<D>;
-  auto kern = gqa_mma_decode_kernel<T, D>;
+  auto kern = gqa_mma_decode_kernel<T, D, PAGED>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -1395,6 +1477,46 @@ cudaError_t launch_mma_prefill(const GqaKP& kp, cudaStream_t st) {
 }  // namespace
 
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
+
+// PagedAttention rows on the tensor-core decode kernel (the caller has appended the new rows).
+cudaError_t launch_paged_mma(const PagedMmaArgs& a, cudaStream_t st) {
+  GqaKP kp{};
+  kp.q = a.query;
+  kp.kv_k = a.key_cache;
+  kp.kv_v = a.value_cache;
+  kp.cos_c = a.cos_cache;
+  kp.sin_c = a.sin_cache;
+  kp.out = a.out;
+  kp.err = device_error_slot();
+  kp.B = a.num_tokens;
+  kp.S = 1;
+  kp.H = a.num_heads;
+  kp.HK = a.kv_heads;
+  kp.D = a.head_size;
+  kp.G = a.num_heads / a.kv_heads;
+  kp.R = kp.G;
+  kp.max_seq = a.max_seq;
+  kp.half = a.rotary_half;
+  kp.do_rotary = a.do_rotary ? 1 : 0;
+  kp.interleaved = a.interleaved ? 1 : 0;
+  kp.qstride = (int64_t)a.num_heads * a.head_size;
+  kp.scale_log2 = a.scale * kLog2e;
+  kp.p_cum = a.cum;
+  kp.p_past = a.past;
+  kp.p_bt = a.block_table;
+  kp.p_batch = a.batch;
+  kp.p_nblocks = a.num_blocks;
+  kp.p_bs = a.block_size;
+  kp.p_maxb = a.max_blocks;
+  // one wave: the kernel holds one CTA per SM (its K / V streams fill shared memory)
+  const int64_t heads = std::max<int64_t>(1, (int64_t)a.num_tokens * a.kv_heads);
+  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>(8, num_sms() / heads));
+  if (a.dtype == kF16)
+    return a.head_size == 64 ? launch_mma_decode<__half, 64, true>(kp, splits, st)
+                             : launch_mma_decode<__half, 128, true>(kp, splits, st);
+  return a.head_size == 64 ? launch_mma_decode<__nv_bfloat16, 64, true>(kp, splits, st)
+                           : launch_mma_decode<__nv_bfloat16, 128, true>(kp, splits, st);
+}
 
 int launch_gqa(const GqaArgs& a, cudaStream_t st) {
   const b200ep_gqa_params& p = a.p;

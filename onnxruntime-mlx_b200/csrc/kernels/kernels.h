@@ -65,4 +65,23 @@ size_t gqa_workspace_bytes(const b200ep_gqa_params& p);
 // Validates geometry (returns a B200EP_* status and message via set_error) and launches.
 int launch_gqa(const GqaArgs& a, cudaStream_t st);
 
+// PagedAttention rows (fp16 / bf16, head_size 64 / 128, at most 8 query heads per kv head, fewer
+// than 65536 rows, 16-byte aligned caches) on the tensor-core decode kernel of gqa.cu; the new
+// rows must already be in the caches.
+struct PagedMmaArgs {
+  const void* query;
+  void* key_cache;
+  void* value_cache;
+  const int32_t* cum;
+  const int32_t* past;
+  const int32_t* block_table;
+  const void* cos_cache;
+  const void* sin_cache;
+  void* out;
+  int dtype, batch, num_tokens, num_heads, kv_heads, head_size;
+  int num_blocks, block_size, max_blocks, max_seq, rotary_half, do_rotary, interleaved;
+  float scale;
+};
+cudaError_t launch_paged_mma(const PagedMmaArgs& a, cudaStream_t st);
+
 }  // namespace b200ep

@@ -3,7 +3,10 @@
 // with mlx_scatter and runs a masked SDPA per sequence).
 //
 // Two launches, both reading the control tensors (cumulative lengths, past lengths, block table)
-// on the device, so nothing is copied to the host:
+// on the device, so nothing is copied to the host.  Rows with head_size 64 / 128 and at most 8
+// query heads per kv head attend on the tensor-core decode kernel of gqa.cu
+// (gqa_mma_decode_kernel<..., PAGED = true>: per-warp cp.async K / V streams whose row addresses
+// go through the block table, mma.sync scores, cluster merge); paged_attn_kernel covers the rest.
 //   paged_append_kernel — one CTA per packed token: finds its sequence, RoPEs the new k row at
 //     position past_b + j (fp32, rounded once to the I/O dtype) and writes k and v into their
 //     block-table slot of the caches.
@@ -16,13 +19,16 @@
 //     head_size / 32 dims of each value row (coalesced, 8 rows in flight).  Warp states merge in
 //     shared memory, the cluster's CTA states in rank 0 through distributed shared memory.
 // A slot outside the caches / block table, or a position outside the cos / sin rows, is never
-// read or written: the append skips it, attention masks the key (or writes a zero row when the
-// query itself is out of range), and the device error word records it.
+// read or written: the append skips it, attention masks the key (the tensor-core path reads it as
+// zeros; a query row whose own position is out of range is left unwritten there and zeroed here),
+// and the device error word records it.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
+#include "kernels/kernels.h"
 
 namespace b200ep {
 
@@ -340,11 +346,25 @@ cudaError_t launch_attn_g(const PagedKP& kp, int splits, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_paged_t(const PagedKP& kp, cudaStream_t st) {
+cudaError_t launch_paged_t(const PagedKP& kp, int dtype, cudaStream_t st) {
   const size_t app_smem = (size_t)kp.HK * kp.D * sizeof(float);
   if (app_smem > 48 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = launch_k(paged_append_kernel<T>, dim3((unsigned)kp.ntok), dim3(128), app_smem, st, kp))
     return e;
+  // the tensor-core decode kernel of gqa.cu (cp.async K / V streams, mma.sync scores) where it
+  // applies; the SIMT kernel below otherwise
+  if ((kp.D == 64 || kp.D == 128) && kp.G <= 8 && kp.ntok < 65536 &&
+      reinterpret_cast<uintptr_t>(kp.q) % 8 == 0 && !getenv("ONNXRUNTIME_EP_B200_PAGED_SIMT")) {
+    PagedMmaArgs a{};
+    a.query = kp.q, a.key_cache = kp.kc, a.value_cache = kp.vc;
+    a.cum = kp.cum, a.past = kp.past, a.block_table = kp.bt;
+    a.cos_cache = kp.cos_c, a.sin_cache = kp.sin_c, a.out = kp.out;
+    a.dtype = dtype, a.batch = kp.batch, a.num_tokens = kp.ntok, a.num_heads = kp.H, a.kv_heads = kp.HK;
+    a.head_size = kp.D, a.num_blocks = kp.nblocks, a.block_size = kp.bs, a.max_blocks = kp.maxb;
+    a.max_seq = kp.max_seq, a.rotary_half = kp.half, a.do_rotary = kp.rot, a.interleaved = kp.inter;
+    a.scale = kp.scale;
+    return launch_paged_mma(a, st);
+  }
   // key splits per (token, kv head, query-head chunk): as many as fit one wave of the two CTAs
   // per SM (a partial second wave would double the time of its keys), at most a portable cluster
   // of 8
@@ -402,7 +422,8 @@ extern "C" B200EP_API int b200ep_paged_attention(const b200ep_paged_params* p, c
     B200EP_CHECK_ARG((int64_t)kp.HK * kp.gchunks <= 65535 && (int64_t)kp.ntok * 8 < (1ll << 31),
                      "PagedAttention: too many kv heads or tokens");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const cudaError_t e = dtype == kF16 ? launch_paged_t<__half>(kp, st) : launch_paged_t<__nv_bfloat16>(kp, st);
+    const cudaError_t e =
+        dtype == kF16 ? launch_paged_t<__half>(kp, dtype, st) : launch_paged_t<__nv_bfloat16>(kp, dtype, st);
     return cuda_status(e, "PagedAttention launch");
   } catch (const std::exception& e) {
     return set_error(B200EP_EINTERNAL, std::string("exception: ") + e.what());

@@ -545,6 +545,14 @@ def test_paged_attention_vs_oracle(ops, H, KV, D, bs, new_lens, pasts, inter, dt
         np.testing.assert_array_equal(to_np(vc), wv)
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_paged_attention_simt_path_vs_oracle(ops, dt, monkeypatch):
+    """The SIMT attention kernel on shapes the tensor-core kernel also takes (forced by the
+    ONNXRUNTIME_EP_B200_PAGED_SIMT switch), so both paths stay checked against the oracle."""
+    monkeypatch.setenv("ONNXRUNTIME_EP_B200_PAGED_SIMT", "1")
+    test_paged_attention_vs_oracle(ops, 32, 8, 128, 16, [37, 1, 5], [0, 1200, 33], 0, dt)
+
+
 def test_paged_attention_block_outside_cache_reports_error(ops):
     """A block-table entry past the caches is never dereferenced: the append skips that row, the
     attention masks the key, and the device error word records it (then the test clears it)."""
