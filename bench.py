@@ -382,7 +382,9 @@ def paged_kernel_timing(batch, ctx, peaks, peak_kind, reps=5, block=16):
     launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
     alg = 2 * batch * HK * ctx * D * 2 + (q.numel() + k.numel() + v.numel() + out.numel()) * 2
     peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
-    return {"kernel": "paged_append_kernel + paged_attn_kernel", "batch": batch, "context": ctx, "block": block,
+    kern = "paged_append_kernel + " + ("paged_attn_kernel" if os.environ.get("ONNXRUNTIME_EP_B200_PAGED_SIMT")
+                                       else "gqa_mma_decode_kernel<PAGED>")
+    return {"kernel": kern, "batch": batch, "context": ctx, "block": block,
             "launch_us": round(launch_s * 1e6, 2), "algorithmic_bytes_per_launch": alg,
             "achieved": round(alg / launch_s / 1e9, 1), "unit": "GB/s", "frac": round(alg / launch_s / 1e9 / peak, 4),
             "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
