@@ -1416,9 +1416,10 @@ bool mma_decode_path(const b200ep_gqa_params& p, int dtype) {
 // — but no more than two waves of CTAs over the SMs need (one CTA per SM: 207 KB of shared
 // memory), so that many sequences (batch x kv heads >= 148) stream longer runs per CTA.
 int mma_splits(const b200ep_gqa_params& p) {
+  // one wave: the kernel holds one CTA per SM (its K / V streams fill shared memory)
   const int64_t units = (p.cap + kUnit - 1) / kUnit;
   const int64_t heads = std::max<int64_t>(1, p.batch * p.kv_heads);
-  const int64_t by_sms = std::max<int64_t>(1, (2 * num_sms() + heads - 1) / heads);
+  const int64_t by_sms = std::max<int64_t>(1, num_sms() / heads);
   return (int)std::max<int64_t>(1, std::min<int64_t>({8, (units + kMmaWarps - 1) / kMmaWarps, by_sms}));
 }
 
