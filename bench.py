@@ -390,6 +390,52 @@ def paged_kernel_timing(batch, ctx, peaks, peak_kind, reps=5, block=16):
             "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
 
 
+def paged_prompt_timing(S, past, peaks, peak_kind, reps=10, block=16):
+    """PagedAttention over one S-row prompt chunk after `past` cached tokens (32 q / 8 kv heads,
+    head 128, fp16, 16-row blocks, random block table): CUDA-event timing of append + attention,
+    replayed from a CUDA graph.  Useful flops: 4 * H * D per visible (query, key) pair."""
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    H, HK, D = 32, 8, 128
+    nblk = (past + S + block - 1) // block
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kc = torch.randn(nblk, block, HK, D, device="cuda", generator=g).half()
+    vc = torch.randn(nblk, block, HK, D, device="cuda", generator=g).half()
+    bt = torch.randperm(nblk, device="cuda", generator=g).to(torch.int32).reshape(1, nblk)
+    q = torch.randn(S, H * D, device="cuda", generator=g).half()
+    k = torch.randn(S, HK * D, device="cuda", generator=g).half()
+    v = torch.randn(S, HK * D, device="cuda", generator=g).half()
+    cum = torch.tensor([0, S], dtype=torch.int32, device="cuda")
+    pst = torch.tensor([past], dtype=torch.int32, device="cuda")
+    ang = torch.arange(past + S + 8, device="cuda", dtype=torch.float64)[:, None] / (
+        10000.0 ** (torch.arange(D // 2, device="cuda", dtype=torch.float64) / (D // 2)))[None, :]
+    cos, sin = ang.cos().half(), ang.sin().half()
+    out = torch.empty(S, H * D, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        ops.paged_attention(q, k, v, kc, vc, cum, pst, bt, cos, sin, num_heads=H, kv_heads=HK, out=out)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            ops.paged_attention(q, k, v, kc, vc, cum, pst, bt, cos, sin, num_heads=H, kv_heads=HK, out=out)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / reps
+    flops = 4 * H * D * sum(past + i + 1 for i in range(S))
+    peak = float(peaks.get("bf16_tflops", TENSOR_FALLBACK))
+    tf = flops / launch_s / 1e12
+    return {"kernel": "paged_append_kernel + gqa_mma_prefill_kernel<PAGED>", "S": S, "past": past,
+            "launch_us": round(launch_s * 1e6, 2), "achieved": round(tf, 1), "unit": "TFLOP/s",
+            "frac": round(tf / peak, 4), "peak": peak, "peak_source": f"{peak_kind} bf16_tflops"}
+
+
 def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
     """GroupQueryAttention over a whole prompt (32 q / 8 kv heads, head 128, fp16, past 0): the
     rotate-and-append kernel plus the tensor-core prefill kernel, CUDA-event timed over graph
@@ -763,6 +809,9 @@ def main():
             cases = ((args.batch, args.context),) if args.context else ((1, 1024), (8, 1024), (8, 8192), (32, 2048))
             for b, ctx in cases:
                 print(json.dumps(paged_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
+            if not args.context:
+                for S, past in ((512, 0), (2048, 0), (128, 1024)):
+                    print(json.dumps(paged_prompt_timing(S, past, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "gemm":
             for name, m, k, n in GEMM_SHAPES:
                 print(json.dumps(gemm_kernel_timing(name, m, k, n, peaks, peak_kind)), flush=True)

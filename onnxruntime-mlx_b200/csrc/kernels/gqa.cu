@@ -1127,7 +1127,11 @@ struct PfSmem {
   static constexpr int kTotal = 2 * 2 * kTile;   // [buffer][K, V]
 };
 
-template <typename T, int D>
+// PAGED: the PagedAttention form (see GqaKP): blockIdx.z is a sequence whose rows are the packed
+// rows [p_cum[b], p_cum[b + 1]) of kp.S; the preceding append launch wrote their rotated q rows
+// (rounded to T) into the output rows, which each CTA reads before it overwrites them; key tiles
+// take their row addresses from the block table, looked up one tile ahead.
+template <typename T, int D, bool PAGED = false>
 __global__ void __launch_bounds__(kPfWarps * 32)
 gqa_mma_prefill_kernel(GqaKP kp) {
   using L = PfSmem<D>;
@@ -1137,10 +1141,21 @@ gqa_mma_prefill_kernel(GqaKP kp) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int h = blockIdx.y, b = blockIdx.z, kvh = h / kp.G;
-  const int past = past_len(kp, b);
-  if (!range_ok(kp, past)) return;  // reported by gqa_append_kernel
+  int past, Sb;       // past length and rows of this sequence
+  int64_t row0 = 0;   // PAGED: its first packed row
+  if constexpr (PAGED) {
+    row0 = __ldg(kp.p_cum + b);
+    Sb = __ldg(kp.p_cum + b + 1) - (int)row0;
+    past = __ldg(kp.p_past + b);
+    if (Sb <= 0 || row0 < 0 || row0 + Sb > kp.S || past < 0 || (kp.do_rotary && past + Sb > kp.max_seq)) return;
+  } else {
+    past = past_len(kp, b);
+    Sb = kp.S;
+    if (!range_ok(kp, past)) return;  // reported by gqa_append_kernel
+  }
   const int i0 = blockIdx.x * kPfRows;
-  const int ilast = min(kp.S, i0 + kPfRows) - 1;  // last query row of the CTA
+  if (PAGED && i0 >= Sb) return;
+  const int ilast = min(Sb, i0 + kPfRows) - 1;  // last query row of the CTA
   const int win = kp.local_window;
   const int lo_blk = win > 0 ? max(0, past + i0 - win + 1) : 0;
   const int hi_blk = past + ilast;  // last key any row of the CTA sees
@@ -1149,18 +1164,47 @@ gqa_mma_prefill_kernel(GqaKP kp) {
   const T* kvk = static_cast<const T*>(kp.kv_k) + head_base * D;
   const T* kvv = static_cast<const T*>(kp.kv_v) + head_base * D;
 
+  // PAGED: thread r < 64 holds the cache row of key r of the next tile to issue (looked up one tile
+  // ahead; the block table is not written by the append, so the first lookup precedes the wait)
+  __shared__ int prow_s[PAGED ? 2 : 1][PAGED ? kPfKeys : 1];
+  bool bad_row = false;
+  auto lookup = [&](int t) {
+    const int j = t * kPfKeys + (int)threadIdx.x;
+    return threadIdx.x < kPfKeys && j <= hi_blk ? paged_row(kp, b, j) : -1;
+  };
+  int prow_next = 0;
+  if constexpr (PAGED) prow_next = lookup(t0);
   pdl_wait();  // the append kernel wrote the rotated q rows and the new k / v rows
   pdl_trigger();
   auto issue = [&](int t, int buf) {
     unsigned char* kb = sm + buf * 2 * L::kTile;
     unsigned char* vb = kb + L::kTile;
     const int key0 = t * kPfKeys;
-    for (int i = threadIdx.x; i < kPfKeys * D / 8; i += kPfWarps * 32) {
-      const int r = i / (D / 8), ch = i % (D / 8);
-      const bool v = key0 + r <= hi_blk;
-      const int64_t row = v ? key0 + r : 0;
-      cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
-      cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+    if constexpr (PAGED) {
+      if (threadIdx.x < kPfKeys) {
+        bad_row |= key0 + (int)threadIdx.x <= hi_blk && prow_next < 0;
+        prow_s[buf][threadIdx.x] = prow_next;
+      }
+      prow_next = lookup(t + 1);
+      __syncthreads();
+      const T* kc = static_cast<const T*>(kp.kv_k);
+      const T* vc = static_cast<const T*>(kp.kv_v);
+      for (int i = threadIdx.x; i < kPfKeys * D / 8; i += kPfWarps * 32) {
+        const int r = i / (D / 8), ch = i % (D / 8);
+        const int pr = prow_s[buf][r];
+        const bool v = pr >= 0;
+        const int64_t off = v ? ((int64_t)pr * kp.HK + kvh) * D + ch * 8 : 0;
+        cp_async16(kb + swz<D>(r, ch), kc + off, v);
+        cp_async16(vb + swz<D>(r, ch), vc + off, v);
+      }
+    } else {
+      for (int i = threadIdx.x; i < kPfKeys * D / 8; i += kPfWarps * 32) {
+        const int r = i / (D / 8), ch = i % (D / 8);
+        const bool v = key0 + r <= hi_blk;
+        const int64_t row = v ? key0 + r : 0;
+        cp_async16(kb + swz<D>(r, ch), kvk + row * D + ch * 8, v);
+        cp_async16(vb + swz<D>(r, ch), kvv + row * D + ch * 8, v);
+      }
     }
     cp_async_commit();
   };
@@ -1168,12 +1212,24 @@ gqa_mma_prefill_kernel(GqaKP kp) {
 
   // this lane's query rows ra = g and rb = g + 8 of the warp (index i, position past + i)
   const int ia = i0 + warp * 16 + g, ib = ia + 8;
-  const bool va = ia < kp.S, vb_ = ib < kp.S;
+  const bool va = ia < Sb, vb_ = ib < Sb;
   const int qa_pos = past + ia, qb_pos = past + ib;
   const int lo_a = win > 0 ? max(0, qa_pos - win + 1) : 0, lo_b = win > 0 ? max(0, qb_pos - win + 1) : 0;
   // Q as A fragments (the fp32 workspace holds values already rounded through T)
   uint32_t qf[KS][4];
-  {
+  if constexpr (PAGED) {
+    // the rotated rows (already T) in the output buffer
+    const T* qo = static_cast<const T*>(kp.out);
+    const T* qra = qo + ((row0 + (va ? ia : 0)) * kp.H + h) * D;
+    const T* qrb = qo + ((row0 + (vb_ ? ib : 0)) * kp.H + h) * D;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      qf[kk][0] = va ? *reinterpret_cast<const uint32_t*>(qra + kk * 16 + 2 * c) : 0u;
+      qf[kk][1] = vb_ ? *reinterpret_cast<const uint32_t*>(qrb + kk * 16 + 2 * c) : 0u;
+      qf[kk][2] = va ? *reinterpret_cast<const uint32_t*>(qra + kk * 16 + 8 + 2 * c) : 0u;
+      qf[kk][3] = vb_ ? *reinterpret_cast<const uint32_t*>(qrb + kk * 16 + 8 + 2 * c) : 0u;
+    }
+  } else {
     const float* qra = kp.qrot + (((int64_t)b * kp.S + (va ? ia : 0)) * kp.H + h) * D;
     const float* qrb = kp.qrot + (((int64_t)b * kp.S + (vb_ ? ib : 0)) * kp.H + h) * D;
 #pragma unroll
@@ -1189,7 +1245,7 @@ gqa_mma_prefill_kernel(GqaKP kp) {
     }
   }
   // rows of this warp: the first and last keys any of them sees
-  const int wi0 = i0 + warp * 16, wi1 = min(kp.S - 1, wi0 + 15);
+  const int wi0 = i0 + warp * 16, wi1 = min(Sb - 1, wi0 + 15);
   const int w_hi = past + wi1, w_lo = win > 0 ? max(0, past + wi0 - win + 1) : 0;
 
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
@@ -1208,7 +1264,7 @@ gqa_mma_prefill_kernel(GqaKP kp) {
     __syncthreads();
     const int key0 = t * kPfKeys;
     // a warp whose rows all end before this tile (or start after it) skips it
-    if (wi0 < kp.S && key0 <= w_hi && key0 + kPfKeys - 1 >= w_lo) {
+    if (wi0 < Sb && key0 <= w_hi && key0 + kPfKeys - 1 >= w_lo) {
       const unsigned char* kb = sm + buf * 2 * L::kTile;
       const unsigned char* vb = kb + L::kTile;
       float sacc[8][4];
@@ -1250,6 +1306,9 @@ gqa_mma_prefill_kernel(GqaKP kp) {
       const float cb = m_b == -INFINITY ? 0.f : exp2f(m_b - mnb);
       float psa = 0.f, psb = 0.f;
       uint32_t pa[4][4];  // P as A fragments for the tile's four 16-key k-steps
+      // PagedAttention in bf16: P as hi + lo bf16 parts (see gqa_mma_decode_kernel)
+      constexpr bool kPSplit = PAGED && std::is_same<T, __nv_bfloat16>::value;
+      uint32_t pl[kPSplit ? 4 : 1][4];
 #pragma unroll
       for (int nb = 0; nb < 8; ++nb) {
         const float p0 = sacc[nb][0] == -INFINITY ? 0.f : exp2f(sacc[nb][0] - mna);
@@ -1260,6 +1319,10 @@ gqa_mma_prefill_kernel(GqaKP kp) {
         psb += p2 + p3;
         pa[nb >> 1][(nb & 1) * 2] = pack2<T>(p0, p1);
         pa[nb >> 1][(nb & 1) * 2 + 1] = pack2<T>(p2, p3);
+        if constexpr (kPSplit) {
+          pl[nb >> 1][(nb & 1) * 2] = pack2<T>(p0 - round_through<T>(p0), p1 - round_through<T>(p1));
+          pl[nb >> 1][(nb & 1) * 2 + 1] = pack2<T>(p2 - round_through<T>(p2), p3 - round_through<T>(p3));
+        }
       }
       psa += __shfl_xor_sync(0xffffffffu, psa, 1);
       psa += __shfl_xor_sync(0xffffffffu, psa, 2);
@@ -1286,20 +1349,26 @@ gqa_mma_prefill_kernel(GqaKP kp) {
           ldsm_x4_t(bfr, vb + swz<D>(r, n + (lane >> 4)));
           mma_f32<T>(o[n], pa[ks], bfr[0], bfr[1]);
           mma_f32<T>(o[n + 1], pa[ks], bfr[2], bfr[3]);
+          if constexpr (kPSplit) {
+            mma_f32<T>(o[n], pl[ks], bfr[0], bfr[1]);
+            mma_f32<T>(o[n + 1], pl[ks], bfr[2], bfr[3]);
+          }
         }
     }
     __syncthreads();  // the buffer is refilled by the next iteration's prefetch
   }
+  if constexpr (PAGED)
+    if (__syncthreads_or(bad_row) && threadIdx.x == 0) report_device_error(kp.err, kErrGqaRange, b);
 
   T* out = static_cast<T*>(kp.out);
   const float ia_inv = l_a > 0.f ? 1.f / l_a : 0.f, ib_inv = l_b > 0.f ? 1.f / l_b : 0.f;
 #pragma unroll
   for (int n = 0; n < NB; ++n) {
     if (va)
-      *reinterpret_cast<uint32_t*>(out + (((int64_t)b * kp.S + ia) * kp.H + h) * D + n * 8 + 2 * c) =
+      *reinterpret_cast<uint32_t*>(out + ((PAGED ? row0 + ia : (int64_t)b * kp.S + ia) * kp.H + h) * D + n * 8 + 2 * c) =
           pack2<T>(o[n][0] * ia_inv, o[n][1] * ia_inv);
     if (vb_)
-      *reinterpret_cast<uint32_t*>(out + (((int64_t)b * kp.S + ib) * kp.H + h) * D + n * 8 + 2 * c) =
+      *reinterpret_cast<uint32_t*>(out + ((PAGED ? row0 + ib : (int64_t)b * kp.S + ib) * kp.H + h) * D + n * 8 + 2 * c) =
           pack2<T>(o[n][2] * ib_inv, o[n][3] * ib_inv);
   }
 }
@@ -1459,6 +1528,19 @@ bool mma_prefill_path(const b200ep_gqa_params& p, int dtype, int esz) {
 }
 
 template <typename T, int D>
+cudaError_t launch_paged_prefill_t(const GqaKP& kp, int max_rows, cudaStream_t st) {
+  auto kern = gqa_mma_prefill_kernel<T, D, true>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem<D>::kTotal);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_k(kern, dim3(div_up(max_rows, kPfRows), kp.H, kp.p_batch), dim3(kPfWarps * 32),
+                  (size_t)PfSmem<D>::kTotal, st, kp);
+}
+
+template <typename T, int D>
 cudaError_t launch_mma_prefill(const GqaKP& kp, cudaStream_t st) {
   const int warps = 4;
   const int items = kp.B * kp.S * (kp.H + kp.HK);
@@ -1478,6 +1560,39 @@ cudaError_t launch_mma_prefill(const GqaKP& kp, cudaStream_t st) {
 }  // namespace
 
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
+
+// PagedAttention prompt chunks on the tensor-core prefill kernel: the caller has appended the new
+// k / v rows and written the rotated q rows into `out`.
+cudaError_t launch_paged_prefill(const PagedMmaArgs& a, cudaStream_t st) {
+  GqaKP kp{};
+  kp.kv_k = a.key_cache;
+  kp.kv_v = a.value_cache;
+  kp.out = a.out;
+  kp.err = device_error_slot();
+  kp.B = a.batch;
+  kp.S = a.num_tokens;
+  kp.H = a.num_heads;
+  kp.HK = a.kv_heads;
+  kp.D = a.head_size;
+  kp.G = a.num_heads / a.kv_heads;
+  kp.max_seq = a.max_seq;
+  kp.do_rotary = a.do_rotary ? 1 : 0;
+  kp.scale_log2 = a.scale * kLog2e;
+  kp.p_cum = a.cum;
+  kp.p_past = a.past;
+  kp.p_bt = a.block_table;
+  kp.p_batch = a.batch;
+  kp.p_nblocks = a.num_blocks;
+  kp.p_bs = a.block_size;
+  kp.p_maxb = a.max_blocks;
+  // rows of the longest sequence are not known on the host: every sequence gets the row blocks
+  // of all packed rows, and the CTAs past its own rows exit at once
+  if (a.dtype == kF16)
+    return a.head_size == 64 ? launch_paged_prefill_t<__half, 64>(kp, a.num_tokens, st)
+                             : launch_paged_prefill_t<__half, 128>(kp, a.num_tokens, st);
+  return a.head_size == 64 ? launch_paged_prefill_t<__nv_bfloat16, 64>(kp, a.num_tokens, st)
+                           : launch_paged_prefill_t<__nv_bfloat16, 128>(kp, a.num_tokens, st);
+}
 
 // PagedAttention rows on the tensor-core decode kernel (the caller has appended the new rows).
 cudaError_t launch_paged_mma(const PagedMmaArgs& a, cudaStream_t st) {

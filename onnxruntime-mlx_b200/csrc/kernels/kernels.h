@@ -83,5 +83,8 @@ struct PagedMmaArgs {
   float scale;
 };
 cudaError_t launch_paged_mma(const PagedMmaArgs& a, cudaStream_t st);
+// Prompt chunks (the same conditions) on the tensor-core prefill kernel of gqa.cu; the rotated q
+// rows (rounded to the I/O dtype) must already be in `out`.
+cudaError_t launch_paged_prefill(const PagedMmaArgs& a, cudaStream_t st);
 
 }  // namespace b200ep

@@ -6,7 +6,10 @@
 // on the device, so nothing is copied to the host.  Rows with head_size 64 / 128 and at most 8
 // query heads per kv head attend on the tensor-core decode kernel of gqa.cu
 // (gqa_mma_decode_kernel<..., PAGED = true>: per-warp cp.async K / V streams whose row addresses
-// go through the block table, mma.sync scores, cluster merge); paged_attn_kernel covers the rest.
+// go through the block table, mma.sync scores, cluster merge), or, for prompt chunks (16 rows or
+// more per sequence on average), on its prefill kernel (gqa_mma_prefill_kernel<..., PAGED = true>:
+// 64-row query tiles against 64-key tiles fetched through the block table, the rotated q rows
+// handed over in the output buffer); paged_attn_kernel covers the rest.
 //   paged_append_kernel — one CTA per packed token: finds its sequence, RoPEs the new k row at
 //     position past_b + j (fp32, rounded once to the I/O dtype) and writes k and v into their
 //     block-table slot of the caches.
@@ -54,6 +57,7 @@ struct PagedKP {
   void* out;
   DeviceErrorSlot* err;
   int batch, ntok, H, HK, D, G, gm, gchunks, nblocks, bs, maxb, max_seq, half, rot, inter;
+  int qout;  // the append also writes the rotated q rows (rounded) into out (prompt path)
   float scale;
 };
 
@@ -103,28 +107,41 @@ __device__ float rope_at(const float* x, int i, const PagedKP& kp, int pos) {
 
 template <typename T>
 __global__ void __launch_bounds__(128) paged_append_kernel(PagedKP kp) {
-  extern __shared__ float xs[];  // [kv_heads * head_size] new k row, fp32
+  extern __shared__ float xs[];  // [max(heads, kv_heads) * head_size] one row, fp32
   pdl_wait();
   pdl_trigger();
   const int i = blockIdx.x;
   const int b = seq_of(kp, i);
   const int pos = b >= 0 ? __ldg(kp.past + b) + (i - __ldg(kp.cum + b)) : -1;
-  const int slot = b >= 0 ? slot_of(kp, b, pos) : -1;
-  if (slot < 0 || (kp.rot && pos >= kp.max_seq)) {
-    if (threadIdx.x == 0) report_device_error(kp.err, kErrPagedSlot, i);
-    return;
+  const bool pos_ok = pos >= 0 && !(kp.rot && pos >= kp.max_seq);
+  const int slot = pos_ok ? slot_of(kp, b, pos) : -1;
+  if (slot < 0 && threadIdx.x == 0) report_device_error(kp.err, kErrPagedSlot, i);
+  if (!pos_ok) return;
+  if (slot >= 0) {
+    const int row = kp.HK * kp.D;
+    const T* K = static_cast<const T*>(kp.k) + (size_t)i * row;
+    const T* V = static_cast<const T*>(kp.v) + (size_t)i * row;
+    for (int e = threadIdx.x; e < row; e += blockDim.x) xs[e] = to_f<T>(K[e]);
+    __syncthreads();
+    T* kc = static_cast<T*>(kp.kc) + (size_t)slot * row;
+    T* vc = static_cast<T*>(kp.vc) + (size_t)slot * row;
+    for (int e = threadIdx.x; e < row; e += blockDim.x) {
+      const int h = e / kp.D;
+      kc[e] = from_f<T>(rope_at<T>(xs + h * kp.D, e - h * kp.D, kp, pos));
+      vc[e] = V[e];
+    }
   }
-  const int row = kp.HK * kp.D;
-  const T* K = static_cast<const T*>(kp.k) + (size_t)i * row;
-  const T* V = static_cast<const T*>(kp.v) + (size_t)i * row;
-  for (int e = threadIdx.x; e < row; e += blockDim.x) xs[e] = to_f<T>(K[e]);
-  __syncthreads();
-  T* kc = static_cast<T*>(kp.kc) + (size_t)slot * row;
-  T* vc = static_cast<T*>(kp.vc) + (size_t)slot * row;
-  for (int e = threadIdx.x; e < row; e += blockDim.x) {
-    const int h = e / kp.D;
-    kc[e] = from_f<T>(rope_at<T>(xs + h * kp.D, e - h * kp.D, kp, pos));
-    vc[e] = V[e];
+  if (kp.qout) {  // the prompt kernel reads the rotated q rows from out
+    __syncthreads();
+    const int row = kp.H * kp.D;
+    const T* Q = static_cast<const T*>(kp.q) + (size_t)i * row;
+    for (int e = threadIdx.x; e < row; e += blockDim.x) xs[e] = to_f<T>(Q[e]);
+    __syncthreads();
+    T* O = static_cast<T*>(kp.out) + (size_t)i * row;
+    for (int e = threadIdx.x; e < row; e += blockDim.x) {
+      const int h = e / kp.D;
+      O[e] = from_f<T>(rope_at<T>(xs + h * kp.D, e - h * kp.D, kp, pos));
+    }
   }
 }
 
@@ -346,15 +363,23 @@ cudaError_t launch_attn_g(const PagedKP& kp, int splits, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_paged_t(const PagedKP& kp, int dtype, cudaStream_t st) {
-  const size_t app_smem = (size_t)kp.HK * kp.D * sizeof(float);
+cudaError_t launch_paged_t(const PagedKP& kp_in, int dtype, cudaStream_t st) {
+  PagedKP kp = kp_in;
+  const bool mma = (kp.D == 64 || kp.D == 128) && kp.G <= 8 && kp.ntok < 65536 &&
+                   reinterpret_cast<uintptr_t>(kp.q) % 8 == 0 && !getenv("ONNXRUNTIME_EP_B200_PAGED_SIMT");
+  // prompt chunks (16 rows or more per sequence on average) attend as 64-row tiles on the
+  // tensor-core prefill kernel of gqa.cu, which reads the rotated q rows the append leaves in out
+  const bool prompt = mma && (int64_t)kp.ntok >= 16ll * kp.batch && kp.batch <= 65535 &&
+                      (size_t)kp.H * kp.D * sizeof(float) <= 48 * 1024 &&
+                      reinterpret_cast<uintptr_t>(kp.out) % 4 == 0;
+  kp.qout = prompt ? 1 : 0;
+  const size_t app_smem = (size_t)(prompt ? std::max(kp.H, kp.HK) : kp.HK) * kp.D * sizeof(float);
   if (app_smem > 48 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = launch_k(paged_append_kernel<T>, dim3((unsigned)kp.ntok), dim3(128), app_smem, st, kp))
     return e;
   // the tensor-core decode kernel of gqa.cu (cp.async K / V streams, mma.sync scores) where it
   // applies; the SIMT kernel below otherwise
-  if ((kp.D == 64 || kp.D == 128) && kp.G <= 8 && kp.ntok < 65536 &&
-      reinterpret_cast<uintptr_t>(kp.q) % 8 == 0 && !getenv("ONNXRUNTIME_EP_B200_PAGED_SIMT")) {
+  if (mma) {
     PagedMmaArgs a{};
     a.query = kp.q, a.key_cache = kp.kc, a.value_cache = kp.vc;
     a.cum = kp.cum, a.past = kp.past, a.block_table = kp.bt;
@@ -363,7 +388,7 @@ cudaError_t launch_paged_t(const PagedKP& kp, int dtype, cudaStream_t st) {
     a.head_size = kp.D, a.num_blocks = kp.nblocks, a.block_size = kp.bs, a.max_blocks = kp.maxb;
     a.max_seq = kp.max_seq, a.rotary_half = kp.half, a.do_rotary = kp.rot, a.interleaved = kp.inter;
     a.scale = kp.scale;
-    return launch_paged_mma(a, st);
+    return prompt ? launch_paged_prefill(a, st) : launch_paged_mma(a, st);
   }
   // key splits per (token, kv head, query-head chunk): as many as fit one wave of the two CTAs
   // per SM (a partial second wave would double the time of its keys), at most a portable cluster

@@ -518,6 +518,9 @@ def _paged_case(rng, *, H, KV, D, bs, new_lens, pasts, nb_extra=3, rotary=True, 
     (64, 8, 128, 32, [1, 3], [2047, 64], 0),                      # 70B-style group of 8
     (32, 2, 64, 16, [4, 1], [9, 300], 1),                         # group of 16 (two CTAs per kv head)
     (8, 8, 32, 4, [2, 1, 6], [5, 0, 11], 1),                      # MHA, tiny blocks
+    (32, 8, 128, 16, [200], [0], 0),                              # prompt (64-row tiles)
+    (32, 8, 128, 16, [70, 45], [300, 0], 0),                      # two prompt chunks, one after a past
+    (16, 4, 64, 32, [40], [77], 1),                               # prompt chunk, head 64, interleaved
 ])
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_paged_attention_vs_oracle(ops, H, KV, D, bs, new_lens, pasts, inter, dt):
