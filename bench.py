@@ -137,6 +137,9 @@ def dist_setup(n_gpus):
 
         import torch.distributed as dist
 
+        # NCCL's own log (its version banner included, when the environment sets NCCL_DEBUG) goes to
+        # stderr, so that rank 0's stdout carries only the result line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
