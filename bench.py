@@ -137,9 +137,6 @@ def dist_setup(n_gpus):
 
         import torch.distributed as dist
 
-        # NCCL's own log (its version banner included, when the environment sets NCCL_DEBUG) goes to
-        # stderr, so that rank 0's stdout carries only the result line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -822,6 +819,14 @@ def main():
             print(json.dumps(dominant_kernel_roofline(args.batch, peaks, peak_kind, reps=2)), flush=True)
         return
 
+    # N > 1: libraries that write to file descriptor 1 directly (NCCL's version banner when the
+    # environment sets NCCL_DEBUG) write to stderr instead; rank 0 prints the result line on the
+    # original stdout, which then carries that line only
+    out_fd = None
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        sys.stdout.flush()
+        out_fd = os.dup(1)
+        os.dup2(2, 1)
     rank, world, local = dist_setup(args.gpus)
     res = run_ours(args, rank, world, local, tp=args.parallel == "tp")
     if world > 1 and args.parallel == "dp" and not args.no_tp_leg:
@@ -831,7 +836,10 @@ def main():
         res["tp"]["parallelism"] = t["config"]["parallelism"]
         res["tp"]["e2e"] = t["e2e"]["value"]
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        if out_fd is not None:
+            os.write(out_fd, (json.dumps(res) + "\n").encode())
+        else:
+            print(json.dumps(res), flush=True)
     if world > 1:
         import torch.distributed as dist
 
