@@ -2,26 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
 
-Workload (single GPU): 32 layers, hidden 4096, 32/8 heads, head 128, FFN 14336,
-vocab 128256, every projection MatMulNBits int4 block 32 with fp16 scales and uint8 zero points,
-random-init weights (seed 0), int4 GatherBlockQuantized embedding, prompt of 1024 random token
-ids prefilled through the same EP graph (untimed), then decode steps.  One step = one decode
-token for every sequence of the batch: the whole graph runs as one compiled partition (a CUDA
-graph replay) whose positions advance from device-side seqlens_k.
+Workload (the Llama-3-8B-shaped int4 decoder, single GPU): 32 layers, hidden 4096, 32/8 heads,
+head 128, FFN 14336, vocab 128256, every projection MatMulNBits int4 block 32 with fp16 scales and
+uint8 zero points, random-init weights (seed 0), int4 GatherBlockQuantized embedding, prompt of 1024
+random token ids prefilled through the same EP graph (untimed), then decode steps.  One step = one
+decode token for every sequence of the batch: the whole graph runs as one compiled partition (a
+CUDA graph replay) whose positions advance from device-side seqlens_k.
 
 Reported: `value` = decode tokens/s with inputs resident in HBM (CUDA events, max over ranks);
 `e2e` = the same through the compiled partition's C ABI with host buffers (token ids and
 sequence lengths staged host->device, logits read back every step); `roofline` = the dominant
 kernel (the fused gate/up MatMulNBits GEMV) timed live with CUDA events on a weight set larger
-than L2; `cpu_baseline` = the C oracle timed on the host cores for one decoder layer + lm_head
-and extrapolated to 32 layers.  --impl reference times that CPU oracle path alone (the
-reference implementation — Rust over MLX/Metal — cannot run on Linux; ORT's CPU EP is not
-installable here).
+than L2; `cpu_baseline` = the C oracle (a restatement of ORT CPU semantics) timed on every host core
+for whole decode steps (all 32 layers + lm_head).  --impl reference times that CPU path alone, one
+full decode step per timed step (the reference implementation — Rust over MLX/Metal — cannot run
+on Linux, and ORT's CPU EP is not installed on this image).
 
-Multi-GPU: one process per GPU under torchrun, one model sharded over the ranks (tensor
-parallel, strong scaling): q/k/v, gate/up and the vocabulary projection split by output rows
-(attention by KV head), o_proj / down_proj split by K blocks and followed by an NCCL all-reduce,
-the logits all-gathered; every rank decodes the same tokens; value = tokens / max rank time.
+Multi-GPU (N > 1, one process per GPU under torchrun): by default one model sharded over the ranks
+(tensor parallel, strong scaling): q/k/v, gate/up and the vocabulary projection split by output rows
+(attention by KV head), o_proj / down_proj split by K blocks and followed by an all-reduce (peer
+memory for decode rows, NCCL for prompts), the logits all-gathered; every rank decodes the same
+tokens; value = tokens / max rank time.  The line also carries `tp_parity` (the sharded decoder's
+logits against a one-GPU plan of the same graph, prompt + decode steps, compared on rank 0) and
+`replicas` (the same N GPUs as independent data-parallel replicas, weak scaling).  Every rank reads
+the library's device error word after the warm-up and after the timed region; a non-zero code fails
+the run.
 """
 
 from __future__ import annotations
@@ -42,6 +47,14 @@ sys.path.insert(0, ROOT)
 
 PROMPT = 1024
 GEN = 256
+MODEL = "8b"  # --model: "8b" (the headline workload) or "70b"
+MODEL_NAMES = {"8b": "Llama-3-8B", "70b": "Llama-3-70B"}
+
+
+def model_cfg():
+    from onnxruntime_ep_b200.decoder import LLAMA3_8B, LLAMA3_70B
+
+    return {"8b": LLAMA3_8B, "70b": LLAMA3_70B}[MODEL]
 HBM_FALLBACK = 6553.0
 TENSOR_FALLBACK = 1590.0
 
@@ -164,64 +177,130 @@ def max_over_ranks(x, world):
 
 
 # ---- the CPU baseline (oracle port) --------------------------------------------------------
-def cpu_layer_sample(cfg, batch, ctx, threads=0):
-    """One decoder layer + lm_head of a decode step on the C oracle; returns (seconds, desc)."""
-    import numpy as np
+def host_cores():
+    """Host cores this process may run on (the affinity mask, not an inherited OMP_NUM_THREADS)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
 
-    from oracle import oracle
-    from onnxruntime_ep_b200.decoder import quantize_params, rotary_caches
 
-    rng = np.random.default_rng(1)
-    dt = np.float16
-    hid, H, HK, D = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim
-    W = {}
-    for name, n, k in (("q", H * D, hid), ("k", HK * D, hid), ("v", HK * D, hid), ("o", hid, H * D),
-                       ("gate", cfg.ffn, hid), ("up", cfg.ffn, hid), ("down", hid, cfg.ffn),
-                       ("lm", cfg.vocab, hid)):
-        W[name] = (quantize_params(rng, n, k, cfg.block, dt), n, k)
-    x = rng.standard_normal((batch, 1, hid)).astype(dt)
-    g = rng.uniform(0.8, 1.2, hid).astype(dt)
-    cap = ctx + 8
-    kc = rng.standard_normal((batch, HK, cap, D)).astype(dt)
-    vc = rng.standard_normal((batch, HK, cap, D)).astype(dt)
-    cos, sin = rotary_caches(cap + 8, D, 10000.0, dt)
-    seq = np.full(batch, ctx, np.int32)
+class CpuDecoder:
+    """Whole decode steps of the decoder on the C oracle (ORT CPU semantics, every host core): per
+    layer RMS norm, q / k / v, GroupQueryAttention over a shared KV buffer holding `ctx` rows, o,
+    skip RMS norm, gate / up, SiLU * up, down, skip RMS norm; then the final norm and lm_head.  Layer
+    weights are `nsets` distinct random sets used round-robin over the layers (4 x 126 MB of int4
+    records exceed any host cache, so every layer streams its weights from DRAM as a real model
+    does); each layer has its own KV cache."""
 
-    def mnb(a, key):
-        (b, s, z), n, k = W[key]
-        return oracle.matmulnbits(a, b, s, z, N=n, K=k, threads=threads)
+    def __init__(self, cfg, batch, ctx, threads, nsets=4):
+        import numpy as np
 
-    t0 = time.perf_counter()
-    n1 = oracle.rms_norm(x, g, 1e-5, threads=threads)
-    q, k, v = mnb(n1, "q"), mnb(n1, "k"), mnb(n1, "v")
-    attn, _, _ = oracle.gqa(q, k, v, kc, vc, seq, cos, sin, num_heads=H, kv_heads=HK, shared_buffer=True,
-                            threads=threads)
-    o = mnb(attn, "o")
-    n2, r2 = oracle.skip_rms_norm(o, x, g, 1e-5, threads=threads)
-    ga, up = mnb(n2, "gate").astype(np.float32), mnb(n2, "up").astype(np.float32)
-    h = (ga / (1 + np.exp(-ga)) * up).astype(dt)
-    mnb(h, "down")
-    t_layer = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    mnb(n2, "lm")
-    t_lm = time.perf_counter() - t0
-    return t_layer, t_lm
+        from onnxruntime_ep_b200.decoder import quantize_params, rotary_caches
+
+        self.cfg, self.batch, self.ctx, self.threads = cfg, batch, ctx, threads
+        rng = np.random.default_rng(1)
+        dt = np.float16
+        hid, H, HK, D = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim
+        self.sets = []
+        for _ in range(nsets):
+            W = {}
+            for name, n, k in (("q", H * D, hid), ("k", HK * D, hid), ("v", HK * D, hid), ("o", hid, H * D),
+                               ("gate", cfg.ffn, hid), ("up", cfg.ffn, hid), ("down", hid, cfg.ffn)):
+                W[name] = (quantize_params(rng, n, k, cfg.block, dt), n, k)
+            self.sets.append(W)
+        self.lm = (quantize_params(rng, cfg.vocab, hid, cfg.block, dt), cfg.vocab, hid)
+        self.x = rng.standard_normal((batch, 1, hid)).astype(dt)
+        self.g = rng.uniform(0.8, 1.2, hid).astype(dt)
+        cap = ctx + 8
+        self.kv = [(rng.standard_normal((batch, HK, cap, D)).astype(dt),
+                    rng.standard_normal((batch, HK, cap, D)).astype(dt)) for _ in range(cfg.layers)]
+        self.cos, self.sin = rotary_caches(cap + 8, D, 10000.0, dt)
+        self.seq = np.full(batch, ctx, np.int32)
+
+    def _mnb(self, a, w):
+        from oracle import oracle
+
+        (b, s, z), n, k = w
+        return oracle.matmulnbits(a, b, s, z, N=n, K=k, threads=self.threads)
+
+    def step(self, layers=None):
+        """One decode step (one token per sequence) through `layers` layers (default: all) and the
+        vocabulary projection; returns its wall time in seconds."""
+        import numpy as np
+
+        from oracle import oracle
+
+        cfg, th, dt = self.cfg, self.threads, np.float16
+        t0 = time.perf_counter()
+        x, res = self.x, None
+        for li in range(layers or cfg.layers):
+            W = self.sets[li % len(self.sets)]
+            if res is None:
+                n1, res1 = oracle.rms_norm(x, self.g, 1e-5, threads=th), x
+            else:
+                n1, res1 = oracle.skip_rms_norm(x, res, self.g, 1e-5, threads=th)
+            q, k, v = self._mnb(n1, W["q"]), self._mnb(n1, W["k"]), self._mnb(n1, W["v"])
+            kc, vc = self.kv[li]
+            attn, _, _ = oracle.gqa(q, k, v, kc, vc, self.seq, self.cos, self.sin, num_heads=cfg.heads,
+                                    kv_heads=cfg.kv_heads, shared_buffer=True, threads=th)
+            o = self._mnb(attn, W["o"])
+            n2, res = oracle.skip_rms_norm(o, res1, self.g, 1e-5, threads=th)
+            ga, up = self._mnb(n2, W["gate"]).astype(np.float32), self._mnb(n2, W["up"]).astype(np.float32)
+            x = self._mnb((ga / (1 + np.exp(-ga)) * up).astype(dt), W["down"])
+        nf, _ = oracle.skip_rms_norm(x, res, self.g, 1e-5, threads=th)
+        self._mnb(nf, self.lm)
+        return time.perf_counter() - t0
 
 
 def cpu_baseline(cfg, batch, samples=2):
+    """The oracle on every host core for `samples` whole decode steps after one warm step (~10-30 s)."""
     from oracle import oracle
 
     oracle.build()
-    cores = oracle.max_threads()
-    cpu_layer_sample(cfg, batch, PROMPT)  # warm (page in, thread pool)
-    best = None
-    for _ in range(samples):
-        tl, tlm = cpu_layer_sample(cfg, batch, PROMPT)
-        step = cfg.layers * tl + tlm
-        best = step if best is None else min(best, step)
+    cores = host_cores()
+    dec = CpuDecoder(cfg, batch, PROMPT, cores)
+    if cfg.layers <= 32:
+        dec.step()  # warm (page in, thread pool)
+        best = min(dec.step() for _ in range(samples))
+        what = f"{samples} whole B={batch} decode steps ({cfg.layers} layers + lm_head)"
+    else:
+        # deep models: 8 layers + lm_head per sample (the layer time scaled to every layer)
+        dec.step(8)
+        t8 = min(dec.step(8) for _ in range(samples))
+        t0 = min(dec.step(1) for _ in range(samples))  # 1 layer + lm_head: separates the lm_head
+        per_layer = (t8 - t0) / 7
+        best = t0 + (cfg.layers - 1) * per_layer
+        what = (f"8 and 1 layers + lm_head of a B={batch} decode step (best of {samples}), the measured per-layer "
+                f"time {per_layer * 1e3:.0f} ms scaled to {cfg.layers} layers")
     return {"value": batch / best, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"C oracle, 1 decoder layer + lm_head of a B={batch} decode step at context {PROMPT}, "
-                      f"extrapolated to {cfg.layers} layers (best of {samples}); ORT CPU EP unavailable here"}
+            "sample": f"C oracle (ORT CPU semantics), {what} at context {PROMPT} on {cores} threads; ORT's CPU EP "
+                      f"is not installed on this image"}
+
+
+def workload_config(cfg, B, world, mode, n_steps, cap):
+    """The `config` object both arms report (the same keys for the same workload)."""
+    seqs = B if mode in ("tp", "single") else world * B
+    par = {"single": "single GPU",
+           "tp": (f"tp{world}: q/k/v, gate/up and lm_head split by output rows (attention by KV head), o/down "
+                  f"by K blocks + peer-memory (decode) / NCCL (prompt) all-reduce, logits all-gathered"),
+           "dp": (f"dp{world}: data-parallel replicas, a full int4 model and its own sequences per GPU, no "
+                  f"collective on the data path")}[mode]
+    return {"workload": f"{MODEL_NAMES[MODEL]}-shaped int4 decoder, decode step", "layers": cfg.layers,
+            "hidden": cfg.hidden,
+            "heads": f"{cfg.heads}/{cfg.kv_heads}", "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B,
+            "global_batch": seqs, "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + n_steps}",
+            "kv_capacity": cap, "parallelism": par,
+            "l2": f"weights {weight_gb(cfg):.1f} GB/step streamed from HBM (>> 126 MB L2)"}
+
+
+def weight_gb(cfg):
+    """int4 weights + fp16 scales + packed zero points read per decode token (all projections and
+    the vocabulary projection)."""
+    per_layer = (cfg.heads * cfg.head_dim + 2 * cfg.kv_heads * cfg.head_dim) * cfg.hidden + \
+        cfg.hidden * cfg.heads * cfg.head_dim + 3 * cfg.ffn * cfg.hidden
+    params = cfg.layers * per_layer + cfg.vocab * cfg.hidden
+    return params * (0.5 + 2 / cfg.block + 0.5 / cfg.block) / 1e9
 
 
 # ---- the GPU arm ---------------------------------------------------------------------------
@@ -534,22 +613,97 @@ def gemm_kernel_timing(name, M, K, N, peaks, peak_kind, reps=5):
             "peak_source": f"{peak_kind} bf16_tflops (burst)"}
 
 
-def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
-    """One decode measurement.  tp=False: every rank holds a full model and decodes its own
-    sequences (data-parallel replicas, no collective on the data path; weak scaling).  tp=True: one
-    model sharded over the ranks (tensor parallel), the same tokens on every rank (strong scaling)."""
+def device_error_check(where):
+    """Read and clear the library's device error word (bounded waits that expired, bad positions);
+    a non-zero code fails the run instead of reporting a number taken over stalled or wrong steps."""
+    from onnxruntime_ep_b200 import ops
+
+    code, detail = ops.device_error(clear=True)
+    if code:
+        raise RuntimeError(f"device error {code} (detail {detail}) reported by a kernel {where}")
+
+
+def kv_buffers(cfg, B, hk, cap):
+    import torch
+
+    return [[torch.zeros(B, hk, cap, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
+            for _ in range(cfg.layers)]
+
+
+def bind_decoder(part, cfg, kv, ids, seqlens, total, logits):
+    """C-ABI tensor arrays for one run of the decoder partition (KV caches shared past / present)."""
+    from onnxruntime_ep_b200 import ep as E
+
+    feeds = {"input_ids": ids, "seqlens_k": seqlens, "total_sequence_length": total}
+    outs = {"logits": logits}
+    for i in range(cfg.layers):
+        feeds[f"past_key_values.{i}.key"], feeds[f"past_key_values.{i}.value"] = kv[i]
+        outs[f"present.{i}.key"], outs[f"present.{i}.value"] = kv[i]
+    ins = (E.Tensor * len(part.input_names))(*[E.make_tensor(feeds[n]) for n in part.input_names])
+    out = (E.Tensor * len(part.output_names))(*[E.make_tensor(outs[n]) for n in part.output_names])
+    return ins, out
+
+
+def run_part(part, ins, outs, stream):
+    from onnxruntime_ep_b200 import ep as E
+
+    E.check(E._lib().b200ep_compiled_run(part._c, ins, len(part.input_names), outs, len(part.output_names),
+                                         ctypes.c_void_p(stream.cuda_stream)))
+
+
+PARITY_PROMPT, PARITY_STEPS = 16, 4
+
+
+def parity_logits(part, cfg, hk, B):
+    """Logits of a fixed short sequence (a PARITY_PROMPT-token prompt then PARITY_STEPS decode steps,
+    token ids from a fixed seed) through `part`, as one float32 array [rows, vocab] on the host."""
     import numpy as np
     import torch
 
-    from onnxruntime_ep_b200 import ep as E
-    from onnxruntime_ep_b200.decoder import LLAMA3_8B, build_decoder
+    cap = PARITY_PROMPT + PARITY_STEPS + 8
+    kv = kv_buffers(cfg, B, hk, cap)
+    rng = np.random.default_rng(12345)
+    ids = rng.integers(0, cfg.vocab, size=(B, PARITY_PROMPT + PARITY_STEPS), dtype=np.int64)
+    stream = torch.cuda.current_stream()
+    rows = []
+    lg = torch.empty(B, PARITY_PROMPT, cfg.vocab, dtype=torch.float16, device="cuda")
+    ins, outs = bind_decoder(part, cfg, kv, torch.from_numpy(ids[:, :PARITY_PROMPT].copy()).cuda(),
+                             torch.full((B,), PARITY_PROMPT - 1, dtype=torch.int32, device="cuda"),
+                             torch.tensor([PARITY_PROMPT], dtype=torch.int32, device="cuda"), lg)
+    run_part(part, ins, outs, stream)
+    rows.append(lg.float().cpu().numpy().reshape(-1, cfg.vocab))
+    for t in range(PARITY_STEPS):
+        p = PARITY_PROMPT + t
+        lg1 = torch.empty(B, 1, cfg.vocab, dtype=torch.float16, device="cuda")
+        ins, outs = bind_decoder(part, cfg, kv, torch.from_numpy(ids[:, p:p + 1].copy()).cuda(),
+                                 torch.full((B,), p, dtype=torch.int32, device="cuda"),
+                                 torch.tensor([p + 1], dtype=torch.int32, device="cuda"), lg1)
+        run_part(part, ins, outs, stream)
+        rows.append(lg1.float().cpu().numpy().reshape(-1, cfg.vocab))
+    torch.cuda.synchronize()
+    del kv
+    return np.concatenate(rows, 0)
 
-    cfg = LLAMA3_8B
-    B = args.batch
-    cap = PROMPT + GEN + 64
-    n_steps = steps or args.steps
-    tp = tp and world > 1
-    t_build = time.time()
+
+def compare_logits(got, ref):
+    """Composite-decoder comparison: max |diff| against 2e-2 of the reference logit range, and the
+    share of rows whose argmax agrees (ties within the tolerance count as agreement)."""
+    import numpy as np
+
+    rng_ = float(ref.max() - ref.min())
+    d = np.abs(got - ref)
+    tol = 2e-2 * rng_
+    am_g, am_r = got.argmax(-1), ref.argmax(-1)
+    agree = np.mean([(a == b) or (ref[i, a] >= ref[i, b] - tol) for i, (a, b) in enumerate(zip(am_g, am_r))])
+    return {"rows": int(ref.shape[0]), "max_abs": round(float(d.max()), 5), "mean_abs": round(float(d.mean()), 6),
+            "logit_range": round(rng_, 4), "tol": round(tol, 5), "argmax_agree": round(float(agree), 4),
+            "ok": bool(d.max() <= tol and agree >= 0.95)}
+
+
+def build_part(cfg, local, rank, world, tp):
+    from onnxruntime_ep_b200 import ep as E
+    from onnxruntime_ep_b200.decoder import build_decoder
+
     ep = E.ExecutionProvider(device_id=local)
     if tp:
         import torch.distributed as dist
@@ -557,44 +711,39 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
         uid = [E.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ep.set_tensor_parallel(rank, world, uid[0])
-    g = build_decoder(cfg, batch=-1, seq=-1, cap=-1)
-    sess = E.Session(g, ep)
-    part = sess.parts[0]
+    sess = E.Session(build_decoder(cfg, batch=-1, seq=-1, cap=-1), ep)
+    return ep, sess, sess.parts[0]
+
+
+def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None, parity=False):
+    """One decode measurement.  tp=False: every rank holds a full model and decodes its own
+    sequences (data-parallel replicas, no collective on the data path; weak scaling).  tp=True: one
+    model sharded over the ranks (tensor parallel), the same tokens on every rank (strong scaling);
+    parity=True then also compares the sharded logits with a one-GPU plan on rank 0."""
+    import numpy as np
+    import torch
+
+    cfg = model_cfg()
+    B = args.batch
+    cap = PROMPT + GEN + 64
+    n_steps = steps or args.steps
+    tp = tp and world > 1
+    t_build = time.time()
+    ep, sess, part = build_part(cfg, local, rank, world, tp)
     t_build = time.time() - t_build
-
     hk = cfg.kv_heads // world if tp else cfg.kv_heads
-    kv = []
-    for i in range(cfg.layers):
-        kv.append([torch.zeros(B, hk, cap, cfg.head_dim, dtype=torch.float16, device="cuda")
-                   for _ in range(2)])
-    names_in = part.input_names
-    names_out = part.output_names
-
-    def bind(ids, seqlens, total, logits):
-        feeds = {"input_ids": ids, "seqlens_k": seqlens, "total_sequence_length": total}
-        outs = {"logits": logits}
-        for i in range(cfg.layers):
-            feeds[f"past_key_values.{i}.key"], feeds[f"past_key_values.{i}.value"] = kv[i]
-            outs[f"present.{i}.key"], outs[f"present.{i}.value"] = kv[i]
-        ins = (E.Tensor * len(names_in))(*[E.make_tensor(feeds[n]) for n in names_in])
-        out = (E.Tensor * len(names_out))(*[E.make_tensor(outs[n]) for n in names_out])
-        return ins, out
-
-    L = E._lib()
+    kv = kv_buffers(cfg, B, hk, cap)
     stream = torch.cuda.current_stream()
-
-    def step(ins, outs):
-        E.check(L.b200ep_compiled_run(part._c, ins, len(names_in), outs, len(names_out),
-                                      ctypes.c_void_p(stream.cuda_stream)))
+    device_error_check("before the run")
 
     # prefill the prompt through the same graph (untimed)
     rng = np.random.default_rng(0 if tp else rank)
     prompt = torch.from_numpy(rng.integers(0, cfg.vocab, size=(B, PROMPT), dtype=np.int64)).cuda()
     pre_logits = torch.empty(B, PROMPT, cfg.vocab, dtype=torch.float16, device="cuda")
     t_pre = time.time()
-    ins, outs = bind(prompt, torch.full((B,), PROMPT - 1, dtype=torch.int32, device="cuda"),
-                     torch.tensor([PROMPT], dtype=torch.int32, device="cuda"), pre_logits)
-    step(ins, outs)
+    ins, outs = bind_decoder(part, cfg, kv, prompt, torch.full((B,), PROMPT - 1, dtype=torch.int32, device="cuda"),
+                             torch.tensor([PROMPT], dtype=torch.int32, device="cuda"), pre_logits)
+    run_part(part, ins, outs, stream)
     torch.cuda.synchronize()
     t_pre = time.time() - t_pre
     del pre_logits
@@ -606,24 +755,22 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
     logits = torch.empty(B, 1, cfg.vocab, dtype=torch.float16, device="cuda")
     pool = torch.from_numpy(rng.integers(0, cfg.vocab, size=(max(GEN, n_steps + args.warmup) + 8, B, 1),
                                          dtype=np.int64)).cuda()
-    ins, outs = bind(ids, seqlens, total, logits)
+    ins, outs = bind_decoder(part, cfg, kv, ids, seqlens, total, logits)
     n_step = [0]
 
     def decode_step():
         ids.copy_(pool[n_step[0] % pool.shape[0]])
         seqlens.add_(1)
         total.add_(1)
-        step(ins, outs)
+        run_part(part, ins, outs, stream)
         n_step[0] += 1
-
-    def reset_positions():
-        seqlens.fill_(PROMPT - 1)
-        total.fill_(PROMPT)
 
     for _ in range(args.warmup):
         decode_step()
     torch.cuda.synchronize()
-    reset_positions()
+    device_error_check("during the warm-up")
+    seqlens.fill_(PROMPT - 1)
+    total.fill_(PROMPT)
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -634,6 +781,7 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
         e1.record()
         torch.cuda.synchronize()
     barrier(world)
+    device_error_check("in the timed region")
     dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
     seqs = B if tp else world * B  # sequences the whole job decodes per step
     value = seqs * n_steps / dev_s
@@ -643,7 +791,7 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
     h_seq = torch.full((B,), PROMPT - 1, dtype=torch.int32).pin_memory()
     h_tot = torch.tensor([PROMPT], dtype=torch.int32).pin_memory()
     h_logits = torch.empty(B, 1, cfg.vocab, dtype=torch.float16).pin_memory()
-    ins_h, outs_h = bind(h_ids, h_seq, h_tot, h_logits)
+    ins_h, outs_h = bind_decoder(part, cfg, kv, h_ids, h_seq, h_tot, h_logits)
     pool_h = pool.cpu().numpy()
     # numpy views of the pinned buffers: the per-step host updates cost ~1 us instead of a torch
     # CPU op each
@@ -653,7 +801,7 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
         n_ids[...] = pool_h[t % pool_h.shape[0]]
         n_seq[...] += 1
         n_tot[...] += 1
-        step(ins_h, outs_h)  # synchronises: the logits are host-resident
+        run_part(part, ins_h, outs_h, stream)  # synchronises: the logits are host-resident
 
     for t in range(max(2, args.warmup)):
         e2e_step(t)
@@ -668,16 +816,36 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    device_error_check("in the end-to-end region")
     e2e_s = max_over_ranks(max(e0.elapsed_time(e1) / 1e3, wall), world)
     e2e = {"value": round(seqs * n_steps / e2e_s, 2), "unit": "tokens/s",
            "h2d_bytes_per_step": B * 8 + B * 4 + 4, "d2h_bytes_per_step": B * cfg.vocab * 2,
            "path": "b200ep_compiled_run with pinned host tensors"}
 
+    tp_parity = None
+    if tp and parity:
+        # the sharded decoder's logits on a fixed prompt + decode steps (every rank takes the same
+        # collective steps), then a one-GPU plan of the same graph on rank 0
+        got = parity_logits(part, cfg, hk, B)
+        device_error_check("in the parity run")
+        if rank == 0:
+            ep1, sess1, part1 = build_part(cfg, local, 0, 1, False)
+            ref = parity_logits(part1, cfg, cfg.kv_heads, B)
+            del part1, sess1, ep1
+            tp_parity = compare_logits(got, ref)
+            tp_parity["against"] = "one-GPU plan of the same graph (rank 0)"
+        barrier(world)
+
     peaks, peak_kind = measured_peaks()
     roof = dominant_kernel_roofline(B, peaks, peak_kind) if with_cpu else None
     desc = json.loads(part.describe())
+    mode = "tp" if tp else ("dp" if world > 1 else "single")
+    config = workload_config(cfg, B, world, mode, n_steps, cap)
+    config.update({"cuda_graph_replays": desc["graph_replays"], "fused_qkv": desc["fused_qkv"],
+                   "fused_swiglu": desc["fused_swiglu"], "peer_allreduce": desc.get("peer_allreduce", 0),
+                   "prefill_s": round(t_pre, 2), "build_compile_s": round(t_build, 1)})
     result = {
-        "metric": f"int4 decode tokens/s (Llama-3-8B shape, batch {B})",
+        "metric": f"int4 decode tokens/s ({MODEL_NAMES[MODEL]} shape, batch {B})",
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -689,27 +857,16 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
         "vs_baseline": None,
         "dtype": "int4 weights, fp16 activations, fp32 accumulate",
         "data": "synthetic: random-init int4 weights (seed 0), random token ids",
-        "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)",
-                   "layers": cfg.layers, "hidden": cfg.hidden, "heads": f"{cfg.heads}/{cfg.kv_heads}",
-                   "ffn": cfg.ffn, "vocab": cfg.vocab, "batch_per_gpu": B, "global_batch": seqs,
-                   "prompt": PROMPT, "context_during_timing": f"{PROMPT}..{PROMPT + n_steps}",
-                   "kv_capacity": cap,
-                   "parallelism": (f"tp{world}: q/k/v, gate/up and lm_head split by output rows (attention by "
-                                   f"KV head), o/down by K blocks + peer-memory / NCCL all-reduce, logits "
-                                   f"all-gathered")
-                   if tp else (f"dp{world}: data-parallel replicas, a full int4 model and its own sequences "
-                               f"per GPU, no collective on the data path" if world > 1 else "single GPU"),
-                   "l2": "weights 4.4 GB/step streamed from HBM (>> 126 MB L2)",
-                   "cuda_graph_replays": desc["graph_replays"], "fused_qkv": desc["fused_qkv"],
-                   "fused_swiglu": desc["fused_swiglu"], "prefill_s": round(t_pre, 2),
-                   "build_compile_s": round(t_build, 1)},
+        "config": config,
         "e2e": e2e,
         "roofline": roof,
         "clocks": clocks.summary(),
         "gpu_launches": part.launches_per_run() * n_steps,
     }
+    if tp_parity is not None:
+        result["tp_parity"] = tp_parity
     # release the compiled partition (its CUDA graphs hold NCCL calls) before the process group goes
-    del part, sess, ep, ins, outs, ins_h, outs_h
+    del part, sess, ep, ins, outs, ins_h, outs_h, kv
     import gc
 
     gc.collect()
@@ -720,30 +877,27 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None):
 
 
 def run_reference(args, rank, world):
-    """The reference path's CPU timing (oracle port; see module docstring)."""
-    from onnxruntime_ep_b200.decoder import LLAMA3_8B
-
+    """The reference arm: the CPU oracle (the ORT CPU semantics the reference is checked against)
+    on every host core, one whole decode step (32 layers + lm_head) per timed step, rank 0 only."""
     if rank != 0:
         return None
     from oracle import oracle
 
     oracle.build()
-    cfg = LLAMA3_8B
+    cfg = model_cfg()
     B = args.batch
-    cores = oracle.max_threads()
-    for _ in range(max(1, min(args.warmup, 1))):
-        cpu_layer_sample(cfg, B, PROMPT)
-    t_total = 0.0
-    for _ in range(args.steps):
-        tl, tlm = cpu_layer_sample(cfg, B, PROMPT)
-        t_total += cfg.layers * tl + tlm
+    cores = host_cores()
+    dec = CpuDecoder(cfg, B, PROMPT, cores)
+    for _ in range(args.warmup):
+        dec.step()
+    t_total = sum(dec.step() for _ in range(args.steps))
     value = B * args.steps / t_total
-    sample = (f"C oracle (restatement of ORT CPU semantics), one decoder layer + lm_head per step at context "
-              f"{PROMPT}, extrapolated to {cfg.layers} layers; reference (Rust/MLX/Metal) and ORT CPU EP "
-              f"cannot run here")
+    sample = (f"C oracle (restatement of ORT CPU semantics) on {cores} threads, every step a whole decode step "
+              f"({cfg.layers} layers + lm_head) at context {PROMPT}; the reference (Rust over MLX/Metal) cannot "
+              f"run on Linux and ORT's CPU EP is not installed on this image")
     return {
         "impl": "reference",
-        "metric": f"int4 decode tokens/s (Llama-3-8B shape, batch {B})",
+        "metric": f"int4 decode tokens/s ({MODEL_NAMES[MODEL]} shape, batch {B})",
         "value": round(value, 4),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -751,11 +905,11 @@ def run_reference(args, rank, world):
         "warmup": args.warmup,
         "ms_per_step": round(t_total / args.steps * 1e3, 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "int4 weights, fp16 activations, double accumulate",
-        "data": "synthetic",
-        "config": {"workload": "Llama-3-8B-shaped int4 decoder decode step (BASELINE config 4)", "batch": B},
+        "data": "synthetic: random-init int4 weights, random activations",
+        "config": workload_config(cfg, B, world, "tp" if world > 1 else "single", args.steps, PROMPT + GEN + 64),
         "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -768,14 +922,19 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="decoder shape: Llama-3-8B (the headline workload, prompt 1024) or Llama-3-70B "
+                         "(prompt 2048)")
+    ap.add_argument("--prompt", type=int, default=0, help="prompt length prefilled before the timed decode steps")
     ap.add_argument("--context", type=int, default=0,
                     help="--kernel-only paged: time this one (batch, context) case instead of the default set")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
-                    help="N > 1: data-parallel replicas (default, weak scaling) or one tensor-parallel model")
-    ap.add_argument("--no-tp-leg", action="store_true",
-                    help="N > 1 with --parallel dp: skip the tensor-parallel measurement reported beside it")
+    ap.add_argument("--parallel", default="tp", choices=["dp", "tp"],
+                    help="N > 1: one tensor-parallel model (default, strong scaling) or data-parallel replicas")
+    ap.add_argument("--no-side-leg", action="store_true",
+                    help="N > 1: skip the other parallel form's measurement reported beside the headline")
+    ap.add_argument("--no-parity", action="store_true", help="N > 1 tensor parallel: skip the tp_parity check")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm", "paged"],
                     help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
                          "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes; "
@@ -783,6 +942,9 @@ def main():
                          "used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global MODEL, PROMPT
+    MODEL = args.model
+    PROMPT = args.prompt or (2048 if MODEL == "70b" else 1024)
 
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
@@ -828,13 +990,15 @@ def main():
         out_fd = os.dup(1)
         os.dup2(2, 1)
     rank, world, local = dist_setup(args.gpus)
-    res = run_ours(args, rank, world, local, tp=args.parallel == "tp")
-    if world > 1 and args.parallel == "dp" and not args.no_tp_leg:
-        # the tensor-parallel form of the same decoder, measured beside the replicas
-        t = run_ours(args, rank, world, local, tp=True, with_cpu=False, steps=min(args.steps, 32))
-        res["tp"] = {k: t[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling")}
-        res["tp"]["parallelism"] = t["config"]["parallelism"]
-        res["tp"]["e2e"] = t["e2e"]["value"]
+    tp = args.parallel == "tp"
+    res = run_ours(args, rank, world, local, tp=tp, parity=tp and not args.no_parity)
+    if world > 1 and not args.no_side_leg:
+        # the other multi-GPU form of the same decoder, measured beside the headline
+        t = run_ours(args, rank, world, local, tp=not tp, with_cpu=False, steps=min(args.steps, 32))
+        side = {k: t[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling")}
+        side["parallelism"] = t["config"]["parallelism"]
+        side["e2e"] = t["e2e"]["value"]
+        res["replicas" if tp else "tp"] = side
     if rank == 0:
         if out_fd is not None:
             os.write(out_fd, (json.dumps(res) + "\n").encode())

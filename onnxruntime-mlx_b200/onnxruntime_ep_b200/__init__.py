@@ -32,6 +32,8 @@ __all__ = [
     "register_execution_provider_library",
     "append_to_session_options",
     "B200EPError",
+    "PluginEntryPointsMissing",
+    "has_plugin_entry_points",
     "__version__",
 ]
 
@@ -102,8 +104,30 @@ def _import_onnxruntime():
     return ort
 
 
+class PluginEntryPointsMissing(RuntimeError):
+    """The library was built without ONNX Runtime's plugin-EP entry points (CreateEpFactories /
+    ReleaseEpFactory), so ONNX Runtime cannot load it as an execution provider."""
+
+
+def has_plugin_entry_points() -> bool:
+    """Whether libb200ep.so exports ONNX Runtime's plugin-EP factory functions.  They are compiled
+    only against ONNX Runtime's own EP C API headers (onnxruntime_ep_c_api.h, ORT >= 1.29); a build
+    without those headers exports the neutral C ABI of b200ep.h / b200ep_ep.h only."""
+    lib = load_library()
+    return all(hasattr(lib, sym) for sym in ("CreateEpFactories", "ReleaseEpFactory"))
+
+
 def register_execution_provider_library(name: str = EP_NAME) -> str:
-    """Register libb200ep.so with ONNX Runtime under ``name``; returns the library path."""
+    """Register libb200ep.so with ONNX Runtime under ``name``; returns the library path.
+
+    Raises PluginEntryPointsMissing when the library has no CreateEpFactories (built without ONNX
+    Runtime's EP headers) — before onnxruntime is asked to load it — and ImportError when
+    onnxruntime itself is not installed."""
+    if not has_plugin_entry_points():
+        raise PluginEntryPointsMissing(
+            "libb200ep.so was built without ONNX Runtime's plugin-EP entry points (CreateEpFactories / "
+            "ReleaseEpFactory): the EP core is reachable through the C ABI of b200ep_ep.h "
+            "(onnxruntime_ep_b200.ep), but ONNX Runtime cannot load this build as an execution provider")
     ort = _import_onnxruntime()
     if not hasattr(ort, "register_execution_provider_library"):
         raise RuntimeError("this onnxruntime has no register_execution_provider_library (needs >= 1.29)")

@@ -194,26 +194,42 @@ int oracle_matmulnbits(const void* A, const uint8_t* B, const void* scales,
                        int64_t K, int bits, int block, int nthreads) {
   if (!A || !B || !scales || !Y || M < 0 || N <= 0 || K <= 0) return OR_EINVAL;
   if (!is_float_dt(dt)) return OR_EINVAL;
+  if (bits != 4 && bits != 8) return OR_EINVAL;
+  if (block < 16 || (block & (block - 1))) return OR_EINVAL;
   if (M == 0) return OR_OK;
-  float* W = (float*)malloc((size_t)N * (size_t)K * sizeof(float));
   float* Af = (float*)malloc((size_t)M * (size_t)K * sizeof(float));
-  if (!W || !Af) { free(W); free(Af); return OR_EINVAL; }
+  if (!Af) return OR_EINVAL;
   set_threads(nthreads);
-  int rc = oracle_matmulnbits_dequant(B, scales, dt, zp, N, K, bits, block, W);
-  if (rc) { free(W); free(Af); return rc; }
   for (int64_t i = 0; i < M * K; ++i) Af[i] = load_f(A, i, dt);
-#pragma omp parallel for schedule(static) collapse(2)
-  for (int64_t m = 0; m < M; ++m)
+  const int64_t nblocks = (K + block - 1) / block;
+  int failed = 0;
+  /* one output row of W at a time: dequantise it (the same (float)(q - zp) * (float)scale as
+     oracle_matmulnbits_dequant) into a per-thread buffer, then every token's dot product in double */
+#pragma omp parallel reduction(| : failed)
+  {
+    float* w = (float*)malloc((size_t)K * sizeof(float));
+    if (!w) failed = 1;
+#pragma omp for schedule(static)
     for (int64_t n = 0; n < N; ++n) {
-      const float* a = Af + m * K;
-      const float* w = W + n * K;
-      double acc = 0.0;
-      for (int64_t k = 0; k < K; ++k) acc += (double)a[k] * (double)w[k];
-      store_f(Y, m * N + n, dt, acc);
+      if (!w) continue;
+      for (int64_t blk = 0; blk < nblocks; ++blk) {
+        const float sc = load_f(scales, n * nblocks + blk, dt);
+        const int z = mnb_zp(zp, n, blk, nblocks, bits);
+        const int64_t k1 = (blk + 1) * block < K ? (blk + 1) * block : K;
+        for (int64_t k = blk * block; k < k1; ++k)
+          w[k] = (float)(mnb_q(B, n, k, nblocks, bits, block) - z) * sc;
+      }
+      for (int64_t m = 0; m < M; ++m) {
+        const float* a = Af + m * K;
+        double acc = 0.0;
+        for (int64_t k = 0; k < K; ++k) acc += (double)a[k] * (double)w[k];
+        store_f(Y, m * N + n, dt, acc);
+      }
     }
-  free(W);
+    free(w);
+  }
   free(Af);
-  return OR_OK;
+  return failed ? OR_EINVAL : OR_OK;
 }
 
 /* ---- RMS norms ------------------------------------------------------------

@@ -24,8 +24,8 @@ onnxruntime nor onnx_ir is installable here, so this script:
    attention.rs:417-461 and the shared-buffer write of attention.rs:893-902);
 3. writes ``*.npz`` fixtures and ``manifest.json`` next to this file.
 
-Run it in a container that has the reference checkout (path via $REFERENCE_ROOT,
-default /root/reference).  It re-executes itself with PYTHONHASHSEED=0 because
+Run it in a container that has the reference checkout, with $REFERENCE_ROOT set to its path
+(required).  It re-executes itself with PYTHONHASHSEED=0 because
 several reference builders seed their RNG from ``hash((name, ...))``.
 """
 
@@ -41,7 +41,7 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT", "")  # checkout of the reference repository (required)
 
 
 # ---- stand-ins for the ONNX-building calls the reference builders make ----------------------
@@ -446,8 +446,9 @@ def main() -> None:
     if os.environ.get("PYTHONHASHSEED") != "0":
         os.environ["PYTHONHASHSEED"] = "0"
         os.execv(sys.executable, [sys.executable] + sys.argv)
-    if not os.path.isdir(REF):
-        raise SystemExit(f"reference checkout not found at {REF}")
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set REFERENCE_ROOT to a checkout of the reference repository "
+                         f"(got {REF!r})")
     m, nb, ops, g11, captured = reference_namespace()
     manifest: dict = {}
     mnb, gq, nm, gb = {}, {}, {}, {}

@@ -48,3 +48,16 @@ def test_library_reports_version_and_error_text_without_gpu():
     lib = load_library()
     assert lib.b200ep_version() >= 10000
     assert isinstance(lib.b200ep_last_error(), bytes)
+
+
+def test_registration_fails_loudly_without_plugin_entry_points():
+    """ORT's plugin-EP headers are not part of this image, so the library exports no
+    CreateEpFactories; the registration helper must refuse with its own error before any attempt to
+    hand the library to ONNX Runtime (the reference's helper is python/src/onnxruntime_ep_mlx/
+    __init__.py:107-132)."""
+    import onnxruntime_ep_b200 as pkg
+
+    if pkg.has_plugin_entry_points():
+        pytest.skip("this build exports the plugin-EP entry points")
+    with pytest.raises(pkg.PluginEntryPointsMissing, match="CreateEpFactories"):
+        pkg.register_execution_provider_library()

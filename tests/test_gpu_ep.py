@@ -269,3 +269,113 @@ def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
     assert sp["path_prefill"] == 1 and sp["path_decode"] == 0 and sp["compiles"] == 1
     assert sd["path_decode"] == steps and sd["graph_replays"] == d["graph_replays"]
     assert sd["claimed_nodes"] == sd["total_nodes"] and sd["weight_bytes"] > 0 and sd["key_misses"] == 1
+
+
+# One Llama-3-8B-shaped decoder layer (hidden 4096, 32 / 8 heads of 128, SwiGLU FFN 14336, int4 block
+# 32 with fp16 scales and uint8 zero points, RMS eps 1e-5) behind the int4 embedding, with a small
+# vocabulary projection so that the outputs are logits.
+LAYER = dict(layers=1, hidden=4096, heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=512, max_seq=1024)
+
+
+def _compare_logits(got, want, what):
+    """Per element within 1e-2 of the reference logit range; the top-1 token agrees on >= 95 % of
+    the rows (a pick whose reference logit is within that tolerance of the reference maximum counts:
+    a near-tie is not a disagreement)."""
+    rng_ = float(want.max() - want.min())
+    tol = 1e-2 * rng_
+    err = float(np.abs(got - want).max())
+    assert err <= tol, f"{what}: max |diff| {err} > 1e-2 x logit range {rng_}"
+    g2, w2 = got.reshape(-1, got.shape[-1]), want.reshape(-1, want.shape[-1])
+    pick = g2.argmax(-1)
+    agree = float(np.mean(w2[np.arange(len(pick)), pick] >= w2.max(-1) - tol))
+    assert agree >= 0.95, f"{what}: top-1 agreement {agree}"
+
+
+def test_llama_layer_prefill_512_then_decode_matches_oracle(ep_mod):
+    """The one-layer workload: a 512-token prompt (tcgen05 prefill GEMM, tensor-core prompt
+    attention, NCCL-free) then 8 decode steps (fused norm / SiLU GEMV prologues, decode attention,
+    one CUDA graph), every output against the op-by-op oracle of the same graph."""
+    from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
+
+    cfg = DecoderConfig(**LAYER)
+    B, P, cap, steps = 1, 512, 528, 8
+    W = {}
+    g = build_decoder(cfg, batch=-1, seq=-1, cap=-1, weights_out=W)
+    sess = ep_mod.Session(g)
+    rng = np.random.default_rng(11)
+    kv_dev = [[torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]]
+    kv_ref = [[np.zeros((B, cfg.kv_heads, cap, cfg.head_dim), np.float16) for _ in range(2)]]
+
+    def run(ids, past):
+        f = {"input_ids": cuda(ids), "seqlens_k": cuda(np.full(B, past + ids.shape[1] - 1, np.int32)),
+             "total_sequence_length": cuda(np.array([past + ids.shape[1]], np.int32)),
+             "past_key_values.0.key": kv_dev[0][0], "past_key_values.0.value": kv_dev[0][1]}
+        o = {"present.0.key": kv_dev[0][0], "present.0.value": kv_dev[0][1]}
+        return sess.run(f, o)["logits"].float().cpu().numpy()
+
+    ids = rng.integers(0, cfg.vocab, size=(B, P), dtype=np.int64)
+    got = run(ids, 0)
+    want = oracle_decoder_step(cfg, W, ids, kv_ref, np.full(B, P - 1, np.int32)).astype(np.float32)
+    _compare_logits(got, want, "prefill 512")
+    for t in range(steps):
+        ids = rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64)
+        got = run(ids, P + t)
+        want = oracle_decoder_step(cfg, W, ids, kv_ref, np.full(B, P + t, np.int32)).astype(np.float32)
+        _compare_logits(got, want, f"decode step {t}")
+    np.testing.assert_allclose(kv_dev[0][0].float().cpu().numpy()[:, :, :P + steps],
+                               kv_ref[0][0].astype(np.float32)[:, :, :P + steps], rtol=1e-2, atol=1e-2)
+    np.testing.assert_allclose(kv_dev[0][1].float().cpu().numpy()[:, :, :P + steps],
+                               kv_ref[0][1].astype(np.float32)[:, :, :P + steps], rtol=1e-2, atol=1e-2)
+
+
+def _gbq_graph(ep_mod, data, scales, zp, idx_shape, idx_code, code, block):
+    g = ep_mod.GraphBuilder()
+    g.input("ids", idx_code, list(idx_shape))
+    g.initializer("data", data)
+    g.initializer("scales", scales, code)
+    ins = ["data", "ids", "scales"]
+    if zp is not None:
+        g.initializer("zp", zp)
+        ins.append("zp")
+    g.output("y", code, list(idx_shape) + [data.shape[1] * 2])
+    g.node("GatherBlockQuantized", ins, ["y"], domain="com.microsoft", bits=4, block_size=block, gather_axis=0,
+           quantize_axis=1)
+    return g
+
+
+def test_gather_block_quantized_golden(ep_mod):
+    """The reference test's GatherBlockQuantized case (symmetric, block 16, fp32 scales; the fixture
+    holds its inputs and expected rows), claimed by the EP and run on the device."""
+    from conftest import load_golden
+
+    c = {k.split("/", 1)[1]: v for k, v in load_golden("gather_block_quantized.npz").items()}
+    g = _gbq_graph(ep_mod, c["data"], c["scales"], None, c["indices"].shape, ep_mod.INT64, ep_mod.FLOAT, 16)
+    sess = ep_mod.Session(g)
+    assert sess.ep.summary()["claimed_nodes"] == 1
+    y = sess.run({"ids": cuda(c["indices"])})["y"].cpu().numpy()
+    np.testing.assert_array_equal(y, c["y"])
+
+
+@pytest.mark.parametrize("dtype,asym,idx64,dim,block", [
+    (np.float16, True, True, 4096, 32),    # the decoder's embedding: wide rows, one thread per 8 values
+    (np.float16, False, False, 4096, 128),
+    (np.float32, True, False, 96, 32),     # narrow rows: one warp per gathered row
+    (np.float16, True, True, 48, 16),
+])
+def test_gather_block_quantized_matches_oracle(ep_mod, dtype, asym, idx64, dim, block):
+    """Symmetric (zero point 8) and asymmetric (packed uint8 zero points) int4 embeddings
+    (quant.rs:1134-1200), int32 / int64 indices including negative ones, against the oracle;
+    dequantised rows are bit-exact."""
+    rng = np.random.default_rng(dim + block)
+    rows, nb = 300, dim // block
+    data = rng.integers(0, 256, size=(rows, dim // 2), dtype=np.uint8)
+    scales = rng.uniform(0.01, 0.05, size=(rows, nb)).astype(dtype)
+    zp = rng.integers(0, 256, size=(rows, (nb + 1) // 2), dtype=np.uint8) if asym else None
+    ids = rng.integers(-rows, rows, size=(3, 5)).astype(np.int64 if idx64 else np.int32)
+    code = ep_mod.FLOAT16 if dtype == np.float16 else ep_mod.FLOAT
+    g = _gbq_graph(ep_mod, data, scales, zp, ids.shape, ep_mod.INT64 if idx64 else ep_mod.INT32, code, block)
+    sess = ep_mod.Session(g)
+    assert sess.ep.summary()["claimed_nodes"] == 1
+    y = sess.run({"ids": cuda(ids)})["y"].cpu().numpy()
+    want = oracle.gather_block_quantized(data, scales, ids, block_size=block, zero_points=zp)
+    np.testing.assert_array_equal(y, want)

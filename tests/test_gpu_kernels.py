@@ -77,7 +77,7 @@ def test_matmulnbits_dequant_bit_exact(ops, name):
 
 
 def make_mnb(rng, M, K, N, block=32, bits=4, dtype=np.float32, asym=True):
-    """BASELINE config 1 distributions: A ~ N(0,1), scales ~ U(0.005, 0.02), zp ~ U{0..15}."""
+    """Single-MatMulNBits workload distributions: A ~ N(0,1), scales ~ U(0.005, 0.02), zp ~ U{0..15}."""
     nblocks = (K + block - 1) // block
     a = rng.standard_normal((M, K)).astype(dtype)
     q = rng.integers(0, 1 << bits, size=(N, nblocks, block), dtype=np.uint8)
@@ -97,7 +97,7 @@ def make_mnb(rng, M, K, N, block=32, bits=4, dtype=np.float32, asym=True):
 
 @pytest.mark.parametrize("M", [1, 16, 512])
 def test_matmulnbits_config1_fp32(ops, M):
-    """fp32 A [M, 4096], B [4096, 4096] int4 block 32, fp32 scales, uint8 zp."""
+    """Single-MatMulNBits workload: fp32 A [M, 4096], B [4096, 4096] int4 block 32, fp32 scales, uint8 zp."""
     rng = np.random.default_rng(0)
     a, b, s, zp = make_mnb(rng, M, 4096, 4096)
     want = oracle.matmulnbits(a, b, s, zp, N=4096, K=4096)
@@ -256,7 +256,7 @@ def make_gqa_inputs(rng, B, S, H, HK, D, past, cap, dtype=np.float16, max_seq=No
 
 @pytest.mark.parametrize("B,past", [(1, 128), (1, 1024), (1, 8191), (8, 512), (8, 4096)])
 def test_gqa_config2_decode_fp16(ops, B, past):
-    """32 q heads, 8 kv heads, D 128, fp16, rotary base 10000 non-interleaved."""
+    """Single-GQA-decode workload: 32 q heads, 8 kv heads, D 128, fp16, rotary base 10000 non-interleaved."""
     rng = np.random.default_rng(B * 100003 + past)
     H, HK, D, S = 32, 8, 128, 1
     cap = past + S + 7
