@@ -559,6 +559,59 @@ def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
             "peak_source": f"{peak_kind} bf16_tflops (burst)"}
 
 
+def c1_kernel_timing(M, peaks, peak_kind, reps=10):
+    """The single-MatMulNBits workload exactly as specified: fp32 A [M, 4096] ~ N(0, 1), B [4096,
+    4096] int4 block 32, fp32 scales ~ U(0.005, 0.02), uint8 zero points ~ U{0..15}, fp32 output,
+    through the ORT-layout entry point (b200ep_matmulnbits: the fp32 SIMT GEMV / tiled kernel, which
+    keep the fp32 contract's 6e-5 tolerance).  CUDA-event timing over rotating weight copies larger
+    than L2, replayed from a CUDA graph.  Algorithmic bytes: weights + scales + zero points + A + Y."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    K = N = 4096
+    block = 32
+    nb = K // block
+    per = N * nb * block // 2 + N * nb * 4 + N * nb // 2
+    copies = max(3, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ws = []
+    for _ in range(copies):
+        q = torch.randint(0, 16, (N, nb, block), dtype=torch.uint8, device="cuda", generator=g)
+        b = (q[..., 0::2] | (q[..., 1::2] << 4)).contiguous()
+        s = torch.rand(N * nb, device="cuda", generator=g) * 0.015 + 0.005
+        z = torch.randint(0, 16, (N * nb,), dtype=torch.uint8, device="cuda", generator=g)
+        z = (z[0::2] | (z[1::2] << 4)).contiguous()
+        ws.append((b, s, z))
+    a = torch.randn(M, K, device="cuda", generator=g)
+    y = torch.empty(M, N, device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for w in ws:
+            ops.matmulnbits(a, *w, K=K, N=N, out=y)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for w in ws:
+                ops.matmulnbits(a, *w, K=K, N=N, out=y)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    alg = per + M * K * 4 + M * N * 4
+    peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
+    gbs = alg / launch_s / 1e9
+    return {"kernel": "b200ep_matmulnbits fp32 (SIMT GEMV / tiled kernel)", "M": M, "K": K, "N": N,
+            "launch_us": round(launch_s * 1e6, 2), "algorithmic_bytes_per_launch": alg, "achieved": round(gbs, 1),
+            "unit": "GB/s", "frac": round(gbs / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "tflops": round(2 * M * N * K / launch_s / 1e12, 2)}
+
+
 GEMM_SHAPES = (("gate/up", 512, 4096, 28672), ("q/k/v", 512, 4096, 6144), ("o_proj", 512, 4096, 4096),
                ("down", 512, 14336, 4096), ("gate/up", 2048, 4096, 28672))
 
@@ -935,10 +988,10 @@ def main():
     ap.add_argument("--no-side-leg", action="store_true",
                     help="N > 1: skip the other parallel form's measurement reported beside the headline")
     ap.add_argument("--no-parity", action="store_true", help="N > 1 tensor parallel: skip the tp_parity check")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm", "paged"],
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm", "paged", "c1"],
                     help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
                          "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes; "
-                         "paged: PagedAttention decode); "
+                         "paged: PagedAttention decode; c1: the fp32 single-MatMulNBits workload at M 1/16/512); "
                          "used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -974,6 +1027,9 @@ def main():
             if not args.context:
                 for S, past in ((512, 0), (2048, 0), (128, 1024)):
                     print(json.dumps(paged_prompt_timing(S, past, peaks, peak_kind)), flush=True)
+        elif args.kernel_only == "c1":
+            for m in (1, 16, 512):
+                print(json.dumps(c1_kernel_timing(m, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "gemm":
             for name, m, k, n in GEMM_SHAPES:
                 print(json.dumps(gemm_kernel_timing(name, m, k, n, peaks, peak_kind)), flush=True)

@@ -158,6 +158,24 @@ B200EP_API int b200ep_group_query_attention(
     const void* sin_cache, const void* q_norm, const void* k_norm, const void* attention_bias,
     void* out, int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* GroupQueryAttention with sliding_window_cache = 1 (reference: the sliding branch of
+ * group_query_attention_op, rust/src/ops/attention.rs:725-880; claim 1552-1575).  past_key /
+ * past_value and present_key / present_value are [batch, kv_heads, cap, head_size] (present may be
+ * the past buffers themselves); p->cap is that capacity and p->local_window the window W (0 < W <=
+ * cap).  After L tokens a cache holds the last end(L) rows, end(L) = L while L <= cap, else
+ * L - (cap - W + 1) * ceil((L - cap) / (cap - W + 1)): rows are reclaimed from the front.  Query row
+ * i of sequence b (absolute position p_b + i, p_b = seqlens_k[b] + 1 - seq) attends the W most recent
+ * keys (causal window); q / k are rotated at their absolute positions; present receives the rows
+ * kept after this step from row 0 and zeros after them.  Packed or separate q / k / v; no qk norm,
+ * no attention_bias.  workspace: b200ep_gqa_sliding_workspace_size bytes, zero-filled before its
+ * first use (null: a library-owned buffer).  Every length is read on the device. */
+B200EP_API size_t b200ep_gqa_sliding_workspace_size(const b200ep_gqa_params* p, int dtype);
+B200EP_API int b200ep_group_query_attention_sliding(
+    const b200ep_gqa_params* p, const void* query, const void* key, const void* value, const void* past_key,
+    const void* past_value, void* present_key, void* present_value, const int32_t* seqlens_k,
+    const void* cos_cache, const void* sin_cache, void* out, int dtype, void* workspace, size_t workspace_bytes,
+    void* stream);
+
 /* GroupQueryAttention that allocates nothing.  No counterpart in the reference: it exists for
  * callers that may not allocate device memory once running (a server that reserves its HBM
  * budget up front and treats later cudaMalloc as failure; a decode loop that must not allocate or

@@ -265,4 +265,36 @@ B200EP_API int b200ep_group_query_attention(
   B200EP_GUARD_END
 }
 
+B200EP_API size_t b200ep_gqa_sliding_workspace_size(const b200ep_gqa_params* p, int dtype) {
+  try {
+    if (!p || p->batch <= 0 || p->seq <= 0 || p->num_heads <= 0 || p->kv_heads <= 0 ||
+        p->head_size <= 0 || p->num_heads % p->kv_heads || p->cap <= 0)
+      return 0;
+    return gqa_sliding_workspace_bytes(*p, dtype);
+  } catch (...) {
+    return 0;
+  }
+}
+
+B200EP_API int b200ep_group_query_attention_sliding(
+    const b200ep_gqa_params* p, const void* query, const void* key, const void* value, const void* past_key,
+    const void* past_value, void* present_key, void* present_value, const int32_t* seqlens_k,
+    const void* cos_cache, const void* sin_cache, void* out, int dtype, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  B200EP_GUARD_BEGIN
+  B200EP_CHECK_ARG(p != nullptr, "GroupQueryAttention: params is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GqaSlidingArgs a{*p, query, key, value, past_key, past_value, present_key, present_value, seqlens_k,
+                   cos_cache, sin_cache, out, dtype, workspace, workspace_bytes};
+  if (!workspace) {
+    const size_t need = b200ep_gqa_sliding_workspace_size(p, dtype);
+    B200EP_CHECK_ARG(need > 0, "GroupQueryAttention: invalid geometry");
+    int rc = library_gqa_workspace(need, st, &a.workspace);
+    if (rc) return rc;
+    a.workspace_bytes = need;
+  }
+  return launch_gqa_sliding(a, st);
+  B200EP_GUARD_END
+}
+
 }  // extern "C"

@@ -193,6 +193,7 @@ int Plan::lower(const Graph& g, const std::vector<int>& nodes, std::string* err)
         st.do_rotary = (int)(n.int_attr("do_rotary", 1) != 0 && n.input_present(7));
         st.interleaved = (int)n.int_attr("rotary_interleaved", 0);
         st.local_window = (int)n.int_attr("local_window_size", -1);
+        st.sliding = n.int_attr("sliding_window_cache", 0) != 0;
         st.scale = n.float_attr("scale", 0.f);
         st.qk_eps = n.float_attr("qk_norm_epsilon", 1e-6f);
         st.in.resize(16, -1);
@@ -963,7 +964,7 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
         S[st.out[0]].shape = {q.shape[0], q.shape[1], (int64_t)st.num_heads * st.head_size};
         int64_t cap = pk.shape[2];
         const Slot& tot = S[st.in[6]];
-        if (tot.kind == Slot::kInput && !tot.host_copy.empty()) {
+        if (!st.sliding && tot.kind == Slot::kInput && !tot.host_copy.empty()) {
           int32_t t = 0;
           memcpy(&t, tot.host_copy.data(), 4);
           cap = std::max<int64_t>(cap, t);
@@ -1126,6 +1127,40 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
         const int64_t B = q.shape[0], Sq = q.shape[1];
         const int64_t pcap = past_k.shape[2], cap = pres_k.shape[2];
         const int esz = dtype_size(q.dtype);
+        if (s.sliding) {
+          // the sliding-window cache: rows reclaimed from the front, present written from row 0
+          const Slot* cos = s.in[7] >= 0 ? &S[s.in[7]] : nullptr;
+          GqaSlidingArgs a{};
+          a.p.batch = B;
+          a.p.seq = Sq;
+          a.p.num_heads = s.num_heads;
+          a.p.kv_heads = s.kv_heads;
+          a.p.head_size = s.head_size;
+          a.p.cap = pcap;
+          a.p.do_rotary = s.do_rotary && cos;
+          a.p.max_seq = cos ? cos->shape[0] : 0;
+          a.p.rotary_half = cos ? cos->shape[1] : 0;
+          a.p.interleaved = s.interleaved;
+          a.p.packed_qkv = s.packed;
+          a.p.local_window = s.local_window;
+          a.p.scale = s.scale;
+          a.query = q.ptr;
+          a.key = s.packed ? nullptr : S[s.in[1]].ptr;
+          a.value = s.packed ? nullptr : S[s.in[2]].ptr;
+          a.past_key = past_k.ptr;
+          a.past_value = past_v.ptr;
+          a.present_key = pres_k.ptr;
+          a.present_value = pres_v.ptr;
+          a.seqlens_k = static_cast<const int32_t*>(S[s.in[5]].ptr);
+          a.cos_cache = cos ? cos->ptr : nullptr;
+          a.sin_cache = s.in[8] >= 0 ? S[s.in[8]].ptr : nullptr;
+          a.out = S[s.out[0]].ptr;
+          a.dtype = q.dtype;
+          a.workspace = S[s.ws_slot].ptr;
+          a.workspace_bytes = (size_t)S[s.ws_slot].numel();
+          if (int rc = launch_gqa_sliding(a, st)) return rc;
+          break;
+        }
         if (pres_k.ptr != past_k.ptr || pres_v.ptr != past_v.ptr) {
           // growing contract: present = past rows followed by the new rows
           const int64_t rows = std::min(pcap, cap);
@@ -1435,7 +1470,9 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
         p.kv_heads = stp.kv_heads;
         p.head_size = stp.head_size;
         p.cap = prog->slots[stp.out[1]].shape[2];
-        prog->slots[stp.ws_slot].shape = {(int64_t)gqa_workspace_bytes(p)};
+        p.local_window = stp.local_window;
+        prog->slots[stp.ws_slot].shape = {(int64_t)(stp.sliding ? gqa_sliding_workspace_bytes(p, q.dtype)
+                                                                 : gqa_workspace_bytes(p))};
       }
     // allocate temps (and staging for host boundary tensors)
     for (size_t i = 0; i < prog->slots.size(); ++i) {

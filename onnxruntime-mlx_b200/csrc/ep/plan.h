@@ -114,6 +114,7 @@ struct Step {
   int num_heads = 0, kv_heads = 0, head_size = 0;
   bool packed = false;
   int do_rotary = 1, interleaved = 0, local_window = -1;
+  bool sliding = false;  // sliding_window_cache = 1: the cache reclaims rows (gqa_sliding.cu)
   float scale = 0.f, qk_eps = 1e-6f;
   int ws_slot = -1;  // workspace (temp, zero-filled when allocated)
   // binary

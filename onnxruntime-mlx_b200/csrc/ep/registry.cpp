@@ -85,8 +85,20 @@ ClaimResult gqa_claim(const NodeView& v) {
   const size_t nin = v.num_inputs();
   REQUIRE(nin >= 7 && nin <= 16, "expects 7 required inputs plus optional rotary/bias/QK-norm inputs, got %zu", nin);
   const bool sliding = v.int_attr("sliding_window_cache", 0) != 0;
-  REQUIRE(!sliding, "sliding_window_cache is not implemented on this EP");
   const bool has_bias = v.input_present(10);
+  if (sliding) {  // attention.rs:1552-1575
+    const int64_t window = v.int_attr("local_window_size", -1);
+    REQUIRE(window > 0, "sliding_window_cache=1 requires local_window_size > 0");
+    REQUIRE(!has_bias, "sliding_window_cache is incompatible with attention_bias");
+    REQUIRE(v.output_present(1) && v.output_present(2), "sliding_window_cache requires present key/value outputs");
+    auto* pk = v.input_info(3);
+    auto* pv = v.input_info(4);
+    REQUIRE(pk && pk->shape.size() == 4 && pk->shape[2] >= window,
+            "sliding-window key cache capacity must be at least local_window_size");
+    REQUIRE(pv && pv->shape.size() == 4 && pv->shape[2] >= window,
+            "sliding-window value cache capacity must be at least local_window_size");
+    REQUIRE(!v.input_present(14), "sliding_window_cache with q/k norm weights is not implemented on this EP");
+  }
   const bool do_rotary = v.int_attr("do_rotary", 1) != 0;
   REQUIRE(nin != 7 || !do_rotary, "7-input GroupQueryAttention requires do_rotary=0 because cos/sin caches are absent");
   const bool packed = v.input_present(0) && !v.input_present(1) && !v.input_present(2);

@@ -65,6 +65,29 @@ size_t gqa_workspace_bytes(const b200ep_gqa_params& p);
 // Validates geometry (returns a B200EP_* status and message via set_error) and launches.
 int launch_gqa(const GqaArgs& a, cudaStream_t st);
 
+// GroupQueryAttention with sliding_window_cache = 1 (gqa_sliding.cu): past / present [B, kv_heads,
+// cap, D] (they may be the same buffers), p.cap = cap, p.local_window = the window (<= cap); packed
+// or separate q / k / v; no qk norm, no attention_bias.
+struct GqaSlidingArgs {
+  b200ep_gqa_params p;
+  const void* query;
+  const void* key;
+  const void* value;
+  const void* past_key;
+  const void* past_value;
+  void* present_key;
+  void* present_value;
+  const int32_t* seqlens_k;
+  const void* cos_cache;
+  const void* sin_cache;
+  void* out;
+  int dtype;
+  void* workspace;  // gqa_sliding_workspace_bytes, zeroed before its first use
+  size_t workspace_bytes;
+};
+size_t gqa_sliding_workspace_bytes(const b200ep_gqa_params& p, int dtype);
+int launch_gqa_sliding(const GqaSlidingArgs& a, cudaStream_t st);
+
 // PagedAttention rows (fp16 / bf16, head_size 64 / 128, at most 8 query heads per kv head, fewer
 // than 65536 rows, 16-byte aligned caches) on the tensor-core decode kernel of gqa.cu; the new
 // rows must already be in the caches.

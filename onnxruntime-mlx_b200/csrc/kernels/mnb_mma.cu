@@ -243,7 +243,10 @@ constexpr int kMaxStages = 4; // ring stages (chosen per launch: 2..4)
 // times the weight stream at 8-16 rows): up to 16 rows at K = 4096 or 4 rows at K = 14336 (the
 // launch then runs one CTA per SM when two no longer fit)
 constexpr size_t kXStageMax = 144 * 1024;
-constexpr int kG = B200EP_MNB_STAGE_RECORDS;  // records per stage (one bulk copy, ~19 KB for 32 x block 32)
+// records per stage (one bulk copy, ~19 KB for 32 x block 32); long streams of staged activations run
+// twice as many per stage (kGLong), which halves the waits and releases per record
+constexpr int kG = B200EP_MNB_STAGE_RECORDS;
+constexpr int kGLong = 2 * kG;
 constexpr int kXcStride = kG * 64 * 2 + 16;  // bytes per activation row of a stage chunk (padded)
 enum { kErrMnbTimeout = 301 };
 
@@ -307,9 +310,6 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -317,6 +317,15 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 enum { kErrArTimeout = 302 };
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // Consumer side of the peer-memory all-reduce: wait until every source rank published `epoch`
 // (bounded; a timeout records an error and proceeds), then x chunks are sums of the slots.
@@ -589,23 +598,24 @@ __device__ __forceinline__ void mnb_unit(const unsigned char* wq, const unsigned
   }
 }
 
-template <typename T, int BLOCK, int NT, bool PAIR, int NC>
+template <typename T, int BLOCK, int NT, bool PAIR, int NC, int G>
 __global__ void __launch_bounds__((NC + 1) * 32, NC > kNC ? 1 : kMinCtas)
 mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __restrict__ Y, int M, int N, int K,
                int ntiles, int ksteps4, int xrows, int xmode, uint32_t zero, int stages, MnbPro pro, MnbAr oar,
                DeviceErrorSlot* err) {
   using RC = Rec<BLOCK>;
   constexpr int UNIT = RC::kUnit;
-  constexpr int PER = kG / (NC * UNIT);   // units per warp per full stage
-  static_assert(kG % (NC * UNIT) == 0, "stage must split evenly");
+  constexpr int PER = G / (NC * UNIT);   // units per warp per full stage
+  static_assert(G % (NC * UNIT) == 0, "stage must split evenly");
+  static_assert(G == kG || G == kGLong, "stage size");
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int* flags = reinterpret_cast<int*>(empty + kMaxStages);
   unsigned char* buf = smem + 256;
-  // ring stage: kG records, then (xmode 2) the stage's k-range of the 8 NT activation rows,
+  // ring stage: G records, then (xmode 2, G == kG only) the stage's k-range of the 8 NT activation rows,
   // row-major with rows kXcStride bytes apart (bulk-copied beside the records)
-  const size_t rec_bytes = (size_t)kG * RC::kBytes;
+  const size_t rec_bytes = (size_t)G * RC::kBytes;
   const size_t stage_bytes = rec_bytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
   float* red = reinterpret_cast<float*>(buf + (size_t)stages * stage_bytes);  // [2][NC][NT][4][32]
   // staged activation rows (xrows > 0): xrows + 1 rows (the last one zero) of kpad halves,
@@ -635,7 +645,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   // kernel before they read activations or write outputs
   if (warp == NC) {
     if (lane == 0) {
-      // the CTA's records in stages of at most kG that never cross a tile boundary
+      // the CTA's records in stages of at most G that never cross a tile boundary
       int slot = 0;
       uint32_t phase = 0;
       int64_t r = rbeg;
@@ -645,7 +655,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           break;
         }
         const int64_t tile_end = (r / ksteps4 + 1) * ksteps4;
-        const int n = (int)lmin(kG, lmin(rend, tile_end) - r);
+        const int n = (int)lmin(G, lmin(rend, tile_end) - r);
         const uint32_t bytes = (uint32_t)(n * RC::kBytes);
         unsigned char* sbuf = buf + (size_t)slot * stage_bytes;
         if (xmode == 2) {
@@ -669,8 +679,11 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
   pdl_wait();
   pdl_trigger();
-  // tensor-parallel partial output: this launch publishes epoch + 1 (see MnbAr)
+  // tensor-parallel partial output: this launch writes region (epoch + 1) & 1 (see MnbAr)
   const unsigned oepoch = oar.world ? __ldcg(oar.ctrs) + 1 : 0;
+  const size_t obase =
+      oar.world ? kArFlagsBytes + (size_t)(oepoch & 1) * oar.region_bytes + (size_t)oar.rank * oar.slot_bytes : 0;
+  bool pushed = false;  // this thread stored into peer mailboxes
   if (stage_x) {
     if (pro.kind == kProNone) {
       // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
@@ -739,7 +752,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       flags[0] = 1;
       alive = false;
     }
-    const int nplan = min(kG, gend - ga);
+    const int nplan = min(G, gend - ga);
     const int n = alive ? nplan : 0;
     const size_t soff = (size_t)slot * stage_bytes;
     if (xmode == 2) {
@@ -762,7 +775,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         mnb_unit<T, BLOCK, NT, 2, PAIR>(r0 + lane * 16, r0, xp, arow, live, 0, ksteps, g, kq, acc,
                                         xc0 + (uint32_t)(q * 128));
       }
-    } else if (stage_x && n == kG) {
+    } else if (stage_x && n == G) {
       // full stage: every address is a per-stage base plus a compile-time offset
       const int xoff = (ga + warp * UNIT) * 128;
 #pragma unroll
@@ -819,8 +832,11 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           acc[nt][e] = 0.f;
         }
       consumer_barrier<NC>();
+      // thread tid sums output row tid % 16 of token column tid / 16: a column's 16 rows are 16
+      // lanes of one warp, so its outputs (and the tensor-parallel mailbox copies) are one 32-byte
+      // store per destination
       for (int tid = threadIdx.x; tid < 256; tid += NC * 32) {
-        const int row = tid >> 4, col = tid & 15;
+        const int row = tid & 15, col = tid >> 4;
         const int m = m0 + col, n = t * 16 + row;
         if (col < 8 * NT && m < M && n < N) {
           const int nt = col >> 3, cc = col & 7;
@@ -829,7 +845,12 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           float v = 0.f;
 #pragma unroll
           for (int w = 0; w < NC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
-          Y[(size_t)m * N + n] = from_f<T>(v);
+          const T tv = from_f<T>(v);
+          Y[(size_t)m * N + n] = tv;
+          // tensor-parallel partial output: slot `rank` of every rank's mailbox, as the tile completes
+          for (int d = 0; d < oar.world; ++d)
+            *reinterpret_cast<T*>(oar.mbox[d] + obase + ((size_t)m * N + n) * sizeof(T)) = tv;
+          pushed = oar.world > 0;
         }
       }
       ++tp;
@@ -840,30 +861,17 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   }
   if (flags[0] && threadIdx.x == 0) report_device_error(err, kErrMnbTimeout, blockIdx.x);
   if (oar.world) {
-    // publish the partial output: the last CTA to finish pushes Y (M x N, complete once every
-    // CTA's writes are visible) into slot `rank` of every rank's mailbox with 16-byte stores,
-    // fences them at system scope, bumps the epoch and releases the flags
-    __threadfence();
+    // publish: every tile this CTA wrote is already in every rank's mailbox.  The threads that
+    // stored fence at system scope; the CTA then counts itself in (acq_rel), and the last CTA of the
+    // launch — which has observed every other CTA's count, each ordered after that CTA's fences —
+    // records the epoch and releases it in every rank's flag word for this source.
+    if (pushed) __threadfence_system();
     consumer_barrier<NC>();
-    if (threadIdx.x == 0) flags[1] = atomicAdd(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1;
-    consumer_barrier<NC>();
-    if (flags[1]) {
-      __threadfence();
-      const size_t bytes = (size_t)M * N * sizeof(T);  // multiple of 16 (N % 8 == 0)
-      const size_t off = kArFlagsBytes + (size_t)(oepoch & 1) * oar.region_bytes + (size_t)oar.rank * oar.slot_bytes;
-      const uint4* src = reinterpret_cast<const uint4*>(Y);
-      for (int d = 0; d < oar.world; ++d) {
-        uint4* dst = reinterpret_cast<uint4*>(oar.mbox[d] + off);
-        for (size_t i = threadIdx.x; i < bytes / 16; i += NC * 32) dst[i] = __ldcg(src + i);
-      }
-      __threadfence_system();
-      consumer_barrier<NC>();
-      if (threadIdx.x == 0) {
-        oar.ctrs[1] = 0;
-        oar.ctrs[0] = oepoch;
-        for (int d = 0; d < oar.world; ++d)
-          st_release_sys(reinterpret_cast<unsigned*>(oar.mbox[d]) + oar.rank, oepoch);
-      }
+    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1) {
+      oar.ctrs[1] = 0;
+      oar.ctrs[0] = oepoch;
+      for (int d = 0; d < oar.world; ++d)
+        st_release_sys(reinterpret_cast<unsigned*>(oar.mbox[d]) + oar.rank, oepoch);
     }
   }
 }
@@ -920,25 +928,16 @@ cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8
 DeviceErrorSlot* device_error_slot();
 
 namespace {
-template <typename T, int BLOCK, int NT, bool PAIR>
-cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
-                         const MnbAr& oar) {
+template <typename T, int BLOCK, int NT, bool PAIR, int G>
+cudaError_t launch_tma_g(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
+                         const MnbAr& oar, int xrows, int xmode, size_t x_bytes) {
   using RC = Rec<BLOCK>;
-  // activation rows staged in shared memory when they fit (M = 1: K <= 16K)
-  const int rows = (int)std::min<int64_t>(8 * NT, M);
-  const size_t x_bytes = (size_t)(rows + 1) * (p.ksteps4 * 64 * 2 + 16);
-  const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
-  const int xrows = x_bytes <= kXStageMax && (a16 || pro.kind != kProNone) ? rows : 0;
-  if (pro.kind != kProNone && !xrows) return cudaErrorInvalidValue;  // caller checks mnb_prologue_fits
-  // activation modes: 1 = all rows staged once per CTA; 2 = each stage's k-range bulk-copied beside
-  // its records (rows too long to stage whole, e.g. 16 rows at K 14336); 0 = read from global memory
-  const int xmode = xrows ? 1 : (a16 && p.K % 64 == 0 && p.ksteps4 * 64 == p.K) ? 2 : 0;
   // 16-token chunks stage 16 activation rows: one CTA per SM, so it gets twice the consumer warps
   constexpr int NC = NT == 2 ? 2 * kNC : kNC;
   constexpr int kMinC = NC > kNC ? 1 : kMinCtas;
-  auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR, NC>;
+  auto kern = mnb_tma_kernel<T, BLOCK, NT, PAIR, NC, G>;
   auto smem_for = [&](int stages) {
-    const size_t stage = (size_t)kG * RC::kBytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
+    const size_t stage = (size_t)G * RC::kBytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
     return 256 + (size_t)stages * stage + (size_t)2 * NC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   };
   constexpr size_t kSmemCap = 232448;  // dynamic shared memory per CTA on sm_100
@@ -989,6 +988,25 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   return launch_k(kern, dim3((unsigned)ctas, gy), dim3((NC + 1) * 32), smem, st, static_cast<const T*>(A),
                   static_cast<const uint8_t*>(p.w), static_cast<T*>(Y), (int)M, (int)p.N, (int)p.K, (int)p.ntiles,
                   (int)p.ksteps4, xrows, xmode, 0u, stages, pro, oar, device_error_slot());
+}
+
+template <typename T, int BLOCK, int NT, bool PAIR>
+cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
+                         const MnbAr& oar) {
+  // activation rows staged in shared memory when they fit (M = 1: K <= 16K)
+  const int rows = (int)std::min<int64_t>(8 * NT, M);
+  const size_t x_bytes = (size_t)(rows + 1) * (p.ksteps4 * 64 * 2 + 16);
+  const bool a16 = (reinterpret_cast<uintptr_t>(A) & 15) == 0;  // staging reads 16-byte chunks
+  const int xrows = x_bytes <= kXStageMax && (a16 || pro.kind != kProNone) ? rows : 0;
+  if (pro.kind != kProNone && !xrows) return cudaErrorInvalidValue;  // caller checks mnb_prologue_fits
+  // activation modes: 1 = all rows staged once per CTA; 2 = each stage's k-range bulk-copied beside
+  // its records (rows too long to stage whole, e.g. 16 rows at K 14336); 0 = read from global memory
+  const int xmode = xrows ? 1 : (a16 && p.K % 64 == 0 && p.ksteps4 * 64 == p.K) ? 2 : 0;
+  // long streams of whole kGLong-record stages (at least three per CTA) run the long stages
+  const int64_t per_cta = (int64_t)p.ntiles * p.ksteps4 / std::max<int64_t>(1, std::min<int64_t>(p.ntiles, 2 * num_sms()));
+  if (xmode == 1 && p.ksteps4 % kGLong == 0 && per_cta >= 3 * kGLong)
+    return launch_tma_g<T, BLOCK, NT, PAIR, kGLong>(A, p, Y, M, st, pro, oar, xrows, xmode, x_bytes);
+  return launch_tma_g<T, BLOCK, NT, PAIR, kG>(A, p, Y, M, st, pro, oar, xrows, xmode, x_bytes);
 }
 
 template <typename T, int BLOCK>

@@ -56,6 +56,10 @@ def _lib():
         L.b200ep_matmulnbits_prepacked.argtypes = [vp, vp, vp, i32, i64, i64, i64, i32, i32, vp]
         L.b200ep_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), i32]
         L.b200ep_paged_attention.argtypes = [ctypes.POINTER(PagedParams)] + [vp] * 11 + [i32, vp]
+        L.b200ep_gqa_sliding_workspace_size.argtypes = [ctypes.POINTER(GqaParams), i32]
+        L.b200ep_gqa_sliding_workspace_size.restype = ctypes.c_size_t
+        L.b200ep_group_query_attention_sliding.argtypes = (
+            [ctypes.POINTER(GqaParams)] + [vp] * 11 + [i32, vp, ctypes.c_size_t, vp])
         _configured = True
     return L
 
@@ -185,6 +189,30 @@ def group_query_attention(query, key, value, kv_key, kv_value, seqlens_k, cos_ca
         _p(cos_cache), _p(sin_cache), _p(q_norm), _p(k_norm), _p(attention_bias), _p(out), _dt(query),
         _p(workspace), ws_bytes, _stream(query.device)))
     return out
+
+
+def group_query_attention_sliding(query, key, value, past_key, past_value, seqlens_k, cos_cache=None,
+                                  sin_cache=None, *, num_heads, kv_heads, local_window, scale=0.0, do_rotary=1,
+                                  interleaved=0, present_key=None, present_value=None, out=None):
+    """GroupQueryAttention with sliding_window_cache = 1: returns (out, present_key, present_value);
+    present defaults to the past buffers (updated in place)."""
+    import torch
+
+    packed = key is None
+    B, S, W = query.shape
+    D = W // (num_heads + 2 * kv_heads) if packed else W // num_heads
+    p = gqa_params(batch=B, seq=S, num_heads=num_heads, kv_heads=kv_heads, head_size=D, cap=past_key.shape[2],
+                   cos_cache=cos_cache, do_rotary=do_rotary, interleaved=interleaved, packed_qkv=packed,
+                   local_window=local_window, scale=scale)
+    present_key = past_key if present_key is None else present_key
+    present_value = past_value if present_value is None else present_value
+    if out is None:
+        out = torch.empty(B, S, num_heads * D, dtype=query.dtype, device=query.device)
+    check(_lib().b200ep_group_query_attention_sliding(
+        ctypes.byref(p), _p(query), _p(key), _p(value), _p(past_key), _p(past_value), _p(present_key),
+        _p(present_value), _p(seqlens_k), _p(cos_cache), _p(sin_cache), _p(out), _dt(query), None, 0,
+        _stream(query.device)))
+    return out, present_key, present_value
 
 
 def gqa_workspace_size(**kw) -> int:

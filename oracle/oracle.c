@@ -470,6 +470,101 @@ int oracle_gqa(const oracle_gqa_params* p, const void* q, const void* k, const v
   return OR_OK;
 }
 
+/* ---- GroupQueryAttention with a sliding-window KV cache -------------------
+ * attention.rs:725-880 (sliding_window_cache = 1, local_window_size = W, capacity cap >= W;
+ * claim 1552-1575), per batch b with S new rows:
+ *   p      = max(seqlens_k[b] + 1 - S, 0)            absolute position of the first new row
+ *   gap    = cap - W + 1
+ *   end(L) = L if L <= cap, else L - gap * ceil((L - cap) / gap)   rows resident after L tokens
+ *   before = end(p), after = end(p + S), kept = after - S, seed_offset = before - kept
+ *   staging (any batch): kept < min(p, W - 1)
+ *   work   = past[b, :, seed_start : before] ++ the new rows, seed_start = staging ? 0 : seed_offset
+ *   query i (at work row seed_rows + i, seed_rows = before - seed_start) attends work rows
+ *   [seed_rows + i - W + 1, seed_rows + i]; q and k are rotated at absolute positions p + i.
+ *   present[b, :, 0 : after] = work[write_start : write_start + after], the rest zero,
+ *   write_start = staging ? seed_offset : 0.
+ * The attention over `work` is oracle_gqa's (shared buffer, no rotary, local window W). */
+static int64_t sliding_end(int64_t len, int64_t cap, int64_t gap) {
+  if (len <= cap) return len;
+  return len - gap * ((len - cap + gap - 1) / gap);
+}
+
+int oracle_gqa_sliding(const oracle_gqa_params* p, const void* q, const void* k, const void* v,
+                       const void* past_k, const void* past_v, const int32_t* seqlens_k,
+                       const void* cos_c, const void* sin_c, void* out, void* present_k,
+                       void* present_v, int dt, int nthreads) {
+  if (!p || !q || !k || !v || !past_k || !past_v || !seqlens_k || !out || !present_k || !present_v ||
+      !is_float_dt(dt) || p->packed_qkv || p->has_qk_norm || p->bias_batch)
+    return OR_EINVAL;
+  const int64_t B = p->batch, S = p->seq, H = p->num_heads, HK = p->kv_heads, D = p->head_size;
+  const int64_t cap = p->past_cap, W = p->local_window;
+  if (B <= 0 || S <= 0 || H <= 0 || HK <= 0 || D <= 0 || D > 1024 || H % HK) return OR_EINVAL;
+  if (W <= 0 || cap < W || p->present_cap != cap) return OR_EINVAL;
+  if (p->do_rotary && (!cos_c || !sin_c || 2 * p->rotary_half > D || p->rotary_half <= 0)) return OR_EINVAL;
+  const int64_t gap = cap - W + 1, wcap = cap + S, esz = dt == OR_F32 ? 4 : 2;
+  int64_t* geo = (int64_t*)malloc((size_t)B * 4 * sizeof(int64_t));
+  int staging = 0;
+  for (int64_t b = 0; b < B; ++b) {
+    int64_t pp = (int64_t)seqlens_k[b] + 1 - S;
+    if (pp < 0) pp = 0;
+    const int64_t before = sliding_end(pp, cap, gap), after = sliding_end(pp + S, cap, gap);
+    const int64_t kept = after - S, required = pp < W - 1 ? pp : W - 1;
+    if (kept < required) staging = 1;
+    if (p->do_rotary && pp + S > p->max_seq) { free(geo); return OR_ERANGE; }
+    geo[4 * b + 0] = pp, geo[4 * b + 1] = before, geo[4 * b + 2] = after, geo[4 * b + 3] = before - kept;
+  }
+  char* wk = (char*)calloc((size_t)(B * HK * wcap * D), (size_t)esz);
+  char* wv = (char*)calloc((size_t)(B * HK * wcap * D), (size_t)esz);
+  char* qr = (char*)malloc((size_t)(B * S * H * D * esz));
+  char* kr = (char*)malloc((size_t)(B * S * HK * D * esz));
+  int32_t* seq_w = (int32_t*)malloc((size_t)B * sizeof(int32_t));
+  /* work = the seed rows; q / k rotated at their absolute positions, rounded to the I/O dtype */
+  for (int64_t b = 0; b < B; ++b) {
+    const int64_t pp = geo[4 * b], before = geo[4 * b + 1], off = geo[4 * b + 3];
+    const int64_t seed_start = staging ? 0 : off, seed_rows = before - seed_start;
+    seq_w[b] = (int32_t)(seed_rows + S - 1);
+    for (int64_t h = 0; h < HK; ++h) {
+      const size_t src = (size_t)(((b * HK + h) * cap + seed_start) * D * esz);
+      const size_t dst = (size_t)(((b * HK + h) * wcap) * D * esz);
+      memcpy(wk + dst, (const char*)past_k + src, (size_t)(seed_rows * D * esz));
+      memcpy(wv + dst, (const char*)past_v + src, (size_t)(seed_rows * D * esz));
+    }
+    for (int64_t s = 0; s < S; ++s) {
+      float vec[1024];
+      for (int64_t h = 0; h < H + HK; ++h) {
+        const int isk = h >= H;
+        const void* src = isk ? k : q;
+        const int64_t hh = isk ? h - H : h, width = isk ? HK * D : H * D;
+        for (int64_t i = 0; i < D; ++i) vec[i] = load_f(src, (b * S + s) * width + hh * D + i, dt);
+        if (p->do_rotary) rope_vec(vec, D, p->rotary_half, pp + s, cos_c, sin_c, dt, p->interleaved);
+        for (int64_t i = 0; i < D; ++i)
+          store_f(isk ? (void*)kr : (void*)qr, (b * S + s) * width + hh * D + i, dt, vec[i]);
+      }
+    }
+  }
+  oracle_gqa_params ap = *p;
+  ap.past_cap = ap.present_cap = wcap;
+  ap.do_rotary = 0;
+  ap.shared_buffer = 1;
+  ap.local_window = (int32_t)W;
+  int rc = oracle_gqa(&ap, qr, kr, v, wk, wv, seq_w, NULL, NULL, NULL, NULL, NULL, out, wk, wv, dt, nthreads);
+  if (rc == OR_OK) {
+    memset(present_k, 0, (size_t)(B * HK * cap * D * esz));
+    memset(present_v, 0, (size_t)(B * HK * cap * D * esz));
+    for (int64_t b = 0; b < B; ++b) {
+      const int64_t after = geo[4 * b + 2], ws = staging ? geo[4 * b + 3] : 0;
+      for (int64_t h = 0; h < HK; ++h) {
+        const size_t src = (size_t)(((b * HK + h) * wcap + ws) * D * esz);
+        const size_t dst = (size_t)(((b * HK + h) * cap) * D * esz);
+        memcpy((char*)present_k + dst, wk + src, (size_t)(after * D * esz));
+        memcpy((char*)present_v + dst, wv + src, (size_t)(after * D * esz));
+      }
+    }
+  }
+  free(geo), free(wk), free(wv), free(qr), free(kr), free(seq_w);
+  return rc;
+}
+
 /* ---- PagedAttention (com.microsoft) ---------------------------------------
  * paged_attention_op, attention.rs:2495-2746 (SEPARATE K / V caches, no
  * slot_mapping / head_sink / q-k norm, rotary_offset 0):

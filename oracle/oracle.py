@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_rms_norm.argtypes = [vp, vp, vp, i32, i64, i64, f32, i32]
         L.oracle_skip_rms_norm.argtypes = [vp, vp, vp, vp, vp, i32, i64, i64, f32, i32]
         L.oracle_gqa.argtypes = [ctypes.POINTER(GqaParams)] + [vp] * 14 + [i32, i32]
+        L.oracle_gqa_sliding.argtypes = [ctypes.POINTER(GqaParams)] + [vp] * 11 + [i32, i32]
         L.oracle_gather_block_quantized.argtypes = [vp, vp, i32, vp, vp, i64, i64, i64, i32, vp, i32]
         L.oracle_half_to_float.argtypes = [ctypes.c_uint16]
         L.oracle_half_to_float.restype = ctypes.c_float
@@ -238,6 +239,36 @@ def gqa(query, key, value, past_key, past_value, seqlens_k, cos_cache=None, sin_
     ]
     rc = lib().oracle_gqa(ctypes.byref(p), *[_ptr(x) for x in args], code, threads)
     _check(rc, "oracle_gqa")
+    return out, pk, pv
+
+
+def gqa_sliding(query, key, value, past_key, past_value, seqlens_k, cos_cache=None, sin_cache=None, *,
+                num_heads, kv_heads, local_window, scale=0.0, do_rotary=1, interleaved=0, dtype=None, threads=0):
+    """GroupQueryAttention with sliding_window_cache = 1 (attention.rs:725-880): past_key /
+    past_value [B, kv_heads, cap, D] hold the resident rows; returns (attn_output, present_key,
+    present_value) with present at the same capacity (rows beyond the resident ones zero)."""
+    query = np.ascontiguousarray(query)
+    code = _dtype_code(query, dtype)
+    B, S, width = query.shape
+    D = width // num_heads
+    cap = past_key.shape[2]
+    p = GqaParams()
+    p.batch, p.seq, p.num_heads, p.kv_heads, p.head_size = B, S, num_heads, kv_heads, D
+    p.past_cap = p.present_cap = cap
+    p.max_seq = 0 if cos_cache is None else cos_cache.shape[0]
+    p.rotary_half = 0 if cos_cache is None else cos_cache.shape[1]
+    p.do_rotary, p.interleaved = int(do_rotary), int(interleaved)
+    p.shared_buffer, p.local_window, p.scale = 1, int(local_window), float(scale)
+    npdt = _np_dtype(code)
+    out = np.empty((B, S, num_heads * D), dtype=npdt)
+    pk = np.empty((B, kv_heads, cap, D), dtype=npdt)
+    pv = np.empty_like(pk)
+    args = [query, np.ascontiguousarray(key), np.ascontiguousarray(value), np.ascontiguousarray(past_key),
+            np.ascontiguousarray(past_value), np.ascontiguousarray(seqlens_k, dtype=np.int32),
+            None if cos_cache is None else np.ascontiguousarray(cos_cache),
+            None if sin_cache is None else np.ascontiguousarray(sin_cache), out, pk, pv]
+    rc = lib().oracle_gqa_sliding(ctypes.byref(p), *[_ptr(x) for x in args], code, threads)
+    _check(rc, "oracle_gqa_sliding")
     return out, pk, pv
 
 

@@ -234,6 +234,65 @@ def np_gqa(feeds, attrs, *, cap_shared):
     return out, present_k, present_v
 
 
+def np_gqa_sliding(feeds, attrs):
+    """GroupQueryAttention with sliding_window_cache = 1 in float64, following attention.rs:725-880:
+    per batch the resident rows end at end(L) = L - gap * ceil((L - cap) / gap) once L exceeds the
+    capacity (gap = cap - window + 1); the attention runs over the seed rows (from row 0 when any
+    batch's kept rows cannot cover the window: the staging form) followed by the new rows, with the
+    causal window mask; q / k are rotated at their absolute positions; present holds the rows kept
+    after this step from row 0, zeros after them."""
+    H, HK = attrs["num_heads"], attrs["kv_num_heads"]
+    W = attrs["local_window_size"]
+    q = feeds["query"].astype(np.float64)
+    B, S, width = q.shape
+    D = width // H
+    k = feeds["key"].astype(np.float64).reshape(B, S, HK, D).transpose(0, 2, 1, 3)
+    v = feeds["value"].astype(np.float64).reshape(B, S, HK, D).transpose(0, 2, 1, 3)
+    q = q.reshape(B, S, H, D).transpose(0, 2, 1, 3)
+    pk, pv = feeds["past_key"].astype(np.float64), feeds["past_value"].astype(np.float64)
+    cap = pk.shape[2]
+    gap = cap - W + 1
+
+    def end(length):
+        return length if length <= cap else length - gap * ((length - cap + gap - 1) // gap)
+
+    geo, staging = [], False
+    for b in range(B):
+        p = max(int(feeds["seqlens_k"][b]) + 1 - S, 0)
+        before, after = end(p), end(p + S)
+        kept = after - S
+        staging |= kept < min(p, W - 1)
+        geo.append((p, before, after, before - kept))
+    scale = attrs.get("scale") or 1.0 / np.sqrt(D)
+    out = np.zeros((B, H, S, D))
+    present_k, present_v = np.zeros_like(pk), np.zeros_like(pv)
+    for b, (p, before, after, off) in enumerate(geo):
+        qb, kb = q[b], k[b]
+        if attrs.get("do_rotary", 1) and "cos_cache" in feeds:
+            pos = np.arange(p, p + S)
+            il = attrs.get("rotary_interleaved", 0)
+            qb = np_rope(qb, feeds["cos_cache"], feeds["sin_cache"], pos, il).astype(np.float32).astype(np.float64)
+            kb = np_rope(kb, feeds["cos_cache"], feeds["sin_cache"], pos, il).astype(np.float32).astype(np.float64)
+        start = 0 if staging else off
+        wk = np.concatenate([pk[b, :, start:before], kb], axis=1)
+        wv = np.concatenate([pv[b, :, start:before], v[b]], axis=1)
+        seed, klen = before - start, before - start + S
+        qpos = seed + np.arange(S)[:, None]
+        kpos = np.arange(klen)[None, :]
+        allow = (kpos <= qpos) & (kpos >= qpos - W + 1)
+        keys = np.repeat(wk, H // HK, axis=0)
+        vals = np.repeat(wv, H // HK, axis=0)
+        sc = np.matmul(qb, keys.transpose(0, 2, 1)) * scale
+        sc = np.where(allow[None], sc, -np.inf)
+        pr = np.exp(sc - sc.max(-1, keepdims=True))
+        pr /= pr.sum(-1, keepdims=True)
+        out[b] = np.matmul(pr, vals)
+        ws = off if staging else 0
+        present_k[b, :, :after] = wk[:, ws:ws + after]
+        present_v[b, :, :after] = wv[:, ws:ws + after]
+    return out.transpose(0, 2, 1, 3).reshape(B, S, H * D), present_k, present_v
+
+
 # ---- fixture families ----------------------------------------------------------------------
 def gen_matmulnbits(nb, m, out, manifest):
     cases = []
@@ -307,6 +366,14 @@ SHARED_GQA_CASES = [  # tests/ops/test_mlx_ops.py:218-224
     ("shared-decode-norope", dict(batch=1, num_heads=4, kv_heads=2, head=16, seq=1, past=5, cap=32,
                                   do_rotary=0)),
 ]
+SLIDING_GQA_CASES = [  # tests/ops/test_mlx_ops.py:251-297 (sliding_window_cache = 1)
+    ("sliding-decode", dict(batch=1, num_heads=4, kv_heads=2, head=16, seq=1, past=8, cap=5, do_rotary=0,
+                            sliding_window=1, local_window=3)),
+    ("sliding-chunk-staging", dict(batch=1, num_heads=4, kv_heads=2, head=16, seq=3, past=5, cap=5,
+                                   do_rotary=0, sliding_window=1, local_window=4)),
+    ("sliding-batched-rope", dict(batch=2, num_heads=4, kv_heads=2, head=16, seq=1, past=7, cap=6,
+                                  do_rotary=1, sliding_window=1, local_window=4)),
+]
 GQA11_CASES = [  # tests/ops/test_gqa11.py:215-221
     ("prefill", dict(batch=1, seq=6, past=0, cap=6, num_heads=4, kv_heads=2, head=16, window=4)),
     ("chunked", dict(batch=1, seq=3, past=4, cap=7, num_heads=4, kv_heads=2, head=16, window=3)),
@@ -340,6 +407,12 @@ def gen_gqa(m, g11, captured, out, manifest):
         attrs = dict(_captured["last_model"]["attributes"])
         _store_gqa(out, manifest, f"gqa/{name}", feeds, attrs, np_gqa(feeds, attrs, cap_shared=True),
                    shared=True, source="tests/ops/_models.py:gqa_shared_buffer_model")
+    for name, geom in SLIDING_GQA_CASES:
+        _model, feeds = m.gqa_shared_buffer_model(name, **geom)
+        attrs = dict(_captured["last_model"]["attributes"])
+        _store_gqa(out, manifest, f"gqasliding/{name}", feeds, attrs, np_gqa_sliding(feeds, attrs), shared=True,
+                   source="tests/ops/_models.py:gqa_shared_buffer_model (sliding_window=1)")
+        manifest[f"gqasliding/{name}"]["family"] = "gqa_sliding"
     for name, geom in GQA11_CASES:
         _model, feeds = g11["_gqa11_model"](with_position_ids=False, **geom)
         attrs = dict(_captured["attrs11"])

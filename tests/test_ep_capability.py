@@ -66,7 +66,8 @@ def test_matmulnbits_declines_with_reason(kw, reason):
 
 
 def gqa_graph(*, packed=False, do_rotary=1, nin=9, softcap=0.0, qk_output=0, smooth=0, pos_ids=False,
-              dtype=FLOAT16, cos_dtype=None, kquant=None, qk_norm=False, present=True):
+              dtype=FLOAT16, cos_dtype=None, kquant=None, qk_norm=False, present=True, sliding_window=None,
+              bias=False):
     g = GraphBuilder()
     B, S, H, HK, D, cap = 1, 1, 4, 2, 16, 32
     qw = (H + 2 * HK) * D if packed else H * D
@@ -88,6 +89,11 @@ def gqa_graph(*, packed=False, do_rotary=1, nin=9, softcap=0.0, qk_output=0, smo
     if pos_ids:
         g.input("pos", INT64, [B, S])
         ins += ["pos"]
+    if bias:
+        while len(ins) < 10:
+            ins.append("")
+        g.input("bias", dtype, [B, 1, S, cap])
+        ins.append("bias")
     if qk_norm:
         while len(ins) < 14:
             ins.append("")
@@ -110,12 +116,15 @@ def gqa_graph(*, packed=False, do_rotary=1, nin=9, softcap=0.0, qk_output=0, smo
         attrs["smooth_softmax"] = smooth
     if kquant:
         attrs["k_quant_type"] = kquant
+    if sliding_window is not None:
+        attrs["sliding_window_cache"] = 1
+        attrs["local_window_size"] = sliding_window
     g.node("GroupQueryAttention", ins, outs, domain="com.microsoft", **attrs)
     return g
 
 
 @pytest.mark.parametrize("kw", [dict(), dict(packed=True), dict(nin=7, do_rotary=0), dict(dtype=FLOAT),
-                                dict(qk_norm=True)])
+                                dict(qk_norm=True), dict(sliding_window=16), dict(sliding_window=32, packed=True)])
 def test_gqa_claims(kw):
     _, groups, _ = claimed(gqa_graph(**kw))
     assert groups == [0]
@@ -128,6 +137,11 @@ def test_gqa_claims(kw):
     (dict(smooth=1), "smooth_softmax"),
     (dict(kquant="PER_TENSOR"), "quantized KV"),
     (dict(cos_dtype=FLOAT), "must have output dtype"),
+    # sliding-window cache conditions (attention.rs:1552-1575)
+    (dict(sliding_window=0), "local_window_size > 0"),
+    (dict(sliding_window=8, bias=True), "incompatible with attention_bias"),
+    (dict(sliding_window=8, present=False), "present key/value"),
+    (dict(sliding_window=64), "capacity must be at least local_window_size"),
 ])
 def test_gqa_declines_with_reason(kw, reason):
     ep, groups, _ = claimed(gqa_graph(**kw))

@@ -275,6 +275,8 @@ def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
 # 32 with fp16 scales and uint8 zero points, RMS eps 1e-5) behind the int4 embedding, with a small
 # vocabulary projection so that the outputs are logits.
 LAYER = dict(layers=1, hidden=4096, heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=512, max_seq=1024)
+# One Llama-3-70B-shaped layer: hidden 8192, 64 / 8 heads of 128, FFN 28672.
+LAYER_70B = dict(layers=1, hidden=8192, heads=64, kv_heads=8, head_dim=128, ffn=28672, vocab=512, max_seq=1024)
 
 
 def _compare_logits(got, want, what):
@@ -291,14 +293,16 @@ def _compare_logits(got, want, what):
     assert agree >= 0.95, f"{what}: top-1 agreement {agree}"
 
 
-def test_llama_layer_prefill_512_then_decode_matches_oracle(ep_mod):
-    """The one-layer workload: a 512-token prompt (tcgen05 prefill GEMM, tensor-core prompt
-    attention, NCCL-free) then 8 decode steps (fused norm / SiLU GEMV prologues, decode attention,
-    one CUDA graph), every output against the op-by-op oracle of the same graph."""
+@pytest.mark.parametrize("shape,P,steps", [("8b", 512, 8), ("70b", 64, 4)])
+def test_llama_layer_prefill_then_decode_matches_oracle(ep_mod, shape, P, steps):
+    """One decoder layer: a prompt (512 tokens for the Llama-3-8B layer, 64 for the Llama-3-70B
+    layer: tcgen05 prefill GEMM, tensor-core prompt attention) then decode steps (fused norm / SiLU
+    GEMV prologues, decode attention, one CUDA graph), every output against the op-by-op oracle of
+    the same graph."""
     from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
 
-    cfg = DecoderConfig(**LAYER)
-    B, P, cap, steps = 1, 512, 528, 8
+    cfg = DecoderConfig(**(LAYER if shape == "8b" else LAYER_70B))
+    B, cap = 1, P + steps + 16
     W = {}
     g = build_decoder(cfg, batch=-1, seq=-1, cap=-1, weights_out=W)
     sess = ep_mod.Session(g)
@@ -316,7 +320,7 @@ def test_llama_layer_prefill_512_then_decode_matches_oracle(ep_mod):
     ids = rng.integers(0, cfg.vocab, size=(B, P), dtype=np.int64)
     got = run(ids, 0)
     want = oracle_decoder_step(cfg, W, ids, kv_ref, np.full(B, P - 1, np.int32)).astype(np.float32)
-    _compare_logits(got, want, "prefill 512")
+    _compare_logits(got, want, f"prefill {P}")
     for t in range(steps):
         ids = rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64)
         got = run(ids, P + t)
@@ -379,3 +383,63 @@ def test_gather_block_quantized_matches_oracle(ep_mod, dtype, asym, idx64, dim, 
     y = sess.run({"ids": cuda(ids)})["y"].cpu().numpy()
     want = oracle.gather_block_quantized(data, scales, ids, block_size=block, zero_points=zp)
     np.testing.assert_array_equal(y, want)
+
+
+def test_gqa_sliding_window_cache_through_ep(ep_mod):
+    """GroupQueryAttention with sliding_window_cache = 1 claimed by the EP and run as a compiled plan
+    with present bound to the past buffers (a 20-row prompt, then 30 decode steps from persistent
+    device inputs, so the decode runs replay one CUDA graph): outputs and cache rows against the
+    oracle at every step."""
+    B, H, HK, D, cap, W = 1, 8, 2, 64, 32, 16
+    g = ep_mod.GraphBuilder()
+    code = ep_mod.FLOAT16
+    g.input("q", code, [B, -1, H * D])
+    g.input("k", code, [B, -1, HK * D])
+    g.input("v", code, [B, -1, HK * D])
+    g.input("pk", code, [B, HK, cap, D])
+    g.input("pv", code, [B, HK, cap, D])
+    g.input("seqlens", ep_mod.INT32, [B])
+    g.input("total", ep_mod.INT32, [1])
+    half = D // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half) / half))
+    ang = np.arange(128)[:, None] * inv[None, :]
+    cos, sin = np.cos(ang).astype(np.float16), np.sin(ang).astype(np.float16)
+    g.initializer("cos", cos, code)
+    g.initializer("sin", sin, code)
+    g.output("out", code, [B, -1, H * D])
+    g.output("prk", code, [B, HK, cap, D])
+    g.output("prv", code, [B, HK, cap, D])
+    g.node("GroupQueryAttention", ["q", "k", "v", "pk", "pv", "seqlens", "total", "cos", "sin"], ["out", "prk", "prv"],
+           domain="com.microsoft", num_heads=H, kv_num_heads=HK, do_rotary=1, sliding_window_cache=1,
+           local_window_size=W)
+    sess = ep_mod.Session(g)
+    assert sess.ep.summary()["claimed_nodes"] == 1
+    rng = np.random.default_rng(5)
+    tk = torch.zeros(B, HK, cap, D, dtype=torch.float16, device="cuda")
+    tv = torch.zeros_like(tk)
+    ok, ov = np.zeros((B, HK, cap, D), np.float16), np.zeros((B, HK, cap, D), np.float16)
+    dq, dk, dv = (torch.zeros(B, 1, w, dtype=torch.float16, device="cuda") for w in (H * D, HK * D, HK * D))
+    dseq = torch.zeros(B, dtype=torch.int32, device="cuda")
+    dtot = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dout = torch.zeros(B, 1, H * D, dtype=torch.float16, device="cuda")
+    n = 0
+    for step, S in enumerate([20] + [1] * 30):
+        q = rng.standard_normal((B, S, H * D)).astype(np.float16)
+        k = rng.standard_normal((B, S, HK * D)).astype(np.float16)
+        v = rng.standard_normal((B, S, HK * D)).astype(np.float16)
+        seq = np.full(B, n + S - 1, np.int32)
+        want, ok, ov = oracle.gqa_sliding(q, k, v, ok, ov, seq, cos, sin, num_heads=H, kv_heads=HK, local_window=W)
+        if S == 1:  # persistent device inputs, updated in place
+            dq.copy_(cuda(q)), dk.copy_(cuda(k)), dv.copy_(cuda(v))
+            dseq.fill_(int(seq[0])), dtot.fill_(n + S)
+            res = sess.run({"q": dq, "k": dk, "v": dv, "pk": tk, "pv": tv, "seqlens": dseq, "total": dtot},
+                           {"out": dout, "prk": tk, "prv": tv})
+        else:
+            res = sess.run({"q": cuda(q), "k": cuda(k), "v": cuda(v), "pk": tk, "pv": tv, "seqlens": cuda(seq),
+                            "total": cuda(np.array([n + S], np.int32))}, {"prk": tk, "prv": tv})
+        np.testing.assert_allclose(res["out"].float().cpu().numpy(), want.astype(np.float32), rtol=1e-2, atol=1e-3,
+                                   err_msg=f"step {step}")
+        np.testing.assert_allclose(tk.float().cpu().numpy(), ok.astype(np.float32), rtol=1e-2, atol=1e-3)
+        np.testing.assert_array_equal(tv.cpu().numpy(), ov)
+        n += S
+    assert json.loads(sess.parts[0].describe())["graph_replays"] >= 25

@@ -367,6 +367,81 @@ def test_gqa_repeated_decode_steps_match_oracle(ops):
     np.testing.assert_array_equal(to_np(tk), ok)
 
 
+SLIDING_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "gqa_sliding")
+
+
+@pytest.mark.parametrize("name", SLIDING_CASES)
+def test_gqa_sliding_window_cache_golden(ops, name):
+    """The reference test's sliding-window cache geometries (tests/ops/test_mlx_ops.py:251-323: a
+    decode step that reclaims rows, a 3-row chunk in the staging form, a batched step with rotary),
+    fp32, through b200ep_group_query_attention_sliding; present compared over the resident rows and
+    zero after them."""
+    meta, c = MANIFEST[name], golden_case(GQA, name)
+    a = meta["attrs"]
+    tk, tv = cuda(c["past_key"]), cuda(c["past_value"])
+    out, pk, pv = ops.group_query_attention_sliding(
+        cuda(c["query"]), cuda(c["key"]), cuda(c["value"]), tk, tv, cuda(c["seqlens_k"]),
+        cuda(c["cos_cache"]) if "cos_cache" in c else None, cuda(c["sin_cache"]) if "sin_cache" in c else None,
+        num_heads=a["num_heads"], kv_heads=a["kv_num_heads"], local_window=a["local_window_size"],
+        scale=a.get("scale", 0.0), do_rotary=a.get("do_rotary", 1) if "cos_cache" in c else 0)
+    np.testing.assert_allclose(to_np(out), c["out"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(to_np(pk), c["present_key"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(to_np(pv), c["present_value"])
+
+
+@pytest.mark.parametrize("dt", [np.float16, "bf16"])
+def test_gqa_sliding_window_cache_decode_run(ops, dt):
+    """A 40-row prompt then 40 decode steps on a 48-row cache with a 32-key window (rows reclaimed 17
+    at a time, three times), two sequences of different lengths, 32 / 8 heads of 128 with rotary: every
+    step's output and the resident cache rows against the oracle run on the same state."""
+    rng = np.random.default_rng(21)
+    B, H, HK, D, cap, W = 2, 32, 8, 128, 48, 32
+    npdt = np.float16 if dt == np.float16 else np.float32
+    def cast(x):
+        x = np.asarray(x, np.float32)
+        return x.astype(np.float16) if dt == np.float16 else oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(x))
+    def dev(x):
+        t = cuda(np.ascontiguousarray(x, np.float32))
+        return t.half() if dt == np.float16 else t.bfloat16()
+    def host(t):
+        return t.float().cpu().numpy()
+    half = D // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half) / half))
+    ang = np.arange(128)[:, None] * inv[None, :]
+    cos, sin = cast(np.cos(ang)), cast(np.sin(ang))
+    okc = np.zeros((B, HK, cap, D), np.float32)
+    ovc = np.zeros_like(okc)
+    tk, tv = dev(okc), dev(ovc)
+    lens = np.array([0, 5])  # sequence 1 starts 5 tokens ahead (its first 5 rows were filled before)
+    okc[1, :, :5] = cast(rng.standard_normal((HK, 5, D)))
+    ovc[1, :, :5] = cast(rng.standard_normal((HK, 5, D)))
+    tk.copy_(dev(okc)), tv.copy_(dev(ovc))
+    code = None if dt == np.float16 else "bf16"
+    def oracle_run(q, k, v, seq):
+        if code is None:
+            return oracle.gqa_sliding(q.astype(np.float16), k.astype(np.float16), v.astype(np.float16),
+                                      okc.astype(np.float16), ovc.astype(np.float16), seq, cos, sin,
+                                      num_heads=H, kv_heads=HK, local_window=W)
+        bf = oracle.f32_to_bf16_bits
+        o, pk, pv = oracle.gqa_sliding(bf(q), bf(k), bf(v), bf(okc), bf(ovc), seq, bf(cos), bf(sin), num_heads=H,
+                                       kv_heads=HK, local_window=W, dtype="bf16")
+        return tuple(oracle.bf16_bits_to_f32(x) for x in (o, pk, pv))
+    for step, S in enumerate([40] + [1] * 40):
+        q = cast(rng.standard_normal((B, S, H * D)))
+        k = cast(rng.standard_normal((B, S, HK * D)))
+        v = cast(rng.standard_normal((B, S, HK * D)))
+        seq = (lens + S - 1).astype(np.int32)
+        want, wk, wv = oracle_run(q, k, v, seq)
+        out, _, _ = ops.group_query_attention_sliding(dev(q), dev(k), dev(v), tk, tv, cuda(seq), dev(cos), dev(sin),
+                                                      num_heads=H, kv_heads=HK, local_window=W)
+        tol = dict(rtol=1e-2, atol=1e-3) if dt == np.float16 else dict(rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(host(out), np.asarray(want, np.float32), err_msg=f"step {step}", **tol)
+        np.testing.assert_allclose(host(tk), np.asarray(wk, np.float32), err_msg=f"step {step} keys", **tol)
+        np.testing.assert_array_equal(host(tv), np.asarray(wv, np.float32), err_msg=f"step {step} values")
+        okc, ovc = np.asarray(wk, np.float32), np.asarray(wv, np.float32)
+        lens = lens + S
+
+
 def test_gqa_out_of_range_is_reported_not_faulted(ops):
     rng = np.random.default_rng(4)
     B, S, H, HK, D, past = 1, 1, 8, 2, 64, 10

@@ -28,6 +28,7 @@ PAGED = load_golden("paged_attention.npz")
 MNB_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "matmulnbits")
 GQA_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "gqa")
 PAGED_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "paged")
+SLIDING_CASES = sorted(k for k, v in MANIFEST.items() if v["family"] == "gqa_sliding")
 
 
 @pytest.mark.parametrize("name", MNB_CASES)
@@ -71,6 +72,24 @@ def test_oracle_gqa(name):
     np.testing.assert_allclose(present_v[:, :, :valid], c["present_value"][:, :, :valid], rtol=0, atol=0)
     if shared:
         assert present_k.shape[2] == c["past_key"].shape[2]
+
+
+@pytest.mark.parametrize("name", SLIDING_CASES)
+def test_oracle_gqa_sliding_window_cache(name):
+    """The sliding-window KV cache (attention.rs:725-880) on the reference test's three geometries
+    (a decode step that reclaims rows, a 3-row chunk that needs the staging form, a batched step
+    with rotary): attention output and the resident rows of present (the reference compares rows
+    [0, end) at 3e-3; tests/ops/test_mlx_ops.py:301-323)."""
+    assert len(SLIDING_CASES) == 3
+    meta, c = MANIFEST[name], golden_case(GQA, name)
+    a = meta["attrs"]
+    out, pk, pv = oracle.gqa_sliding(
+        c["query"], c["key"], c["value"], c["past_key"], c["past_value"], c["seqlens_k"], c.get("cos_cache"),
+        c.get("sin_cache"), num_heads=a["num_heads"], kv_heads=a["kv_num_heads"], local_window=a["local_window_size"],
+        scale=a.get("scale", 0.0), do_rotary=a.get("do_rotary", 1), interleaved=a.get("rotary_interleaved", 0))
+    np.testing.assert_allclose(out, c["out"], rtol=2e-5, atol=2e-5)
+    np.testing.assert_allclose(pk, c["present_key"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(pv, c["present_value"])
 
 
 @pytest.mark.parametrize("name,eps,dt", [("rms", 1e-6, None), ("sln", 1e-5, None), ("rms16", 1e-6, None)])
