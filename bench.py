@@ -51,10 +51,16 @@ MODEL = "8b"  # --model: "8b" (the headline workload) or "70b"
 MODEL_NAMES = {"8b": "Llama-3-8B", "70b": "Llama-3-70B"}
 
 
+LAYERS = 0  # --layers: decoder depth override (0 = the model's own)
+
+
 def model_cfg():
+    import dataclasses
+
     from onnxruntime_ep_b200.decoder import LLAMA3_8B, LLAMA3_70B
 
-    return {"8b": LLAMA3_8B, "70b": LLAMA3_70B}[MODEL]
+    cfg = {"8b": LLAMA3_8B, "70b": LLAMA3_70B}[MODEL]
+    return dataclasses.replace(cfg, layers=LAYERS) if LAYERS else cfg
 HBM_FALLBACK = 6553.0
 TENSOR_FALLBACK = 1590.0
 
@@ -283,7 +289,11 @@ def workload_config(cfg, B, world, mode, n_steps, cap):
     seqs = B if mode in ("tp", "single") else world * B
     par = {"single": "single GPU",
            "tp": (f"tp{world}: q/k/v, gate/up and lm_head split by output rows (attention by KV head), o/down "
-                  f"by K blocks + peer-memory (decode) / NCCL (prompt) all-reduce, logits all-gathered"),
+                  f"by K blocks + peer-memory (decode) / NCCL (prompt) all-reduce, logits all-gathered"
+                  if TP_ATTENTION == "sharded" else
+                  f"tp{world}: attention (q/k/v, GQA, o_proj) in full on every rank, gate/up and lm_head split "
+                  f"by output rows, down by K blocks + one peer-memory (decode) / NCCL (prompt) all-reduce per "
+                  f"layer, logits all-gathered"),
            "dp": (f"dp{world}: data-parallel replicas, a full int4 model and its own sequences per GPU, no "
                   f"collective on the data path")}[mode]
     return {"workload": f"{MODEL_NAMES[MODEL]}-shaped int4 decoder, decode step", "layers": cfg.layers,
@@ -304,6 +314,57 @@ def weight_gb(cfg):
 
 
 # ---- the GPU arm ---------------------------------------------------------------------------
+GEMV_SHAPES = (("q/k/v", 6144, 4096), ("o_proj", 4096, 4096), ("gate/up", 28672, 4096), ("down", 4096, 14336),
+               ("lm_head", 128256, 4096))
+
+
+def gemv_shape_timing(name, N, K, batch, peaks, peak_kind, reps=10):
+    """One decode GEMV shape alone (prepacked int4 block 32, fp16 scales + uint8 zero points, fp16
+    activations, no fused prologue): CUDA-event timing over rotating weight copies larger than L2,
+    replayed from a CUDA graph."""
+    import numpy as np
+    import torch
+
+    from onnxruntime_ep_b200 import ops
+
+    block = 32
+    nb = K // block
+    per = N * nb * block // 2 + N * nb * 2 + N * nb // 2
+    copies = max(3, int(np.ceil(3 * 126e6 / per)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    packs = []
+    for _ in range(copies):
+        Bq = torch.randint(0, 256, (N, nb, block // 2), dtype=torch.uint8, device="cuda", generator=g)
+        S = (torch.rand(N * nb, device="cuda", generator=g) * 0.01 + 0.001).half()
+        Z = torch.randint(0, 256, (N * nb // 2,), dtype=torch.uint8, device="cuda", generator=g)
+        packs.append(ops.matmulnbits_prepack(Bq, S, Z, K=K, N=N, block_size=block))
+        del Bq, S, Z
+    a = torch.randn(batch, K, device="cuda").half()
+    y = torch.empty(batch, N, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                ops.matmulnbits_prepacked(a, packs[i], K=K, N=N, out=y)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+    alg = per + a.numel() * 2 + y.numel() * 2
+    peak = float(peaks.get("hbm_gbs", HBM_FALLBACK))
+    return {"kernel": "mnb_tma_kernel", "proj": name, "M": batch, "N": N, "K": K, "launch_us": round(launch_s * 1e6, 2),
+            "algorithmic_bytes_per_launch": alg, "achieved": round(alg / launch_s / 1e9, 1), "unit": "GB/s",
+            "frac": round(alg / launch_s / 1e9 / peak, 4), "peak": peak, "peak_source": f"{peak_kind} hbm_gbs"}
+
+
 def dominant_kernel_roofline(batch, peaks, peak_kind, reps=10):
     """Live CUDA-event timing of the dominant decode kernel — the fused gate/up int4 GEMV (N = 2 x
     14336, K = 4096, block 32, fp16 scales + uint8 zero points) on the tensor-core path the plan
@@ -753,11 +814,14 @@ def compare_logits(got, ref):
             "ok": bool(d.max() <= tol and agree >= 0.95)}
 
 
+TP_ATTENTION = "sharded"  # --tp-attention
+
+
 def build_part(cfg, local, rank, world, tp):
     from onnxruntime_ep_b200 import ep as E
     from onnxruntime_ep_b200.decoder import build_decoder
 
-    ep = E.ExecutionProvider(device_id=local)
+    ep = E.ExecutionProvider(device_id=local, tp_attention=TP_ATTENTION) if tp else E.ExecutionProvider(device_id=local)
     if tp:
         import torch.distributed as dist
 
@@ -784,7 +848,7 @@ def run_ours(args, rank, world, local, tp=False, with_cpu=True, steps=None, pari
     t_build = time.time()
     ep, sess, part = build_part(cfg, local, rank, world, tp)
     t_build = time.time() - t_build
-    hk = cfg.kv_heads // world if tp else cfg.kv_heads
+    hk = cfg.kv_heads // world if tp and TP_ATTENTION == "sharded" else cfg.kv_heads
     kv = kv_buffers(cfg, B, hk, cap)
     stream = torch.cuda.current_stream()
     device_error_check("before the run")
@@ -979,6 +1043,8 @@ def main():
                     help="decoder shape: Llama-3-8B (the headline workload, prompt 1024) or Llama-3-70B "
                          "(prompt 2048)")
     ap.add_argument("--prompt", type=int, default=0, help="prompt length prefilled before the timed decode steps")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder depth override for diagnosis (a shallower model is not the named workload)")
     ap.add_argument("--context", type=int, default=0,
                     help="--kernel-only paged: time this one (batch, context) case instead of the default set")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -988,15 +1054,22 @@ def main():
     ap.add_argument("--no-side-leg", action="store_true",
                     help="N > 1: skip the other parallel form's measurement reported beside the headline")
     ap.add_argument("--no-parity", action="store_true", help="N > 1 tensor parallel: skip the tp_parity check")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "gqa", "gemm", "paged", "c1"],
-                    help="time one kernel alone (gemv: the roofline leg; gqa: decode attention, B=1 and 8 at "
+    ap.add_argument("--tp-attention", default="sharded", choices=["sharded", "replicated"],
+                    help="tensor parallel: attention sharded by KV head (two all-reduces per layer) or run in "
+                         "full on every rank (one all-reduce per layer, after the FFN)")
+    ap.add_argument("--kernel-only", nargs="?", const="gemv",
+                    choices=["gemv", "gemv-shapes", "gqa", "gemm", "paged", "c1"],
+                    help="time one kernel alone (gemv: the roofline leg; gemv-shapes: every decode projection of "
+                         "the Llama-3-8B layer; gqa: decode attention, B=1 and 8 at "
                          "context 1024 and 8192; gemm: the prefill GEMM at Llama-3-8B projection shapes; "
                          "paged: PagedAttention decode; c1: the fp32 single-MatMulNBits workload at M 1/16/512); "
                          "used for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    global MODEL, PROMPT
+    global MODEL, PROMPT, LAYERS, TP_ATTENTION
     MODEL = args.model
+    TP_ATTENTION = args.tp_attention
+    LAYERS = args.layers
     PROMPT = args.prompt or (2048 if MODEL == "70b" else 1024)
 
     if args.impl == "reference":
@@ -1027,6 +1100,9 @@ def main():
             if not args.context:
                 for S, past in ((512, 0), (2048, 0), (128, 1024)):
                     print(json.dumps(paged_prompt_timing(S, past, peaks, peak_kind)), flush=True)
+        elif args.kernel_only == "gemv-shapes":
+            for name, n, k in GEMV_SHAPES:
+                print(json.dumps(gemv_shape_timing(name, n, k, args.batch, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "c1":
             for m in (1, 16, 512):
                 print(json.dumps(c1_kernel_timing(m, peaks, peak_kind)), flush=True)

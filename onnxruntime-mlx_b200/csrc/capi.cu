@@ -96,9 +96,14 @@ using namespace b200ep;
   }
 
 namespace b200ep {
+namespace {
+thread_local int t_pdl_off = 0;
+}
+PdlOff::PdlOff() { ++t_pdl_off; }
+PdlOff::~PdlOff() { --t_pdl_off; }
 bool pdl_enabled() {
   static const bool on = getenv("ONNXRUNTIME_EP_B200_NO_PDL") == nullptr;
-  return on;
+  return on && t_pdl_off == 0;
 }
 }  // namespace b200ep
 

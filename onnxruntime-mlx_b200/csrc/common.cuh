@@ -145,7 +145,17 @@ inline int div_up(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-bool pdl_enabled();  // false when ONNXRUNTIME_EP_B200_NO_PDL is set
+bool pdl_enabled();  // false when ONNXRUNTIME_EP_B200_NO_PDL is set, or while a PdlOff lives
+
+// Launches issued on this thread while a PdlOff is alive wait for the previous kernel of the
+// stream to complete: for a kernel whose pre-wait code reads what its immediate predecessor writes
+// (attention reading lengths that the integer glue just computed).
+struct PdlOff {
+  PdlOff();
+  ~PdlOff();
+  PdlOff(const PdlOff&) = delete;
+  PdlOff& operator=(const PdlOff&) = delete;
+};
 
 // SMs of the current device (cached; every GPU of a node is the same part)
 inline int num_sms() {

@@ -246,6 +246,8 @@ B200EP_API b200ep_ep* b200ep_ep_create(const char* const* keys, const char* cons
     ep->cfg.fuse = !truthy(getenv("ONNXRUNTIME_EP_B200_NO_FUSION"));
     ep->cfg.verbose = truthy(getenv("ONNXRUNTIME_EP_B200_VERBOSE"));
     if (const char* lp = getenv("ONNXRUNTIME_EP_B200_LAYER_PARTITIONS")) ep->cfg.layer_partitions = lp;
+    if (const char* ta = getenv("ONNXRUNTIME_EP_B200_TP_ATTENTION"))
+      ep->cfg.tp_replicate_attention = std::string(ta) == "replicated";
     for (size_t i = 0; i < n; ++i) {
       if (!keys || !values || !keys[i] || !values[i]) continue;
       std::string k = keys[i], v = values[i];
@@ -255,6 +257,7 @@ B200EP_API b200ep_ep* b200ep_ep_create(const char* const* keys, const char* cons
       else if (k == "layer_partitions") ep->cfg.layer_partitions = v;
       else if (k == "device_id") ep->device = atoi(v.c_str());
       else if (k == "registration_name") ep->name = v;
+      else if (k == "tp_attention") ep->cfg.tp_replicate_attention = v == "replicated";
     }
     return ep;
   } catch (...) {

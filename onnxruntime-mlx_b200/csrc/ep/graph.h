@@ -53,6 +53,13 @@ struct Node {
     return (it != attrs.end() && it->second.kind == Attribute::kInt) ? it->second.i : dflt;
   }
   bool has_attr(const std::string& k) const { return attrs.count(k) != 0; }
+  std::vector<int64_t> ints_attr(const std::string& k) const {
+    auto it = attrs.find(k);
+    if (it == attrs.end()) return {};
+    if (it->second.kind == Attribute::kInts) return it->second.ints;
+    if (it->second.kind == Attribute::kInt) return {it->second.i};
+    return {};
+  }
   float float_attr(const std::string& k, float dflt) const {
     auto it = attrs.find(k);
     if (it == attrs.end()) return dflt;

@@ -6,6 +6,7 @@
 #include <chrono>
 #include <set>
 #include <sstream>
+#include <tuple>
 #include <unordered_map>
 
 #include "../common.cuh"
@@ -37,6 +38,18 @@ struct Plan::Program {
   std::vector<std::unique_ptr<DevMem>> mems;
   std::map<std::string, cudaGraphExec_t> graphs;
   int path = 2;  // 0 decode, 1 prefill, 2 general (for the session summary)
+  // integer glue evaluated on the host (no launch) and the host values that device steps read:
+  // packed into one buffer uploaded by one copy per call (upl_*), plus output slots copied singly
+  std::vector<char> host_step;
+  std::vector<int> host_steps;
+  std::vector<std::pair<int, size_t>> uploads;  // slot, offset in the packed buffer
+  std::vector<int> out_uploads;
+  std::vector<uint8_t> upl_host;
+  void* upl_dev = nullptr;
+  // the real extent of every input's changing key axis, read by the kernels from dims_dev
+  std::map<int, int> dims_idx;  // slot -> index
+  std::vector<int64_t> dims_host;
+  int64_t* dims_dev = nullptr;
   ~Program() {
     for (auto& kv : graphs)
       if (kv.second) cudaGraphExecDestroy(kv.second);
@@ -271,6 +284,32 @@ int Plan::lower(const Graph& g, const std::vector<int>& nodes, std::string* err)
         st.kind = StepKind::kCast;
         st.to = (int)n.int_attr("to", 0);
         break;
+      case OpKind::kShape:
+        st.kind = StepKind::kShape;
+        st.shp_start = n.int_attr("start", 0);
+        st.shp_end = n.int_attr("end", INT64_MAX);
+        break;
+      case OpKind::kGather: {
+        st.kind = StepKind::kGatherIdx;
+        const Initializer* idx = g.initializer(n.inputs[1]);
+        st.ivals = const_ints(idx);
+        st.idx_rank = (int)idx->shape.size();
+        st.in.resize(1);
+        break;
+      }
+      case OpKind::kReduceSum:
+        st.kind = StepKind::kReduceSum;
+        st.keepdims = n.int_attr("keepdims", 1) != 0;
+        st.in.resize(1);
+        break;
+      case OpKind::kUnsqueeze:
+      case OpKind::kSqueeze:
+      case OpKind::kReshape:
+        st.kind = StepKind::kCopy;
+        st.layout = e->kind == OpKind::kUnsqueeze ? 1 : e->kind == OpKind::kSqueeze ? 2 : 3;
+        st.ivals = n.input_present(1) ? const_ints(g.initializer(n.inputs[1])) : n.ints_attr("axes");
+        st.in.resize(1);
+        break;
     }
     steps_.push_back(std::move(st));
   }
@@ -300,6 +339,7 @@ int Plan::lower(const Graph& g, const std::vector<int>& nodes, std::string* err)
     for (int o : st.out)
       if (o >= 0 && slots_[o].dtype == 0) {
         if (st.kind == StepKind::kCast) slots_[o].dtype = st.to;
+        else if (st.kind == StepKind::kShape) slots_[o].dtype = kI64;
         else if (st.kind == StepKind::kGbq) slots_[o].dtype = slots_[st.wS].dtype;
         else if (!st.in.empty() && st.in[0] >= 0) slots_[o].dtype = slots_[st.in[0]].dtype;
       }
@@ -627,6 +667,7 @@ std::unique_ptr<Plan> Plan::compile_impl(const Graph& g, const std::vector<int>&
     p->fuse_prologues();
     p->fuse_peer_allreduce();
   }
+  p->compute_free_rules();
   p->stats_.steps = (int)p->steps_.size();
   if (cfg.verbose) fprintf(stderr, "[b200ep] compiled partition: %s\n", p->describe().c_str());
   return p;
@@ -778,6 +819,10 @@ std::shared_ptr<Initializer> slice_blocks(const Initializer& in, int64_t n, int6
 
 }  // namespace
 
+namespace {
+bool packed_inputs(const Step& g) { return g.packed; }
+}  // namespace
+
 int Plan::shard_for_tp(std::string* err) {
   if (!cfg_.tp || cfg_.tp->world == 1) return B200EP_OK;
   const int W = cfg_.tp->world, rk = cfg_.tp->rank;
@@ -833,6 +878,15 @@ int Plan::shard_for_tp(std::string* err) {
   for (int gi = 0; gi < (int)steps_.size(); ++gi) {
     Step& g = steps_[gi];
     if (g.kind != StepKind::kGqa) continue;
+    if (cfg_.tp_replicate_attention) {
+      // attention runs in full on every rank: its projections are kept whole (not sharded, and
+      // not taken by the vocabulary split below)
+      Uses uu = uses_of(steps_, slots_.size());
+      for (int j = 0; j < (packed_inputs(g) ? 1 : 3); ++j)
+        if (uu.producer[g.in[j]] >= 0) done.insert(uu.producer[g.in[j]]);
+      for (int c : uu.users[g.out[0]]) done.insert(c);
+      continue;
+    }
     const int H = g.num_heads, HK = g.kv_heads, D = g.head_size;
     if (H % W || HK % W) return fail("attention heads " + std::to_string(H) + "/" + std::to_string(HK) +
                                      " do not divide over the ranks");
@@ -934,13 +988,208 @@ int Plan::shard_for_tp(std::string* err) {
 }
 
 // ---- shape inference ------------------------------------------------------------------------
+namespace {
+
+const char* step_kind_name(StepKind k) {
+  static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid", "SiluMul",
+                                "Cast", "GatherBlockQuantized", "AllReduce", "AllGather", "PagedAttention",
+                                "Shape", "Gather", "ReduceSum", "Copy"};
+  return names[(int)k];
+}
+
+bool is_int_dtype(int dt) { return dt == kI32 || dt == kI64; }
+
+// values of a little-endian int32 / int64 byte image
+std::vector<int64_t> ints_of(const std::vector<uint8_t>& bytes, int dtype) {
+  std::vector<int64_t> v;
+  if (dtype == kI64) {
+    v.resize(bytes.size() / 8);
+    memcpy(v.data(), bytes.data(), v.size() * 8);
+  } else if (dtype == kI32) {
+    for (size_t i = 0; i + 4 <= bytes.size(); i += 4) {
+      int32_t x;
+      memcpy(&x, bytes.data() + i, 4);
+      v.push_back(x);
+    }
+  }
+  return v;
+}
+
+// host values of the integer constants and of host-resident integer scalars
+void seed_host_values(std::vector<Slot>& S) {
+  for (auto& s : S) {
+    if ((s.kind == Slot::kConst || s.kind == Slot::kInput) && is_int_dtype(s.dtype) && !s.host_copy.empty()) {
+      s.hval = ints_of(s.host_copy, s.dtype);
+      s.hknown = (int64_t)s.hval.size() == numel_of(s.kind == Slot::kConst ? s.cshape : s.shape);
+    } else if (s.kind != Slot::kConst) {
+      s.hknown = false;
+      s.hval.clear();
+    }
+  }
+}
+
+// integer a op b, ONNX wrap-around for int32
+int64_t int_op(int op, int64_t a, int64_t b, int dtype) {
+  const int64_t r = op == kOpAdd ? (int64_t)((uint64_t)a + (uint64_t)b)
+                                 : op == kOpSub ? (int64_t)((uint64_t)a - (uint64_t)b) : (int64_t)((uint64_t)a * (uint64_t)b);
+  return dtype == kI32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)r : r;
+}
+
+}  // namespace
+
+int Plan::infer_glue(const Step& st, std::vector<Slot>& S, std::string* err) const {
+  auto fail = [&](const std::string& m) {
+    *err = m;
+    return B200EP_EINVAL;
+  };
+  Slot& y = S[st.out[0]];
+  const Slot& x = S[st.in[0]];
+  const auto& xs = x.rshape.empty() ? x.shape : x.rshape;  // a changing key axis: this call's extent
+  switch (st.kind) {
+    case StepKind::kShape: {
+      // rust/src/ops/shape.rs:948-961, shape_interval :971-980
+      const int64_t rank = (int64_t)xs.size();
+      int64_t a = st.shp_start, b = st.shp_end == INT64_MAX ? rank : st.shp_end;
+      a = std::clamp<int64_t>(a < 0 ? a + rank : a, 0, rank);
+      b = std::clamp<int64_t>(b < 0 ? b + rank : b, 0, rank);
+      y.shape = {std::max<int64_t>(b - a, 0)};
+      y.hval.assign(xs.begin() + a, xs.begin() + std::max(a, b));
+      y.hknown = true;
+      return B200EP_OK;
+    }
+    case StepKind::kGatherIdx: {
+      if (x.shape.size() != 1) return fail("Gather " + st.name + ": data must be 1-D");
+      const int64_t n = x.shape[0];
+      std::vector<int64_t> idx;
+      for (int64_t i : st.ivals) {
+        const int64_t j = i < 0 ? i + n : i;
+        if (j < 0 || j >= n)
+          return fail("Gather " + st.name + ": index " + std::to_string(i) + " out of range for " + std::to_string(n));
+        idx.push_back(j);
+      }
+      y.shape = st.idx_rank == 0 ? std::vector<int64_t>{} : std::vector<int64_t>{(int64_t)idx.size()};
+      y.hknown = x.hknown;
+      y.hval.clear();
+      if (x.hknown)
+        for (int64_t j : idx) y.hval.push_back(x.hval[j]);
+      return B200EP_OK;
+    }
+    case StepKind::kReduceSum: {
+      if (x.shape.empty()) return fail("ReduceSum " + st.name + ": rank-0 data");
+      y.shape = x.shape;
+      if (st.keepdims) y.shape.back() = 1;
+      else y.shape.pop_back();
+      y.hknown = x.hknown;
+      y.hval.clear();
+      if (x.hknown) {
+        const int64_t len = xs.back(), rows = len ? (int64_t)x.hval.size() / len : 0;
+        for (int64_t r = 0; r < rows; ++r) {
+          int64_t t = 0;
+          for (int64_t c = 0; c < len; ++c) t = int_op(kOpAdd, t, x.hval[r * len + c], y.dtype);
+          y.hval.push_back(t);
+        }
+      }
+      return B200EP_OK;
+    }
+    case StepKind::kCopy: {
+      std::vector<int64_t> o;
+      if (st.layout == 1) {  // Unsqueeze: shape.rs:543-553
+        const int64_t r = (int64_t)x.shape.size() + (int64_t)st.ivals.size();
+        std::vector<char> ins(r, 0);
+        for (int64_t a : st.ivals) {
+          const int64_t k = a < 0 ? a + r : a;
+          if (k < 0 || k >= r || ins[k]) return fail("Unsqueeze " + st.name + ": invalid axes");
+          ins[k] = 1;
+        }
+        size_t j = 0;
+        for (int64_t k = 0; k < r; ++k) o.push_back(ins[k] ? 1 : x.shape[j++]);
+      } else if (st.layout == 2) {  // Squeeze: shape.rs:555-567
+        const int64_t r = (int64_t)x.shape.size();
+        std::vector<char> drop(r, 0);
+        for (int64_t a : st.ivals) {
+          const int64_t k = a < 0 ? a + r : a;
+          if (k < 0 || k >= r || x.shape[k] != 1) return fail("Squeeze " + st.name + ": axis is not of extent 1");
+          drop[k] = 1;
+        }
+        for (int64_t k = 0; k < r; ++k)
+          if (!drop[k]) o.push_back(x.shape[k]);
+      } else {  // Reshape with allowzero = 0: shape.rs:510-528
+        int64_t known = 1, neg = -1;
+        for (size_t k = 0; k < st.ivals.size(); ++k) {
+          int64_t d = st.ivals[k];
+          if (d == 0) {
+            if (k >= x.shape.size()) return fail("Reshape " + st.name + ": 0 beyond the input rank");
+            d = x.shape[k];
+          }
+          if (d == -1) {
+            neg = (int64_t)k;
+            o.push_back(1);
+            continue;
+          }
+          known *= d;
+          o.push_back(d);
+        }
+        const int64_t total = numel_of(x.shape);
+        if (neg >= 0) {
+          if (known == 0 || total % known) return fail("Reshape " + st.name + ": size does not divide");
+          o[neg] = total / known;
+        } else if (known != total) {
+          return fail("Reshape " + st.name + ": element count changes");
+        }
+      }
+      y.shape = o;
+      y.hknown = x.hknown;
+      y.hval = x.hknown ? x.hval : std::vector<int64_t>{};
+      return B200EP_OK;
+    }
+    case StepKind::kBinary: {  // integer Add / Sub / Mul (the output shape is already set)
+      const Slot& b = S[st.in[1]];
+      y.hknown = x.hknown && b.hknown;
+      y.hval.clear();
+      if (!y.hknown) return B200EP_OK;
+      const int rank = (int)y.shape.size();
+      for (int64_t i = 0; i < numel_of(y.shape); ++i) {
+        int64_t rem = i, ia = 0, ib = 0, sa = 1, sb = 1;
+        for (int d = rank - 1; d >= 0; --d) {
+          const int64_t c = rem % y.shape[d];
+          rem /= y.shape[d];
+          const int ja = (int)x.shape.size() - (rank - d), jb = (int)b.shape.size() - (rank - d);
+          const int64_t da = ja >= 0 ? x.shape[ja] : 1, db = jb >= 0 ? b.shape[jb] : 1;
+          if (da != 1) ia += c * sa;
+          if (db != 1) ib += c * sb;
+          sa *= da;
+          sb *= db;
+        }
+        y.hval.push_back(int_op(st.bop, x.hval[ia], b.hval[ib], y.dtype));
+      }
+      return B200EP_OK;
+    }
+    case StepKind::kCast: {  // int32 <-> int64
+      y.hknown = x.hknown;
+      y.hval.clear();
+      if (x.hknown)
+        for (int64_t v : x.hval) y.hval.push_back(st.to == kI32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)v : v);
+      return B200EP_OK;
+    }
+    default:
+      return B200EP_OK;
+  }
+}
+
 int Plan::infer(std::vector<Slot>& S, std::string* err) const {
   auto fail = [&](const std::string& m) {
     *err = m;
     return B200EP_EINVAL;
   };
+  seed_host_values(S);
   for (const Step& st : steps_) {
     switch (st.kind) {
+      case StepKind::kShape:
+      case StepKind::kGatherIdx:
+      case StepKind::kReduceSum:
+      case StepKind::kCopy:
+        if (int rc = infer_glue(st, S, err)) return rc;
+        break;
       case StepKind::kMnb: {
         if (st.pro) {  // the folded producer's outputs: its activation buffer and the residual
           auto sh = S[st.pro_x].shape;
@@ -963,12 +1212,10 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
           return fail("GroupQueryAttention " + st.name + ": query must be rank 3 and past_key rank 4");
         S[st.out[0]].shape = {q.shape[0], q.shape[1], (int64_t)st.num_heads * st.head_size};
         int64_t cap = pk.shape[2];
+        // total_sequence_length when its value is known on the host (a host-resident input or
+        // Cast(Gather(Shape(attention_mask), 1)) evaluated by the glue)
         const Slot& tot = S[st.in[6]];
-        if (!st.sliding && tot.kind == Slot::kInput && !tot.host_copy.empty()) {
-          int32_t t = 0;
-          memcpy(&t, tot.host_copy.data(), 4);
-          cap = std::max<int64_t>(cap, t);
-        }
+        if (!st.sliding && tot.hknown && !tot.hval.empty()) cap = std::max<int64_t>(cap, tot.hval[0]);
         for (int o : {1, 2})
           if (st.out[o] >= 0 && S[st.out[o]].shape.empty())
             S[st.out[o]].shape = {pk.shape[0], pk.shape[1], cap, pk.shape[3]};
@@ -998,11 +1245,17 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
           o[n - 1 - i] = std::max(da, db);
         }
         S[st.out[0]].shape = o;
+        if (is_int_dtype(S[st.out[0]].dtype))
+          if (int rc = infer_glue(st, S, err)) return rc;
         break;
       }
       case StepKind::kSigmoid:
+        S[st.out[0]].shape = S[st.in[0]].shape;
+        break;
       case StepKind::kCast:
         S[st.out[0]].shape = S[st.in[0]].shape;
+        if (is_int_dtype(st.to))
+          if (int rc = infer_glue(st, S, err)) return rc;
         break;
       case StepKind::kSiluMul: {
         auto sh = S[st.in[0]].shape;
@@ -1066,11 +1319,29 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
     prof_ev_.assign(2 * steps_.size() + 2, nullptr);
     for (auto& ev : prof_ev_) cudaEventCreate(&ev);
   }
+  // the attention kernels read their lengths / block tables before their programmatic-launch
+  // wait (data written two or more kernels back); when the step launched just before produced
+  // one of them (integer glue right in front of the attention), that launch serialises fully
+  std::vector<int> producer(S.size(), -1);
+  for (int i = 0; i < (int)steps_.size(); ++i)
+    for (int o : steps_[i].out)
+      if (o >= 0) producer[o] = i;
+  int prev_launch = -1;
   int si = 0;
   for (const Step& s : steps_) {
     if (prof) cudaEventRecord(prof_ev_[2 * si], st);
     ++si;
     cudaError_t e = cudaSuccess;
+    if (!prog.host_step.empty() && prog.host_step[si - 1]) {  // evaluated on the host, value uploaded
+      if (prof) cudaEventRecord(prof_ev_[2 * si - 1], st);
+      continue;
+    }
+    bool fresh = false;
+    if (s.kind == StepKind::kGqa || s.kind == StepKind::kPaged)
+      for (int k = 5; k <= 7 && k < (int)s.in.size(); ++k)
+        fresh |= s.in[k] >= 0 && prev_launch >= 0 && producer[s.in[k]] == prev_launch;
+    std::unique_ptr<PdlOff> pdl_off(fresh ? new PdlOff() : nullptr);
+    prev_launch = si - 1;
     switch (s.kind) {
       case StepKind::kMnb: {
         const Slot& a = S[s.in[0]];
@@ -1271,7 +1542,31 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
           sa *= da;
           sb *= db;
         }
-        e = launch_binary(a.ptr, b.ptr, y.ptr, y.dtype, gm, s.bop, st);
+        e = is_int_dtype(y.dtype) ? launch_binary_int(a.ptr, b.ptr, y.ptr, y.dtype, gm, s.bop, st)
+                                  : launch_binary(a.ptr, b.ptr, y.ptr, y.dtype, gm, s.bop, st);
+        break;
+      }
+      case StepKind::kShape:  // always known on the host
+        break;
+      case StepKind::kGatherIdx: {
+        const Slot& x = S[s.in[0]];
+        IdxList il;
+        il.n = (int)s.ivals.size();
+        for (int i = 0; i < il.n; ++i) il.v[i] = s.ivals[i] < 0 ? s.ivals[i] + x.shape[0] : s.ivals[i];
+        e = launch_gather_idx(x.ptr, S[s.out[0]].ptr, x.dtype, il, st);
+        break;
+      }
+      case StepKind::kReduceSum: {
+        const Slot& x = S[s.in[0]];
+        auto d = prog.dims_idx.find(s.in[0]);
+        const int64_t len = x.shape.back();
+        e = launch_reduce_sum_rows(x.ptr, x.dtype, S[s.out[0]].ptr, S[s.out[0]].dtype, len ? x.numel() / len : 0, len,
+                                   d == prog.dims_idx.end() ? nullptr : prog.dims_dev + d->second, st);
+        break;
+      }
+      case StepKind::kCopy: {
+        const Slot& x = S[s.in[0]];
+        e = launch_copy_bytes(x.ptr, S[s.out[0]].ptr, x.numel() * dtype_size(x.dtype), st);
         break;
       }
       case StepKind::kSigmoid:
@@ -1283,7 +1578,10 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
         break;
       }
       case StepKind::kCast:
-        e = launch_cast(S[s.in[0]].ptr, S[s.in[0]].dtype, S[s.out[0]].ptr, s.to, S[s.in[0]].numel(), st);
+        e = is_int_dtype(s.to) ? launch_cast_int(S[s.in[0]].ptr, S[s.in[0]].dtype, S[s.out[0]].ptr, s.to,
+                                                 S[s.in[0]].numel(), st)
+                               : launch_cast(S[s.in[0]].ptr, S[s.in[0]].dtype, S[s.out[0]].ptr, s.to,
+                                             S[s.in[0]].numel(), st);
         break;
       case StepKind::kGbq: {
         const Slot& idx = S[s.in[0]];
@@ -1311,12 +1609,9 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
   }
   if (prof) {
     cudaStreamSynchronize(st);
-    static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                  "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
-                                "PagedAttention"};
     for (int i = 0; i < si; ++i) {
       const Step& s = steps_[i];
-      std::string key = names[(int)s.kind];
+      std::string key = step_kind_name(s.kind);
       if (s.kind == StepKind::kMnb)
         key += " M=" + std::to_string(S[s.in[0]].numel() / std::max<int64_t>(s.K, 1)) + " N=" + std::to_string(s.N) +
                " K=" + std::to_string(s.K) + (s.pro ? " +prologue" : "") + (s.ar_out ? " +peer-out" : "");
@@ -1329,14 +1624,111 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
       v.second += ms;
     }
   }
-  (void)prog;
   return B200EP_OK;
 }
 
 int Plan::launches_per_run() const {
   int n = 0;
-  for (auto& s : steps_) n += (s.kind != StepKind::kAllReduce && s.kind != StepKind::kAllGather) + (s.kind == StepKind::kPaged);
+  for (auto& s : steps_)
+    n += (s.kind != StepKind::kAllReduce && s.kind != StepKind::kAllGather && s.kind != StepKind::kShape) +
+         (s.kind == StepKind::kPaged);
   return n;
+}
+
+// ---- inputs whose key axis changes every call ----------------------------------------------
+void Plan::compute_free_rules() {
+  free_rule_.assign(in_names_.size(), 0);
+  Uses u = uses_of(steps_, slots_.size());
+  for (size_t id = 0; id < slots_.size(); ++id) {
+    const Slot& sl = slots_[id];
+    if (sl.kind != Slot::kInput) continue;
+    bool folded = false;  // read by a GEMV prologue: never free
+    for (const Step& st : steps_)
+      for (int x : {st.pro_x, st.pro_skip, st.pro_gamma, st.pro_res})
+        folded |= x == (int)id;
+    const auto& users = u.users[id];
+    if (folded || users.empty()) continue;
+    bool shape_only = true, reducible = true;
+    for (int k : users) {
+      const StepKind kd = steps_[k].kind;
+      shape_only &= kd == StepKind::kShape;
+      reducible &= kd == StepKind::kShape || (kd == StepKind::kReduceSum && steps_[k].in[0] == (int)id);
+    }
+    free_rule_[sl.io] = shape_only ? 1 : reducible ? 2 : 0;
+  }
+}
+
+std::vector<int64_t> Plan::key_shape(int io, const std::vector<int64_t>& shape) const {
+  const int rule = io < (int)free_rule_.size() ? free_rule_[io] : 0;
+  if (rule == 0 || shape.empty()) return shape;
+  std::vector<int64_t> k = shape;
+  if (rule == 1) {
+    std::fill(k.begin(), k.end(), 1);
+  } else {
+    int64_t c = 64;
+    while (c < shape.back()) c *= 2;
+    k.back() = c;
+  }
+  return k;
+}
+
+int Plan::stage_dynamic(Program& prog, const std::vector<TensorArg>& in, cudaStream_t st) {
+  std::vector<Slot>& S = prog.slots;
+  bool dims = false;
+  for (size_t id = 0; id < S.size(); ++id) {
+    Slot& s = S[id];
+    if (s.kind != Slot::kInput || free_rule_[s.io] == 0) continue;
+    const TensorArg& a = in[s.io];
+    s.rshape = a.shape;
+    if (free_rule_[s.io] != 2) continue;
+    const size_t bytes = (size_t)numel_of(a.shape) * dtype_size(s.dtype);
+    if (bytes) {
+      B200EP_CUDA_RET(cudaMemcpyAsync(s.ptr, a.data, bytes, a.on_device ? cudaMemcpyDeviceToDevice
+                                                                       : cudaMemcpyHostToDevice, st));
+    }
+    prog.dims_host[prog.dims_idx.at((int)id)] = a.shape.back();
+    dims = true;
+  }
+  if (dims)
+    B200EP_CUDA_RET(cudaMemcpyAsync(prog.dims_dev, prog.dims_host.data(), prog.dims_host.size() * 8,
+                                    cudaMemcpyHostToDevice, st));
+  if (prog.host_steps.empty()) return B200EP_OK;
+  // re-evaluate the host-side glue for this call (shapes of changing inputs, host scalars)
+  for (auto& s : S)
+    if (s.kind == Slot::kInput && is_int_dtype(s.dtype) && !s.host_copy.empty()) s.hval = ints_of(s.host_copy, s.dtype);
+  std::string err;
+  for (int i : prog.host_steps)
+    if (infer_glue(steps_[i], S, &err)) return set_error(B200EP_EINVAL, err);
+  auto pack = [&](const Slot& s, uint8_t* dst) {
+    for (size_t k = 0; k < s.hval.size(); ++k) {
+      if (s.dtype == kI32) {
+        const int32_t v = (int32_t)s.hval[k];
+        memcpy(dst + 4 * k, &v, 4);
+      } else {
+        memcpy(dst + 8 * k, &s.hval[k], 8);
+      }
+    }
+  };
+  for (auto [id, off] : prog.uploads) pack(S[id], prog.upl_host.data() + off);
+  if (!prog.upl_host.empty())
+    B200EP_CUDA_RET(cudaMemcpyAsync(prog.upl_dev, prog.upl_host.data(), prog.upl_host.size(), cudaMemcpyHostToDevice, st));
+  for (int id : prog.out_uploads) {
+    const Slot& s = S[id];
+    std::vector<uint8_t> tmp(s.hval.size() * dtype_size(s.dtype));
+    pack(s, tmp.data());
+    if (!tmp.empty()) B200EP_CUDA_RET(cudaMemcpyAsync(s.ptr, tmp.data(), tmp.size(), cudaMemcpyHostToDevice, st));
+  }
+  // a total_sequence_length computed from this call's mask must fit the compiled cache capacity
+  for (const Step& stp : steps_)
+    if (stp.kind == StepKind::kGqa && !stp.sliding && stp.in[6] >= 0) {
+      const Slot& tot = S[stp.in[6]];
+      const int64_t cap = S[stp.out[1]].shape.size() == 4 ? S[stp.out[1]].shape[2] : 0;
+      if (tot.hknown && !tot.hval.empty() && tot.hval[0] > cap)
+        return set_error(B200EP_EINVAL, "GroupQueryAttention " + stp.name + ": total_sequence_length " +
+                                            std::to_string(tot.hval[0]) + " exceeds the KV capacity " +
+                                            std::to_string(cap));
+    }
+  return B200EP_OK;
 }
 
 int Plan::run(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t caller) {
@@ -1368,15 +1760,20 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
                                         std::to_string(out_names_.size()) + " outputs");
   // Repeat of the previous call (same pointers, residency and shapes): replay its graph directly,
   // skipping the shape-key and pointer-key lookups (they cost tens of microseconds per call).
+  if (free_rule_.size() != in_names_.size()) free_rule_.assign(in_names_.size(), 0);
+  // (inputs with a changing key axis enter by their key shape and are always copied in)
   std::vector<int64_t> sig;
   sig.reserve(4 * (in.size() + out.size()) + 2);
   for (const auto* v : {&in, &out}) {
     sig.push_back((int64_t)v->size());
-    for (const TensorArg& a : *v) {
-      sig.push_back((int64_t)reinterpret_cast<uintptr_t>(a.data));
+    for (size_t i = 0; i < v->size(); ++i) {
+      const TensorArg& a = (*v)[i];
+      const bool free_in = v == &in && free_rule_[i] != 0;
+      sig.push_back(free_in ? 0 : (int64_t)reinterpret_cast<uintptr_t>(a.data));
       sig.push_back(a.on_device ? 1 : 0);
       sig.push_back((int64_t)a.shape.size());
-      sig.insert(sig.end(), a.shape.begin(), a.shape.end());
+      const std::vector<int64_t> ks = free_in ? key_shape((int)i, a.shape) : a.shape;
+      sig.insert(sig.end(), ks.begin(), ks.end());
     }
   }
   if (last_prog_ && last_exec_ && sig == last_sig_) {
@@ -1384,12 +1781,13 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
     std::vector<Slot>& S = prog.slots;
     int64_t h2d = 0, d2h = 0;
     for (auto& s : S)
-      if (s.kind == Slot::kInput && !in[s.io].on_device) {
+      if (s.kind == Slot::kInput && !in[s.io].on_device && free_rule_[s.io] == 0) {
         const size_t bytes = (size_t)numel_of(s.shape) * dtype_size(s.dtype);
         if (bytes) B200EP_CUDA_RET(cudaMemcpyAsync(s.ptr, in[s.io].data, bytes, cudaMemcpyHostToDevice, st));
         if (!s.host_copy.empty()) memcpy(s.host_copy.data(), in[s.io].data, s.host_copy.size());
         h2d += (int64_t)bytes;
       }
+    if (int rc = stage_dynamic(prog, in, st)) return rc;
     ++stats_.runs;
     B200EP_CUDA_RET(cudaGraphLaunch(last_exec_, st));
     ++stats_.graph_replays;
@@ -1416,7 +1814,8 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
   last_exec_ = nullptr;
   // shape key: input shapes plus which inputs are host-resident
   std::string key;
-  for (size_t i = 0; i < in.size(); ++i) key += shape_str(in[i].shape) + (in[i].on_device ? "d" : "h") + ";";
+  for (size_t i = 0; i < in.size(); ++i)
+    key += shape_str(key_shape((int)i, in[i].shape)) + (free_rule_[i] == 1 ? "x" : in[i].on_device ? "d" : "h") + ";";
   for (size_t i = 0; i < out.size(); ++i) key += shape_str(out[i].shape) + (out[i].on_device ? "d" : "h") + ";";
   auto it = programs_.find(key);
   SessionSummary* sum = cfg_.summary.get();
@@ -1429,12 +1828,13 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
     prog->slots = slots_;
     for (auto& s : prog->slots) {
       if (s.kind == Slot::kInput) {
-        s.shape = in[s.io].shape;
+        s.shape = key_shape(s.io, in[s.io].shape);
+        if (free_rule_[s.io]) s.rshape = in[s.io].shape;
         if (in[s.io].dtype != s.dtype && s.dtype != 0)
           return set_error(B200EP_EINVAL, "input " + s.name + " has dtype " + std::to_string(in[s.io].dtype) +
                                               ", expected " + std::to_string(s.dtype));
         s.dtype = in[s.io].dtype;
-        if (!in[s.io].on_device && numel_of(s.shape) == 1 && dtype_size(s.dtype) <= 8) {
+        if (!in[s.io].on_device && !free_rule_[s.io] && numel_of(s.shape) == 1 && dtype_size(s.dtype) <= 8) {
           s.host_copy.resize(dtype_size(s.dtype));
           memcpy(s.host_copy.data(), in[s.io].data, s.host_copy.size());
         }
@@ -1450,13 +1850,64 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
       if (s.kind == Slot::kOutput && s.shape != out[s.io].shape)
         return set_error(B200EP_EINVAL, "output " + s.name + " bound with shape " + shape_str(out[s.io].shape) +
                                             ", plan computes " + shape_str(s.shape));
-    // workspaces for attention steps
+    // integer glue whose values infer computed on the host: no launch; device readers of those
+    // values get them from one packed upload per call
+    prog->host_step.assign(steps_.size(), 0);
+    std::vector<char> dev_read(prog->slots.size(), 0);
+    for (size_t i = 0; i < steps_.size(); ++i) {
+      const Step& stp = steps_[i];
+      const bool glue = stp.kind == StepKind::kShape || stp.kind == StepKind::kGatherIdx ||
+                        stp.kind == StepKind::kReduceSum || stp.kind == StepKind::kCopy ||
+                        ((stp.kind == StepKind::kBinary || stp.kind == StepKind::kCast) &&
+                         is_int_dtype(prog->slots[stp.out[0]].dtype));
+      if (glue && prog->slots[stp.out[0]].hknown) {
+        prog->host_step[i] = 1;
+        prog->host_steps.push_back((int)i);
+        continue;
+      }
+      for (int id : stp.in)
+        if (id >= 0) dev_read[id] = 1;
+      for (int id : {stp.pro_x, stp.pro_skip, stp.pro_gamma})
+        if (id >= 0) dev_read[id] = 1;
+    }
+    size_t upl_bytes = 0;
+    for (size_t id = 0; id < prog->slots.size(); ++id) {
+      const Slot& sl = prog->slots[id];
+      if (!sl.hknown || sl.kind == Slot::kConst || sl.kind == Slot::kInput) continue;
+      if (sl.kind == Slot::kOutput) {
+        prog->out_uploads.push_back((int)id);
+      } else if (dev_read[id]) {
+        prog->uploads.push_back({(int)id, upl_bytes});
+        upl_bytes += ((size_t)std::max<int64_t>(numel_of(sl.shape), 1) * dtype_size(sl.dtype) + 15) & ~(size_t)15;
+      }
+    }
+    prog->upl_host.assign(upl_bytes, 0);
+    for (size_t id = 0; id < prog->slots.size(); ++id) {
+      const Slot& sl = prog->slots[id];
+      if (sl.kind == Slot::kInput && free_rule_[sl.io] == 2) {
+        const int k = (int)prog->dims_idx.size();
+        prog->dims_idx[(int)id] = k;
+      }
+    }
+    prog->dims_host.assign(prog->dims_idx.size(), 0);
+    // workspaces for attention steps: the steps run one after another on one stream, so steps of
+    // the same kind (plain / sliding-window cache) and KV geometry share one zero-filled workspace
+    // (the kernels leave its counters zeroed), sized for the largest of them
+    std::map<std::tuple<bool, int64_t, int64_t>, int> ws_of;
     for (Step& stp : steps_)
       if (stp.kind == StepKind::kGqa && stp.ws_slot < 0) {
+        const Slot& q = prog->slots[stp.in[0]];
+        const auto key = std::make_tuple(stp.sliding, q.shape.empty() ? 0 : q.shape[0], (int64_t)stp.kv_heads);
+        auto f = ws_of.find(key);
+        if (f != ws_of.end()) {
+          stp.ws_slot = f->second;
+          continue;
+        }
         Slot w;
         w.name = stp.name + "#ws";
         w.dtype = kU8;
         stp.ws_slot = (int)slots_.size();
+        ws_of[key] = stp.ws_slot;
         slots_.push_back(w);
         prog->slots.push_back(w);
       }
@@ -1471,21 +1922,88 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
         p.head_size = stp.head_size;
         p.cap = prog->slots[stp.out[1]].shape[2];
         p.local_window = stp.local_window;
-        prog->slots[stp.ws_slot].shape = {(int64_t)(stp.sliding ? gqa_sliding_workspace_bytes(p, q.dtype)
-                                                                 : gqa_workspace_bytes(p))};
+        const int64_t need = (int64_t)(stp.sliding ? gqa_sliding_workspace_bytes(p, q.dtype) : gqa_workspace_bytes(p));
+        auto& sh = prog->slots[stp.ws_slot].shape;
+        if (sh.empty() || sh[0] < need) sh = {need};
       }
-    // allocate temps (and staging for host boundary tensors)
+    // allocate: zero-filled workspaces and host staging each get their own buffer; the other
+    // temporaries share one arena by lifetime (first to last step that touches them), so a deep
+    // prefill does not hold every layer's activations at once.  Reuse is safe under programmatic
+    // dependent launch: a kernel writes its outputs only after its pdl_wait, when every earlier
+    // kernel — and so every earlier reader of a reused buffer — has completed.
+    const int nst = (int)steps_.size();
+    std::vector<int> first(prog->slots.size(), nst), last(prog->slots.size(), -1);
+    for (int si = 0; si < nst; ++si) {
+      const Step& st = steps_[si];
+      auto touch = [&](int id) {
+        if (id < 0 || id >= (int)prog->slots.size()) return;
+        first[id] = std::min(first[id], si);
+        last[id] = std::max(last[id], si);
+      };
+      for (int id : st.in) touch(id);
+      for (int id : st.out) touch(id);
+      for (int id : {st.pro_x, st.pro_skip, st.pro_gamma, st.pro_res, st.ws_slot}) touch(id);
+    }
+    struct Place {
+      int id;
+      size_t bytes, off;
+    };
+    std::vector<Place> arena;
+    std::vector<char> uploaded(prog->slots.size(), 0);
+    for (auto [id, off] : prog->uploads) uploaded[id] = 1;
+    if (upl_bytes || !prog->dims_host.empty()) {
+      auto mem = std::make_unique<DevMem>();
+      if (int rc = mem->alloc(upl_bytes + 8 * prog->dims_host.size() + 16)) return rc;
+      prog->upl_dev = mem->p;
+      prog->dims_dev = reinterpret_cast<int64_t*>(static_cast<char*>(mem->p) + ((upl_bytes + 15) & ~(size_t)15));
+      for (auto [id, off] : prog->uploads) prog->slots[id].ptr = static_cast<char*>(mem->p) + off;
+      prog->mems.push_back(std::move(mem));
+    }
     for (size_t i = 0; i < prog->slots.size(); ++i) {
       Slot& s = prog->slots[i];
-      const bool staged = (s.kind == Slot::kInput && !in[s.io].on_device) || (s.kind == Slot::kOutput && !out[s.io].on_device);
-      if (s.kind == Slot::kTemp || staged) {
-        const size_t bytes = (size_t)std::max<int64_t>(numel_of(s.shape), 1) * std::max(dtype_size(s.dtype), 1);
+      if (uploaded[i]) continue;
+      if (s.kind == Slot::kInput && free_rule_[s.io] == 1) {  // only its shape is read
+        s.ptr = nullptr;
+        continue;
+      }
+      const bool staged = (s.kind == Slot::kInput && (!in[s.io].on_device || free_rule_[s.io] == 2)) ||
+                          (s.kind == Slot::kOutput && !out[s.io].on_device);
+      if (s.kind != Slot::kTemp && !staged) continue;
+      const size_t bytes = (size_t)std::max<int64_t>(numel_of(s.shape), 1) * std::max(dtype_size(s.dtype), 1);
+      if (staged || s.dtype == kU8 || last[i] < 0) {
         auto mem = std::make_unique<DevMem>();
         if (int rc = mem->alloc(bytes)) return rc;
         if (s.dtype == kU8) cudaMemset(mem->p, 0, bytes);  // attention workspaces start zeroed
         s.ptr = mem->p;
         prog->mems.push_back(std::move(mem));
+      } else {
+        arena.push_back(Place{(int)i, (bytes + 255) & ~(size_t)255, 0});
       }
+    }
+    // largest first; each at the lowest offset clear of every placed buffer whose lifetime overlaps
+    std::sort(arena.begin(), arena.end(), [](const Place& a, const Place& b) {
+      return a.bytes != b.bytes ? a.bytes > b.bytes : a.id < b.id;
+    });
+    size_t arena_bytes = 0;
+    for (size_t a = 0; a < arena.size(); ++a) {
+      std::vector<std::pair<size_t, size_t>> busy;
+      for (size_t b = 0; b < a; ++b)
+        if (first[arena[b].id] <= last[arena[a].id] && first[arena[a].id] <= last[arena[b].id])
+          busy.push_back({arena[b].off, arena[b].off + arena[b].bytes});
+      std::sort(busy.begin(), busy.end());
+      size_t off = 0;
+      for (auto [lo, hi] : busy) {
+        if (off + arena[a].bytes <= lo) break;
+        off = std::max(off, hi);
+      }
+      arena[a].off = off;
+      arena_bytes = std::max(arena_bytes, off + arena[a].bytes);
+    }
+    if (!arena.empty()) {
+      auto mem = std::make_unique<DevMem>();
+      if (int rc = mem->alloc(arena_bytes)) return rc;
+      for (const Place& pl : arena) prog->slots[pl.id].ptr = static_cast<char*>(mem->p) + pl.off;
+      prog->mems.push_back(std::move(mem));
     }
     for (const Step& stp : steps_)
       if (stp.kind == StepKind::kGqa) {
@@ -1499,7 +2017,9 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
   // bind boundary tensors
   std::string ptr_key;
   for (auto& s : S) {
-    if (s.kind == Slot::kInput) {
+    if (s.kind == Slot::kInput && free_rule_[s.io]) {
+      // copied in by stage_dynamic (key-axis inputs) or never read (shape-only inputs)
+    } else if (s.kind == Slot::kInput) {
       const TensorArg& a = in[s.io];
       if (a.on_device) {
         s.ptr = a.data;
@@ -1521,6 +2041,7 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
       ptr_key += buf;
     }
   }
+  if (int rc = stage_dynamic(prog, in, st)) return rc;
   ++stats_.runs;
   const bool use_graph = cfg_.cuda_graph && !env_on("ONNXRUNTIME_EP_B200_NO_GRAPH");
   const int64_t replays0 = stats_.graph_replays, captures0 = stats_.graph_captures;
@@ -1594,9 +2115,6 @@ int Plan::run_locked(const std::vector<TensorArg>& in, const std::vector<TensorA
 }
 
 std::string Plan::preview() const {
-  static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
-                                "PagedAttention"};
   auto fnv = [](const std::vector<uint8_t>& b) {
     uint64_t h = 1469598103934665603ull;
     for (uint8_t c : b) h = (h ^ c) * 1099511628211ull;
@@ -1606,7 +2124,7 @@ std::string Plan::preview() const {
   o << "[";
   for (size_t i = 0; i < steps_.size(); ++i) {
     const Step& st = steps_[i];
-    o << (i ? "," : "") << "{\"op\":\"" << names[(int)st.kind] << "\",\"name\":\"" << st.name << "\"";
+    o << (i ? "," : "") << "{\"op\":\"" << step_kind_name(st.kind) << "\",\"name\":\"" << st.name << "\"";
     if (st.kind == StepKind::kMnb) {
       o << ",\"N\":" << st.N << ",\"K\":" << st.K;
       const char* keys[3] = {"B", "scales", "zp"};
@@ -1638,10 +2156,7 @@ std::string Plan::describe() const {
   int npk = 0;
   for (auto& st : steps_) npk += st.prepacked;
   o << ",\"prepacked_matmulnbits\":" << npk << ",\"ops\":[";
-  static const char* names[] = {"MatMulNBits", "GroupQueryAttention", "RmsNorm", "Binary", "Sigmoid",
-                                "SiluMul", "Cast", "GatherBlockQuantized", "AllReduce", "AllGather",
-                                "PagedAttention"};
-  for (size_t i = 0; i < steps_.size(); ++i) o << (i ? "," : "") << "\"" << names[(int)steps_[i].kind] << "\"";
+  for (size_t i = 0; i < steps_.size(); ++i) o << (i ? "," : "") << "\"" << step_kind_name(steps_[i].kind) << "\"";
   o << "]}";
   return o.str();
 }

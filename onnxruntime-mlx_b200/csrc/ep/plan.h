@@ -58,6 +58,10 @@ struct EpConfig {
   bool verbose = false;
   std::string layer_partitions;  // "" = unset
   std::shared_ptr<TpContext> tp;  // null = single GPU
+  // tensor parallel: attention (q/k/v, GroupQueryAttention, o_proj) on every rank in full instead of
+  // sharded by KV head, so the only all-reduce of a layer is the FFN's at the layer boundary
+  // (provider option tp_attention = "replicated"; default "sharded")
+  bool tp_replicate_attention = false;
   bool host_only = false;         // lower, fuse and shard on the host only (no upload): preview()
   std::shared_ptr<SessionSummary> summary;  // null = not recorded
 };
@@ -90,6 +94,13 @@ struct Slot {
   // per run
   std::vector<int64_t> shape;
   void* ptr = nullptr;
+  // integer values known on the host (int constants, Shape results, host-resident scalars and
+  // what the integer glue computes from them); such values are uploaded, not computed by kernels
+  bool hknown = false;
+  std::vector<int64_t> hval;
+  // inputs whose extent along a key axis changes every call without changing the program: the
+  // call's real shape (shape then holds the program's capacity)
+  std::vector<int64_t> rshape;
   int64_t numel() const {
     int64_t n = 1;
     for (auto d : shape) n *= d;
@@ -97,7 +108,12 @@ struct Slot {
   }
 };
 
-enum class StepKind { kMnb, kGqa, kRms, kBinary, kSigmoid, kSiluMul, kCast, kGbq, kAllReduce, kAllGather, kPaged };
+enum class StepKind {
+  kMnb, kGqa, kRms, kBinary, kSigmoid, kSiluMul, kCast, kGbq, kAllReduce, kAllGather, kPaged,
+  // integer glue: Shape, Gather of a shape vector, ReduceSum over the last axis, and the
+  // value-preserving Unsqueeze / Squeeze / Reshape (kCopy)
+  kShape, kGatherIdx, kReduceSum, kCopy
+};
 
 struct Step {
   StepKind kind;
@@ -125,6 +141,12 @@ struct Step {
   int64_t gbq_rows = 0, gbq_dim = 0;
   // tensor parallel gather: shard width along the last axis
   int64_t shard_cols = 0;
+  // integer glue: Shape's [start, end) (unnormalised attributes); ReduceSum keepdims; Gather's
+  // constant indices and their rank; Unsqueeze / Squeeze axes or the Reshape target (layout 1 / 2 / 3)
+  int64_t shp_start = 0, shp_end = INT64_MAX;
+  bool keepdims = true;
+  std::vector<int64_t> ivals;
+  int idx_rank = 0, layout = 0;
   // MatMulNBits weights prepacked for the tensor-core path (fp16/bf16, int4)
   bool prepacked = false;
   std::shared_ptr<DevMem> pk_w;
@@ -181,6 +203,16 @@ class Plan {
   bool ar_fused(int64_t M, int64_t hidden, int cons_block) const;
   int shard_for_tp(std::string* err);
   int infer(std::vector<Slot>& slots, std::string* err) const;
+  // integer glue on the host: output shape of a glue step, and its values when every input's
+  // values are known (returns non-zero with err set on an invalid index / shape)
+  int infer_glue(const Step& st, std::vector<Slot>& S, std::string* err) const;
+  // per call, before the launches: copy inputs with a changing key axis into the program's
+  // buffers, re-evaluate the host-side glue for this call's shapes and upload its values
+  int stage_dynamic(Program& prog, const std::vector<TensorArg>& in, cudaStream_t st);
+  // how an input enters the program key: 0 as is; 1 only its rank (the input feeds only Shape);
+  // 2 its last axis as a power-of-two capacity (it feeds only Shape and ReduceSum over that axis)
+  void compute_free_rules();
+  std::vector<int64_t> key_shape(int io, const std::vector<int64_t>& shape) const;
   int launch_steps(const std::vector<Slot>& slots, Program& prog, cudaStream_t st);
   int run_locked(const std::vector<TensorArg>& in, const std::vector<TensorArg>& out, cudaStream_t st);
   int slot_of(const std::string& name);
@@ -190,6 +222,7 @@ class Plan {
   std::map<std::string, int> slot_index_;
   std::vector<Step> steps_;
   std::vector<std::string> in_names_, out_names_;
+  std::vector<int> free_rule_;  // per boundary input (compute_free_rules)
   std::vector<int> out_dtypes_;
   std::map<std::string, std::unique_ptr<Program>> programs_;
   std::mutex mu_;

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 
 namespace b200ep {
 
@@ -251,8 +252,8 @@ bool broadcastable(const ValueInfo* a, const ValueInfo* b) {
 ClaimResult binary_claim(const NodeView& v) {
   REQUIRE(v.num_inputs() == 2 && v.num_outputs() == 1, "expects 2 inputs and 1 output");
   const int o = out_dt(v, 0);
-  REQUIRE(is_ep_float(o), "float output required, got %s", dtype_name(o));
-  REQUIRE(in_dt(v, 0) == o && in_dt(v, 1) == o, "inputs must share the output float dtype");
+  REQUIRE(is_ep_float(o) || is_ep_int(o), "float or int32 / int64 output required, got %s", dtype_name(o));
+  REQUIRE(in_dt(v, 0) == o && in_dt(v, 1) == o, "inputs must share the output dtype");
   REQUIRE(broadcastable(v.input_info(0), v.input_info(1)), "inputs must be broadcastable with rank <= 6");
   return ClaimResult::yes();
 }
@@ -265,8 +266,94 @@ ClaimResult sigmoid_claim(const NodeView& v) {
 
 ClaimResult cast_claim(const NodeView& v) {
   REQUIRE(v.num_inputs() == 1 && v.num_outputs() == 1, "expects 1 input and 1 output");
-  REQUIRE(is_ep_float(in_dt(v, 0)) && is_ep_float(out_dt(v, 0)), "only float <-> float casts are claimed");
-  REQUIRE(v.int_attr("to", 0) == out_dt(v, 0), "'to' must match the output dtype");
+  const int i = in_dt(v, 0), o = out_dt(v, 0);
+  REQUIRE((is_ep_float(i) && is_ep_float(o)) || (is_ep_int(i) && is_ep_int(o)),
+          "only float <-> float and int32 / int64 <-> int32 / int64 casts are claimed");
+  REQUIRE(v.int_attr("to", 0) == o, "'to' must match the output dtype");
+  return ClaimResult::yes();
+}
+
+// ---- integer glue of exported decoders ------------------------------------------------------
+// The attention-mask chain of a GenAI-exported decoder: seqlens_k = Cast(Sub(ReduceSum(mask, 1), 1))
+// and total_sequence_length = Cast(Gather(Shape(mask), 1)) (rust/src/compiled.rs:385-430 reads the
+// same two quantities).  Claimed for int32 / int64 tensors only, where they are glue rather than
+// model math; everything whose value is known on the host is evaluated there by the plan.
+
+int norm_axis(int64_t a, int64_t rank) { return (int)(a < 0 ? a + rank : a); }
+
+// Shape: rust/src/ops/shape.rs:2071-2109 (1-D int64 output of the sliced rank interval)
+ClaimResult shape_claim(const NodeView& v) {
+  REQUIRE(v.num_inputs() == 1 && v.num_outputs() == 1, "Shape expects 1 input and 1 output, got %zuin/%zuout",
+          v.num_inputs(), v.num_outputs());
+  auto* d = v.input_info(0);
+  REQUIRE(d, "missing data tensor type/shape info");
+  auto* o = v.output_info(0);
+  REQUIRE(o && o->dtype == kI64 && o->shape.size() == 1, "Shape: output must be a 1-D int64 tensor");
+  const int64_t rank = (int64_t)d->shape.size();
+  int64_t s = v.int_attr("start", 0), e = v.int_attr("end", rank);
+  s = std::clamp<int64_t>(s < 0 ? s + rank : s, 0, rank);
+  e = std::clamp<int64_t>(e < 0 ? e + rank : e, 0, rank);
+  REQUIRE(o->shape[0] < 0 || o->shape[0] == std::max<int64_t>(e - s, 0),
+          "Shape: output extent %lld must equal the sliced rank interval %lld (start..end)", (long long)o->shape[0],
+          (long long)std::max<int64_t>(e - s, 0));
+  return ClaimResult::yes();
+}
+
+// Gather over a 1-D integer vector with constant indices (shape.rs:1169-1201 for the general form)
+ClaimResult gather_claim(const NodeView& v) {
+  REQUIRE(v.num_inputs() == 2 && v.num_outputs() == 1, "Gather expects 2 inputs and 1 output");
+  auto* d = v.input_info(0);
+  REQUIRE(d && is_ep_int(d->dtype) && d->shape.size() == 1,
+          "only 1-D int32 / int64 data (shape vectors) is gathered on the EP");
+  REQUIRE(norm_axis(v.int_attr("axis", 0), 1) == 0, "axis must be 0 for 1-D data");
+  const Initializer* idx = v.const_input(1);
+  REQUIRE(idx && (idx->dtype == kI32 || idx->dtype == kI64) && idx->shape.size() <= 1 && idx->numel() <= 8,
+          "indices must be a constant int32 / int64 scalar or vector of at most 8 entries");
+  REQUIRE(out_dt(v, 0) == d->dtype, "output dtype must equal the data dtype");
+  return ClaimResult::yes();
+}
+
+// ReduceSum over the last axis of an integer tensor (reduction.rs:894; the mask's key axis)
+ClaimResult reduce_sum_claim(const NodeView& v) {
+  REQUIRE(v.num_outputs() == 1, "ReduceSum expects 1 output");
+  auto* d = v.input_info(0);
+  REQUIRE(d && is_ep_int(d->dtype) && !d->shape.empty(), "only int32 / int64 data of rank >= 1 is reduced on the EP");
+  REQUIRE(out_dt(v, 0) == d->dtype, "output dtype must equal the data dtype");
+  std::vector<int64_t> axes;
+  if (v.since_version() >= 13) {
+    REQUIRE(v.input_present(1), "axes input required (reducing every axis is not claimed)");
+    const Initializer* a = v.const_input(1);
+    REQUIRE(a, "axes must be a constant initializer");
+    axes = const_ints(a);
+  } else {
+    axes = v.ints_attr("axes");
+  }
+  const int64_t rank = (int64_t)d->shape.size();
+  REQUIRE(axes.size() == 1 && norm_axis(axes[0], rank) == rank - 1, "only a reduction over the last axis is claimed");
+  return ClaimResult::yes();
+}
+
+// Unsqueeze / Squeeze / Reshape of integer tensors with constant axes / shape (shape.rs:1646-1745):
+// the values pass through unchanged
+ClaimResult int_layout_claim(const NodeView& v) {
+  REQUIRE(v.num_outputs() == 1, "%s expects 1 output", v.op_type().c_str());
+  auto* d = v.input_info(0);
+  REQUIRE(d && is_ep_int(d->dtype), "only int32 / int64 tensors are reshaped on the EP");
+  REQUIRE(out_dt(v, 0) == d->dtype, "output dtype must equal the data dtype");
+  const bool axes_input = v.op_type() == "Reshape" || v.since_version() >= 13;
+  if (axes_input) {
+    REQUIRE(v.input_present(1) && v.const_input(1), "%s: the %s input must be a constant initializer",
+            v.op_type().c_str(), v.op_type() == "Reshape" ? "shape" : "axes");
+  } else {
+    REQUIRE(v.has_attr("axes"), "%s: axes attribute required", v.op_type().c_str());
+  }
+  if (v.op_type() == "Reshape") {
+    REQUIRE(v.int_attr("allowzero", 0) == 0, "Reshape: allowzero=1 is not claimed");
+    const auto target = const_ints(v.const_input(1));
+    int unknown = 0;
+    for (auto t : target) unknown += t == -1;
+    REQUIRE(unknown <= 1, "Reshape: at most one -1 in the target shape");
+  }
   return ClaimResult::yes();
 }
 
@@ -341,11 +428,34 @@ const OpEntry kTable[] = {
     {"", "Mul", 7, -1, OpKind::kMul, binary_claim},
     {"", "Sigmoid", 6, -1, OpKind::kSigmoid, sigmoid_claim},
     {"", "Cast", 6, -1, OpKind::kCast, cast_claim},
+    {"", "Shape", 1, -1, OpKind::kShape, shape_claim},
+    {"", "Gather", 1, -1, OpKind::kGather, gather_claim},
+    {"", "ReduceSum", 1, -1, OpKind::kReduceSum, reduce_sum_claim},
+    {"", "Unsqueeze", 1, -1, OpKind::kUnsqueeze, int_layout_claim},
+    {"", "Squeeze", 1, -1, OpKind::kSqueeze, int_layout_claim},
+    {"", "Reshape", 5, -1, OpKind::kReshape, int_layout_claim},
 };
 
 }  // namespace
 
 bool is_ep_float(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
+
+std::vector<int64_t> const_ints(const Initializer* init) {
+  std::vector<int64_t> v;
+  if (!init) return v;
+  const int64_t n = init->numel();
+  if (init->dtype == kI64 && init->bytes.size() == (size_t)n * 8) {
+    v.resize(n);
+    memcpy(v.data(), init->bytes.data(), (size_t)n * 8);
+  } else if (init->dtype == kI32 && init->bytes.size() == (size_t)n * 4) {
+    for (int64_t i = 0; i < n; ++i) {
+      int32_t x;
+      memcpy(&x, init->bytes.data() + 4 * i, 4);
+      v.push_back(x);
+    }
+  }
+  return v;
+}
 
 const char* op_kind_name(OpKind k) {
   switch (k) {
@@ -361,6 +471,12 @@ const char* op_kind_name(OpKind k) {
     case OpKind::kMul: return "Mul";
     case OpKind::kSigmoid: return "Sigmoid";
     case OpKind::kCast: return "Cast";
+    case OpKind::kShape: return "Shape";
+    case OpKind::kGather: return "Gather";
+    case OpKind::kReduceSum: return "ReduceSum";
+    case OpKind::kUnsqueeze: return "Unsqueeze";
+    case OpKind::kSqueeze: return "Squeeze";
+    case OpKind::kReshape: return "Reshape";
   }
   return "?";
 }

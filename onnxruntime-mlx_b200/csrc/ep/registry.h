@@ -23,6 +23,13 @@ enum class OpKind {
   kMul,
   kSigmoid,
   kCast,
+  // integer glue of exported decoders (attention mask -> seqlens_k / total_sequence_length)
+  kShape,
+  kGather,
+  kReduceSum,
+  kUnsqueeze,
+  kSqueeze,
+  kReshape,
 };
 
 const char* op_kind_name(OpKind k);
@@ -45,6 +52,8 @@ class NodeView {
   const ValueInfo* output_info(size_t i) const;
   const Initializer* const_input(size_t i) const;
   int64_t int_attr(const std::string& k, int64_t d) const { return n_.int_attr(k, d); }
+  bool has_attr(const std::string& k) const { return n_.has_attr(k); }
+  std::vector<int64_t> ints_attr(const std::string& k) const { return n_.ints_attr(k); }
   float float_attr(const std::string& k, float d) const { return n_.float_attr(k, d); }
   std::string string_attr(const std::string& k, const std::string& d) const;
 
@@ -76,5 +85,8 @@ ClaimResult claim_decision(const NodeView& v);
 inline bool claimable(const NodeView& v) { return claim_decision(v).ok; }
 
 bool is_ep_float(int dtype);
+inline bool is_ep_int(int dtype) { return dtype == 6 || dtype == 7; }  // int32 / int64
+// Integer values of a constant int32 / int64 initializer (empty when it is neither).
+std::vector<int64_t> const_ints(const Initializer* init);
 
 }  // namespace b200ep

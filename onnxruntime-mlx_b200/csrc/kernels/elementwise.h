@@ -25,6 +25,21 @@ cudaError_t launch_sigmoid(const void* x, void* y, int dtype, int64_t n, cudaStr
 cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, int64_t n, cudaStream_t st);
 cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n, cudaStream_t st);
 
+// Integer glue (index_ops.cu): exact int32 / int64 arithmetic for the attention-mask and
+// shape-vector chains of exported decoders.
+struct IdxList {
+  int n = 0;
+  int64_t v[8] = {};
+};
+cudaError_t launch_binary_int(const void* a, const void* b, void* y, int dtype, const BinaryGeom& g, int op,
+                              cudaStream_t st);
+cudaError_t launch_cast_int(const void* x, int in_dt, void* y, int out_dt, int64_t n, cudaStream_t st);
+// y[r] = sum of row r of x ([rows, len] row-major); len is read from *len_dev when it is non-null
+cudaError_t launch_reduce_sum_rows(const void* x, int x_dt, void* y, int y_dt, int64_t rows, int64_t len,
+                                   const int64_t* len_dev, cudaStream_t st);
+cudaError_t launch_gather_idx(const void* x, void* y, int dtype, const IdxList& idx, cudaStream_t st);
+cudaError_t launch_copy_bytes(const void* x, void* y, int64_t bytes, cudaStream_t st);
+
 struct GbqArgs {
   const uint8_t* data;
   const void* scales;

@@ -1407,8 +1407,10 @@ WsLayout ws_layout(const b200ep_gqa_params& p) {
   w.counters = off;
   off += ((size_t)p.batch * p.kv_heads * sizeof(int) + 255) & ~(size_t)255;
   w.partial = off;
-  off += ((size_t)p.batch * p.kv_heads * choose_splits(p) * RP * (p.head_size + 2) * 4 + 255) &
-         ~(size_t)255;
+  // split-K partials exist only for decode-sized rows (the SIMT split-K kernel; decode_path)
+  if (RP <= 32)
+    off += ((size_t)p.batch * p.kv_heads * choose_splits(p) * RP * (p.head_size + 2) * 4 + 255) &
+           ~(size_t)255;
   w.qrot = off;
   off += ((size_t)p.batch * p.seq * p.num_heads * p.head_size * 4 + 255) & ~(size_t)255;
   w.total = off;

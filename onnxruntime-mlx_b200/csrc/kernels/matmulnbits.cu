@@ -1,10 +1,11 @@
 // MatMulNBits kernels for sm_100a (com.microsoft MatMulNBits; reference translation
 // rust/src/ops/quant.rs:986-1130).
 //
-//   mnb_gemv_kernel   decode path, M <= 4: streams the packed weight rows with 128-bit
+//   mnb_gemv_kernel   decode path, M <= 4 (up to 16 rows in chunks of 4): streams the packed weight rows with 128-bit
 //                     non-allocating loads (16 B = 32 int4 values per lane per load), dequantises
 //                     in registers and reduces with warp shuffles.  HBM-bound.
-//   mnb_tile_kernel   any M / layout: SIMT tiled GEMM over a shared-memory dequantised weight
+//   mnb_wide_kernel   many rows (M > 16), int4, K % 32 == 0: SIMT 128 x 128 tiles, 8 x 8 per thread.
+//   mnb_tile_kernel   any other M / layout: SIMT tiled GEMM over a shared-memory dequantised weight
 //                     tile.  Used for shapes the GEMV does not cover (and as the parity path for
 //                     large M until the tensor-core GEMM takes them).
 //   mnb_dequant_kernel  W[N,K] = (q - zp) * scale, bit-exact against the CPU oracle.
@@ -351,6 +352,104 @@ mnb_tile_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B,
   }
 }
 
+// ---- wide tiled kernel (many rows) ----------------------------------------------------------
+// CTA tile 128(m) x 128(n), K step 32, 256 threads each owning an 8 x 8 output micro-tile: 64 FMAs
+// per four 16-byte shared-memory loads.  Weight tile: thread t dequantises row n0 + t / 2, k half
+// t % 2 (16 values: one 8-byte load, one scale, one zero point; blocks of 16 or more keep a half
+// inside one block); activation tile: two rows of 8 values per thread.  The next K step's global
+// loads are issued before the current step's FMAs.  Requires K % 32 == 0, block % 16 == 0, A 16-byte
+// aligned rows (K % 4 == 0), 4-bit weights.
+constexpr int kWM = 128, kWN = 128, kWK = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+mnb_wide_kernel(const T* __restrict__ A, const uint8_t* __restrict__ B, const T* __restrict__ scales,
+                const uint8_t* __restrict__ zp, T* __restrict__ Y, int M, int N, int K, int block, int nblocks) {
+  __shared__ __align__(16) float as[kWK][kWM + 4];
+  __shared__ __align__(16) float ws[kWK][kWN + 4];
+  pdl_wait();
+  pdl_trigger();
+  const int m0 = blockIdx.y * kWM, n0 = blockIdx.x * kWN;
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int64_t rowbytes = (int64_t)nblocks * block / 2;
+  // weight loader: row wn, k half wh
+  const int wn = tid >> 1, wh = tid & 1;
+  const int n = n0 + wn;
+  // activation loader: rows am + 64 i (i < 2), k chunk ak (8 floats)
+  const int am = tid >> 2, ak = (tid & 3) * 8;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  uint2 wq = make_uint2(0, 0);
+  float wsc = 0.f;
+  int wz = 8;
+  float av[2][8];
+  auto load = [&](int k0) {
+    if (n < N) {
+      const int k = k0 + wh * 16;
+      const int64_t blk = k / block;
+      wq = *reinterpret_cast<const uint2*>(B + (size_t)n * rowbytes + k / 2);
+      wsc = to_f<T>(scales[(size_t)n * nblocks + blk]);
+      wz = zp ? ((blk & 1) ? zp[(size_t)n * ((nblocks + 1) >> 1) + (blk >> 1)] >> 4
+                           : zp[(size_t)n * ((nblocks + 1) >> 1) + (blk >> 1)] & 15)
+              : 8;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int m = m0 + am + 64 * i;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) av[i][j] = 0.f;
+      if (m < M) {
+        const T* src = A + (size_t)m * K + k0 + ak;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) av[i][j] = to_f<T>(src[j]);
+      }
+    }
+  };
+  load(0);
+  for (int k0 = 0; k0 < K; k0 += kWK) {
+    // publish this step's tiles
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t word = j < 8 ? wq.x : wq.y;
+      const int q = (word >> (4 * (j & 7))) & 15;
+      ws[wh * 16 + j][wn] = n < N ? (float)(q - wz) * wsc : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) as[ak + j][am + 64 * i] = av[i][j];
+    __syncthreads();
+    if (k0 + kWK < K) load(k0 + kWK);
+#pragma unroll 4
+    for (int kk = 0; kk < kWK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&as[kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&as[kk][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&ws[kk][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&ws[kk][tx * 8 + 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + ty * 8 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int nn = n0 + tx * 8 + j;
+      if (nn < N) Y[(size_t)m * N + nn] = from_f<T>(acc[i][j]);
+    }
+  }
+}
+
 // ---- host launchers -------------------------------------------------------------------------
 namespace {
 
@@ -411,9 +510,27 @@ cudaError_t launch_dtype(const MnbArgs& a, cudaStream_t st) {
   const int64_t rowbytes = nblocks * a.block * a.bits / 8;
   const int64_t mt = a.M <= 1 ? 1 : a.M <= 2 ? 2 : 4;
   const int64_t stage_bytes = mt * (rowbytes / 16) * (128 / a.bits + 4) * 4;
-  const bool gemv_ok = a.M <= 4 && rowbytes % 16 == 0 && stage_bytes <= 200 * 1024 &&
-                       (reinterpret_cast<uintptr_t>(a.B) % 16) == 0;
-  if (gemv_ok) return a.bits == 4 ? launch_gemv_b<T, 4>(a, st) : launch_gemv_b<T, 8>(a, st);
+  const bool gemv_ok = rowbytes % 16 == 0 && stage_bytes <= 200 * 1024 && (reinterpret_cast<uintptr_t>(a.B) % 16) == 0;
+  if (gemv_ok && a.M <= 4) return a.bits == 4 ? launch_gemv_b<T, 4>(a, st) : launch_gemv_b<T, 8>(a, st);
+  if (gemv_ok && a.M <= 16) {
+    // up to 16 rows: the GEMV over chunks of 4 activation rows (the weights, at most a few tens of
+    // MB for decode shapes, come from L2 after the first chunk)
+    for (int64_t m0 = 0; m0 < a.M; m0 += 4) {
+      MnbArgs c = a;
+      c.A = static_cast<const T*>(a.A) + m0 * a.K;
+      c.Y = static_cast<T*>(a.Y) + m0 * a.N;
+      c.M = std::min<int64_t>(4, a.M - m0);
+      cudaError_t e = a.bits == 4 ? launch_gemv_b<T, 4>(c, st) : launch_gemv_b<T, 8>(c, st);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  if (a.bits == 4 && a.K % kWK == 0 && a.block % 16 == 0 && a.K % a.block == 0 && a.M > 16) {
+    dim3 wgrid((unsigned)div_up(a.N, kWN), (unsigned)div_up(a.M, kWM));
+    return launch_k(mnb_wide_kernel<T>, wgrid, dim3(256), 0, st, static_cast<const T*>(a.A), a.B,
+                    static_cast<const T*>(a.scales), a.zp, static_cast<T*>(a.Y), (int)a.M, (int)a.N, (int)a.K,
+                    a.block, (int)nblocks);
+  }
   dim3 grid((unsigned)div_up(a.N, kTN), (unsigned)div_up(a.M, kTM));
   auto kern = a.bits == 4 ? mnb_tile_kernel<T, 4> : mnb_tile_kernel<T, 8>;
   return launch_k(kern, grid, dim3(256), 0, st, static_cast<const T*>(a.A), a.B, static_cast<const T*>(a.scales),

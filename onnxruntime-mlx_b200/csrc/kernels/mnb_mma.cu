@@ -321,11 +321,6 @@ enum { kErrArTimeout = 302 };
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // Consumer side of the peer-memory all-reduce: wait until every source rank published `epoch`
 // (bounded; a timeout records an error and proceeds), then x chunks are sums of the slots.
@@ -649,7 +644,31 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       int slot = 0;
       uint32_t phase = 0;
       int64_t r = rbeg;
+      // xmode 2: the activation rows of a stage's k-range (64 k per record) are bulk-copied beside
+      // its records.  They are the previous kernel's output, so the records of the first ring
+      // stages go out at once and their activation chunks only after the wait for that kernel.
+      auto copy_x = [&](int sl, int64_t rr, int n) {
+        const int kr = (int)(rr - (rr / ksteps4) * ksteps4);
+        unsigned char* sb = buf + (size_t)sl * stage_bytes;
+        for (int row = 0; row < vrows; ++row)
+          bulk_g2s(sb + rec_bytes + (size_t)row * kXcStride, A + (size_t)(m0 + row) * K + (size_t)kr * 64,
+                   (uint32_t)(n * 128), &full[sl]);
+      };
+      bool waited = xmode != 2;
+      int npend = 0;  // stages issued without their chunks: the first npend stages from rbeg
+      auto flush = [&]() {
+        pdl_wait();
+        int64_t rr = rbeg;
+        for (int j = 0; j < npend; ++j) {
+          const int nn = (int)lmin(G, lmin(rend, (rr / ksteps4 + 1) * ksteps4) - rr);
+          copy_x(j, rr, nn);
+          rr += nn;
+        }
+        npend = 0;
+        waited = true;
+      };
       for (int i = 0; r < rend; ++i) {
+        if (i >= stages && !waited) flush();  // before the ring wraps: the consumers need these chunks
         if (i >= stages && !mbar_wait(&empty[slot], phase ^ 1)) {
           flags[0] = 1;
           break;
@@ -659,12 +678,11 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         const uint32_t bytes = (uint32_t)(n * RC::kBytes);
         unsigned char* sbuf = buf + (size_t)slot * stage_bytes;
         if (xmode == 2) {
-          // the activation rows of this stage's k-range (64 k per record), beside the records
-          const int kr = (int)(r - (r / ksteps4) * ksteps4);
           mbar_arrive_expect_tx(&full[slot], bytes + (uint32_t)(vrows * n * 128));
-          for (int row = 0; row < vrows; ++row)
-            bulk_g2s(sbuf + rec_bytes + (size_t)row * kXcStride, A + (size_t)(m0 + row) * K + (size_t)kr * 64,
-                     (uint32_t)(n * 128), &full[slot]);
+          if (waited)
+            copy_x(slot, r, n);
+          else  // i < stages here, so slot == i == npend
+            ++npend;
         } else {
           mbar_arrive_expect_tx(&full[slot], bytes);
         }
@@ -672,6 +690,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         r += n;
         if (++slot == stages) slot = 0, phase ^= 1;
       }
+      if (!waited) flush();
     }
     return;
   }
@@ -679,11 +698,9 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   // consumers: stage the activation rows of this column chunk while the first copies are in flight
   pdl_wait();
   pdl_trigger();
-  // tensor-parallel partial output: this launch writes region (epoch + 1) & 1 (see MnbAr)
+  // tensor-parallel partial output: this launch publishes epoch + 1 (see MnbAr)
   const unsigned oepoch = oar.world ? __ldcg(oar.ctrs) + 1 : 0;
-  const size_t obase =
-      oar.world ? kArFlagsBytes + (size_t)(oepoch & 1) * oar.region_bytes + (size_t)oar.rank * oar.slot_bytes : 0;
-  bool pushed = false;  // this thread stored into peer mailboxes
+
   if (stage_x) {
     if (pro.kind == kProNone) {
       // 16-byte loads (8 k), each scattered to its 4 fragment-order words; K % 8 == 0 here
@@ -833,8 +850,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
         }
       consumer_barrier<NC>();
       // thread tid sums output row tid % 16 of token column tid / 16: a column's 16 rows are 16
-      // lanes of one warp, so its outputs (and the tensor-parallel mailbox copies) are one 32-byte
-      // store per destination
+      // lanes of one warp, so its outputs are one 32-byte store
       for (int tid = threadIdx.x; tid < 256; tid += NC * 32) {
         const int row = tid & 15, col = tid >> 4;
         const int m = m0 + col, n = t * 16 + row;
@@ -845,12 +861,7 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
           float v = 0.f;
 #pragma unroll
           for (int w = 0; w < NC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
-          const T tv = from_f<T>(v);
-          Y[(size_t)m * N + n] = tv;
-          // tensor-parallel partial output: slot `rank` of every rank's mailbox, as the tile completes
-          for (int d = 0; d < oar.world; ++d)
-            *reinterpret_cast<T*>(oar.mbox[d] + obase + ((size_t)m * N + n) * sizeof(T)) = tv;
-          pushed = oar.world > 0;
+          Y[(size_t)m * N + n] = from_f<T>(v);
         }
       }
       ++tp;
@@ -861,17 +872,30 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
   }
   if (flags[0] && threadIdx.x == 0) report_device_error(err, kErrMnbTimeout, blockIdx.x);
   if (oar.world) {
-    // publish: every tile this CTA wrote is already in every rank's mailbox.  The threads that
-    // stored fence at system scope; the CTA then counts itself in (acq_rel), and the last CTA of the
-    // launch — which has observed every other CTA's count, each ordered after that CTA's fences —
-    // records the epoch and releases it in every rank's flag word for this source.
-    if (pushed) __threadfence_system();
+    // publish the partial output: the last CTA to finish pushes Y (M x N, complete once every
+    // CTA's writes are visible) into slot `rank` of every rank's mailbox with 16-byte stores,
+    // fences them at system scope, bumps the epoch and releases the flags
+    __threadfence();
     consumer_barrier<NC>();
-    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1) {
-      oar.ctrs[1] = 0;
-      oar.ctrs[0] = oepoch;
-      for (int d = 0; d < oar.world; ++d)
-        st_release_sys(reinterpret_cast<unsigned*>(oar.mbox[d]) + oar.rank, oepoch);
+    if (threadIdx.x == 0) flags[1] = atomicAdd(&oar.ctrs[1], 1u) == gridDim.x * gridDim.y - 1;
+    consumer_barrier<NC>();
+    if (flags[1]) {
+      __threadfence();
+      const size_t bytes = (size_t)M * N * sizeof(T);  // multiple of 16 (N % 8 == 0)
+      const size_t off = kArFlagsBytes + (size_t)(oepoch & 1) * oar.region_bytes + (size_t)oar.rank * oar.slot_bytes;
+      const uint4* src = reinterpret_cast<const uint4*>(Y);
+      for (int d = 0; d < oar.world; ++d) {
+        uint4* dst = reinterpret_cast<uint4*>(oar.mbox[d] + off);
+        for (size_t i = threadIdx.x; i < bytes / 16; i += NC * 32) dst[i] = __ldcg(src + i);
+      }
+      __threadfence_system();
+      consumer_barrier<NC>();
+      if (threadIdx.x == 0) {
+        oar.ctrs[1] = 0;
+        oar.ctrs[0] = oepoch;
+        for (int d = 0; d < oar.world; ++d)
+          st_release_sys(reinterpret_cast<unsigned*>(oar.mbox[d]) + oar.rank, oepoch);
+      }
     }
   }
 }
@@ -928,6 +952,8 @@ cudaError_t launch_mnb_prepack(const uint8_t* B, const void* scales, const uint8
 DeviceErrorSlot* device_error_slot();
 
 namespace {
+constexpr size_t kSmemCap = 232448;  // dynamic shared memory per CTA on sm_100
+
 template <typename T, int BLOCK, int NT, bool PAIR, int G>
 cudaError_t launch_tma_g(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaStream_t st, const MnbPro& pro,
                          const MnbAr& oar, int xrows, int xmode, size_t x_bytes) {
@@ -940,7 +966,6 @@ cudaError_t launch_tma_g(const void* A, const MnbPacked& p, void* Y, int64_t M, 
     const size_t stage = (size_t)G * RC::kBytes + (xmode == 2 ? (size_t)8 * NT * kXcStride : 0);
     return 256 + (size_t)stages * stage + (size_t)2 * NC * NT * 4 * 32 * 4 + (xrows ? x_bytes : 0);
   };
-  constexpr size_t kSmemCap = 232448;  // dynamic shared memory per CTA on sm_100
   static size_t configured = 0;        // per instantiation: the largest dynamic smem set so far
   auto configure = [&](size_t smem) -> cudaError_t {
     if (smem <= configured) return cudaSuccess;
@@ -1002,9 +1027,12 @@ cudaError_t launch_tma_t(const void* A, const MnbPacked& p, void* Y, int64_t M, 
   // activation modes: 1 = all rows staged once per CTA; 2 = each stage's k-range bulk-copied beside
   // its records (rows too long to stage whole, e.g. 16 rows at K 14336); 0 = read from global memory
   const int xmode = xrows ? 1 : (a16 && p.K % 64 == 0 && p.ksteps4 * 64 == p.K) ? 2 : 0;
-  // long streams of whole kGLong-record stages (at least three per CTA) run the long stages
+  // long streams of whole kGLong-record stages (at least three per CTA) run the long stages when a
+  // two-stage ring of them, the merge buffers and the staged rows fit one CTA
   const int64_t per_cta = (int64_t)p.ntiles * p.ksteps4 / std::max<int64_t>(1, std::min<int64_t>(p.ntiles, 2 * num_sms()));
-  if (xmode == 1 && p.ksteps4 % kGLong == 0 && per_cta >= 3 * kGLong)
+  constexpr int NCx = NT == 2 ? 2 * kNC : kNC;
+  const size_t smem_long = 256 + (size_t)2 * kGLong * Rec<BLOCK>::kBytes + (size_t)2 * NCx * NT * 4 * 32 * 4 + x_bytes;
+  if (xmode == 1 && p.ksteps4 % kGLong == 0 && per_cta >= 3 * kGLong && smem_long <= kSmemCap)
     return launch_tma_g<T, BLOCK, NT, PAIR, kGLong>(A, p, Y, M, st, pro, oar, xrows, xmode, x_bytes);
   return launch_tma_g<T, BLOCK, NT, PAIR, kG>(A, p, Y, M, st, pro, oar, xrows, xmode, x_bytes);
 }

@@ -26,14 +26,12 @@ struct MnbPacked {
 // x = [M, 2K] holding g in columns [0, K) and u in [K, 2K).
 enum MnbProKind : int { kProNone = 0, kProRms = 1, kProSkipRms = 2, kProSiluMul = 3 };
 // Peer-memory all-reduce between tensor-parallel ranks (one process per GPU, NVLink P2P).  Every
-// rank owns a mailbox mapped into all ranks: [flags: uint32 per source rank][2 regions][source rank
-// slots].  A producer GEMV writes each output tile, rounded to the I/O dtype, into slot `rank` of
-// region (epoch & 1) of every rank's mailbox as soon as the tile is complete (the pushes overlap the
-// rest of the launch); at the end the threads that pushed fence at system scope, every CTA counts
-// itself in, and the launch's last CTA releases `epoch` in every rank's flag word for `rank` (system
-// scope).  A consumer prologue reads the local epoch counter, waits (bounded) until every source's
-// flag reaches it, and sums the slots in rank order — the same order on every rank, so replicated
-// activations stay identical.
+// rank owns a mailbox mapped into all ranks: [flags: uint32 per source rank][2 regions][source
+// rank slots].  A producer GEMV stores its partial output, rounded to the I/O dtype, into slot
+// `rank` of region (epoch & 1) of every rank's mailbox, fences, and its last CTA publishes
+// `epoch` in every rank's flag word for `rank` (release, system scope).  A consumer prologue reads
+// the local epoch counter, waits (bounded) until every source's flag reaches it, and sums the
+// slots in rank order — the same order on every rank, so replicated activations stay identical.
 constexpr int kArMaxRanks = 8;
 constexpr size_t kArFlagsBytes = 256;
 struct MnbAr {

@@ -64,13 +64,17 @@ def rotary_caches(max_seq, rotary_dim, base, np_dtype):
 
 
 def build_decoder(cfg: DecoderConfig, *, batch: int, seq: int, cap: int, with_lm_head: bool = True,
-                  weights_out: dict | None = None) -> GraphBuilder:
+                  weights_out: dict | None = None, mask_glue: bool = False) -> GraphBuilder:
     """One graph for a [batch, seq] step over KV buffers of capacity `cap`.
 
     Inputs: input_ids int64 [B, S], seqlens_k int32 [B], total_sequence_length int32 [1],
     past_key_values.{i}.key / .value [B, kv_heads, cap, head_dim].
     Outputs: logits [B, S, vocab] (or the final hidden state), present.{i}.key / .value.
     ``weights_out`` (optional) receives every initializer, for oracle cross-checks.
+    ``mask_glue``: take attention_mask int64 [B, past + S] instead of seqlens_k /
+    total_sequence_length and derive both in the graph the way GenAI-exported decoders do:
+    seqlens_k = Cast(Sub(ReduceSum(mask, axes=[1]), 1)), total = Cast(Gather(Shape(mask), 1)).
+    The weights are drawn identically, so both forms compute the same logits.
     """
     rng = np.random.default_rng(cfg.seed)
     dt, code = cfg.np_dtype, cfg.code
@@ -93,8 +97,26 @@ def build_decoder(cfg: DecoderConfig, *, batch: int, seq: int, cap: int, with_lm
         return out
 
     g.input("input_ids", INT64, [batch, seq])
-    g.input("seqlens_k", INT32, [batch])
-    g.input("total_sequence_length", INT32, [1])
+    if mask_glue:
+        g.input("attention_mask", INT64, [batch, -1])
+        g.initializer("mask_axes", np.array([1], np.int64))
+        g.initializer("one_i64", np.array(1, np.int64))
+        g.initializer("mask_len_axis", np.array(1, np.int64))
+        g.tensor("mask_sum", INT64, [batch])
+        g.node("ReduceSum", ["attention_mask", "mask_axes"], ["mask_sum"], name="mask_sum", keepdims=0)
+        g.tensor("mask_past", INT64, [batch])
+        g.node("Sub", ["mask_sum", "one_i64"], ["mask_past"], name="mask_past")
+        g.tensor("seqlens_k", INT32, [batch])
+        g.node("Cast", ["mask_past"], ["seqlens_k"], name="seqlens_k", to=INT32)
+        g.tensor("mask_shape", INT64, [2])
+        g.node("Shape", ["attention_mask"], ["mask_shape"], name="mask_shape")
+        g.tensor("mask_width", INT64, [])
+        g.node("Gather", ["mask_shape", "mask_len_axis"], ["mask_width"], name="mask_width", axis=0)
+        g.tensor("total_sequence_length", INT32, [])
+        g.node("Cast", ["mask_width"], ["total_sequence_length"], name="total_sequence_length", to=INT32)
+    else:
+        g.input("seqlens_k", INT32, [batch])
+        g.input("total_sequence_length", INT32, [1])
     cos, sin = rotary_caches(cfg.max_seq, D, cfg.rope_base, dt)
     init("cos_cache", cos)
     init("sin_cache", sin)

@@ -338,3 +338,71 @@ def test_paged_attention_declines_with_reason(kw, reason):
     ep, groups, _ = claimed(paged_graph(**kw))
     assert groups == [-1]
     assert reason in ep.claim_reason(0)
+
+
+def test_mask_glue_decoder_claimed_whole():
+    """A GenAI-style decoder (attention_mask in, seqlens_k / total_sequence_length derived in the
+    graph by ReduceSum / Sub / Cast and Shape / Gather / Cast) is claimed as one partition."""
+    from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
+
+    cfg = DecoderConfig(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000, max_seq=256)
+    g = build_decoder(cfg, batch=2, seq=1, cap=64, mask_glue=True)
+    _, groups, num = claimed(g)
+    assert num == 1 and set(groups) == {0}
+    assert {"mask_sum", "mask_past", "seqlens_k", "mask_shape", "mask_width", "total_sequence_length"} <= set(g.node_names)
+
+
+def _glue_graph(op, data_dtype, data_shape, out_dtype, out_shape, extra=None, **attrs):
+    g = GraphBuilder()
+    g.input("x", data_dtype, data_shape)
+    ins = ["x"]
+    for name, arr in (extra or []):
+        g.initializer(name, arr)
+        ins.append(name)
+    g.output("y", out_dtype, out_shape)
+    g.node(op, ins, ["y"], **attrs)
+    return g
+
+
+@pytest.mark.parametrize("op,args,attrs", [
+    ("Shape", (INT64, [2, -1], INT64, [2], None), {}),
+    ("Shape", (FLOAT16, [2, 3, 4], INT64, [1], None), dict(start=-1)),
+    ("Gather", (INT64, [4], INT64, [], [("i", np.array(1, np.int64))]), dict(axis=0)),
+    ("Gather", (INT64, [4], INT64, [2], [("i", np.array([0, -1], np.int64))]), {}),
+    ("ReduceSum", (INT64, [2, -1], INT64, [2], [("a", np.array([1], np.int64))]), dict(keepdims=0)),
+    ("ReduceSum", (INT32, [2, 5], INT32, [2, 1], [("a", np.array([-1], np.int64))]), {}),
+    ("Unsqueeze", (INT64, [2], INT64, [1, 2], [("a", np.array([0], np.int64))]), {}),
+    ("Squeeze", (INT64, [1, 2], INT64, [2], [("a", np.array([0], np.int64))]), {}),
+    ("Reshape", (INT32, [2, 3], INT32, [6], [("s", np.array([-1], np.int64))]), {}),
+    ("Cast", (INT64, [2], INT32, [2], None), dict(to=INT32)),
+    ("Sub", (INT64, [2], INT64, [2], [("b", np.array(1, np.int64))]), {}),
+])
+def test_integer_glue_claims(op, args, attrs):
+    g = _glue_graph(op, *args, **attrs)
+    ep, groups, num = claimed(g)
+    assert groups == [0] and num == 1, ep.claim_reason(0)
+
+
+@pytest.mark.parametrize("op,args,attrs,reason", [
+    ("Gather", (FLOAT, [4, 8], FLOAT, [8], [("i", np.array(1, np.int64))]), dict(axis=0), "1-D int32 / int64"),
+    ("ReduceSum", (INT64, [2, 5], INT64, [5], [("a", np.array([0], np.int64))]), dict(keepdims=0), "last axis"),
+    ("ReduceSum", (FLOAT, [2, 5], FLOAT, [2], [("a", np.array([1], np.int64))]), dict(keepdims=0), "int32 / int64"),
+    ("Cast", (INT64, [2], FLOAT, [2], None), dict(to=FLOAT), "casts are claimed"),
+    ("Reshape", (INT32, [2, 3], INT32, [6], [("s", np.array([-1, -1], np.int64))]), {}, "at most one -1"),
+    ("Unsqueeze", (FLOAT, [2], FLOAT, [1, 2], [("a", np.array([0], np.int64))]), {}, "int32 / int64"),
+])
+def test_integer_glue_declines_with_reason(op, args, attrs, reason):
+    g = _glue_graph(op, *args, **attrs)
+    ep, groups, num = claimed(g)
+    assert groups == [-1] and num == 0
+    assert reason in ep.claim_reason(0)
+
+
+def test_gather_with_runtime_indices_declined():
+    g = GraphBuilder()
+    g.input("x", INT64, [4])
+    g.input("i", INT64, [])
+    g.output("y", INT64, [])
+    g.node("Gather", ["x", "i"], ["y"], axis=0)
+    ep, groups, _ = claimed(g)
+    assert groups == [-1] and "constant" in ep.claim_reason(0)

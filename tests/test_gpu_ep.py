@@ -293,7 +293,7 @@ def _compare_logits(got, want, what):
     assert agree >= 0.95, f"{what}: top-1 agreement {agree}"
 
 
-@pytest.mark.parametrize("shape,P,steps", [("8b", 512, 8), ("70b", 64, 4)])
+@pytest.mark.parametrize("shape,P,steps", [("8b", 512, 8), ("70b", 64, 4), ("70b", 16, 2)])
 def test_llama_layer_prefill_then_decode_matches_oracle(ep_mod, shape, P, steps):
     """One decoder layer: a prompt (512 tokens for the Llama-3-8B layer, 64 for the Llama-3-70B
     layer: tcgen05 prefill GEMM, tensor-core prompt attention) then decode steps (fused norm / SiLU
@@ -443,3 +443,108 @@ def test_gqa_sliding_window_cache_through_ep(ep_mod):
         np.testing.assert_array_equal(tv.cpu().numpy(), ov)
         n += S
     assert json.loads(sess.parts[0].describe())["graph_replays"] >= 25
+
+
+def _mask_glue_graph(ep_mod, B):
+    """The attention-mask chain of a GenAI-exported decoder on its own: seqlens_k and
+    total_sequence_length are partition outputs (device ReduceSum / Sub / Cast; host Shape / Gather /
+    Cast whose value is uploaded)."""
+    g = ep_mod.GraphBuilder()
+    g.input("attention_mask", ep_mod.INT64, [B, -1])
+    g.initializer("axes", np.array([1], np.int64))
+    g.initializer("one", np.array(1, np.int64))
+    g.initializer("width_axis", np.array(1, np.int64))
+    g.tensor("msum", ep_mod.INT64, [B])
+    g.node("ReduceSum", ["attention_mask", "axes"], ["msum"], keepdims=0)
+    g.tensor("mpast", ep_mod.INT64, [B])
+    g.node("Sub", ["msum", "one"], ["mpast"])
+    g.output("seqlens_k", ep_mod.INT32, [B])
+    g.node("Cast", ["mpast"], ["seqlens_k"], to=ep_mod.INT32)
+    g.tensor("mshape", ep_mod.INT64, [2])
+    g.node("Shape", ["attention_mask"], ["mshape"])
+    g.tensor("width", ep_mod.INT64, [])
+    g.node("Gather", ["mshape", "width_axis"], ["width"], axis=0)
+    g.output("total_sequence_length", ep_mod.INT32, [])
+    g.node("Cast", ["width"], ["total_sequence_length"], to=ep_mod.INT32)
+    return g
+
+
+def test_attention_mask_glue_values(ep_mod):
+    """seqlens_k = sum(mask) - 1 per row and total = mask width, for host- and device-resident masks
+    of changing width (crossing a key-capacity boundary) with padded rows; one compiled program serves
+    every width of a capacity bucket."""
+    B = 3
+    sess = ep_mod.Session(_mask_glue_graph(ep_mod, B))  # two unconnected chains: one partition each
+    rng = np.random.default_rng(5)
+    for T in (1, 9, 63, 64, 65, 100, 128, 129, 700):
+        mask = np.ones((B, T), np.int64)
+        pad = rng.integers(0, T, size=B)
+        for b in range(B):
+            mask[b, :pad[b]] = 0
+        for host in (True, False):
+            r = sess.run({"attention_mask": mask if host else cuda(mask)})
+            np.testing.assert_array_equal(r["seqlens_k"].cpu().numpy(), mask.sum(1).astype(np.int32) - 1)
+            assert int(r["total_sequence_length"].cpu().numpy()) == T
+    ops = set()
+    for part in sess.parts:
+        ops |= set(json.loads(part.describe())["ops"])
+    assert {"Shape", "Gather", "ReduceSum", "Cast", "Binary"} <= ops
+
+
+def test_mask_glue_decoder_matches_explicit_lengths(ep_mod):
+    """A decoder fed attention_mask (GenAI export form: lengths derived in the graph) is claimed whole
+    and computes exactly the logits of the same decoder fed seqlens_k / total_sequence_length; its
+    decode steps replay one CUDA graph although the mask widens every step."""
+    from onnxruntime_ep_b200.decoder import DecoderConfig, build_decoder
+
+    cfg = DecoderConfig(**SMALL)
+    B, P, cap, steps = 2, 8, 64, 6
+    sessions = {}
+    for glue in (False, True):
+        sessions[glue] = (ep_mod.Session(build_decoder(cfg, batch=B, seq=P, cap=cap, mask_glue=glue)),
+                          ep_mod.Session(build_decoder(cfg, batch=B, seq=1, cap=cap, mask_glue=glue)))
+    kv = {glue: [[torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda")
+                  for _ in range(2)] for _ in range(cfg.layers)] for glue in (False, True)}
+    dec_ids = torch.zeros(B, 1, dtype=torch.int64, device="cuda")
+    dec_seq = torch.zeros(B, dtype=torch.int32, device="cuda")
+    dec_tot = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def feeds(glue, ids, past):
+        S = ids.shape[1]
+        if S == 1:
+            dec_ids.copy_(cuda(ids))
+            f = {"input_ids": dec_ids}
+        else:
+            f = {"input_ids": cuda(ids)}
+        if glue:
+            f["attention_mask"] = np.ones((B, past + S), np.int64)  # host-resident, as GenAI feeds it
+        elif S == 1:
+            dec_seq.fill_(past)
+            dec_tot.fill_(past + 1)
+            f.update(seqlens_k=dec_seq, total_sequence_length=dec_tot)
+        else:
+            f.update(seqlens_k=cuda(np.full(B, past + S - 1, np.int32)),
+                     total_sequence_length=cuda(np.array([past + S], np.int32)))
+        outs = {}
+        for i in range(cfg.layers):
+            f[f"past_key_values.{i}.key"], f[f"past_key_values.{i}.value"] = kv[glue][i]
+            outs[f"present.{i}.key"], outs[f"present.{i}.value"] = kv[glue][i]
+        return f, outs
+
+    rng = np.random.default_rng(11)
+    ids = rng.integers(0, cfg.vocab, size=(B, P), dtype=np.int64)
+    got = {glue: sessions[glue][0].run(*feeds(glue, ids, 0))["logits"].float().cpu().numpy() for glue in (False, True)}
+    np.testing.assert_array_equal(got[True], got[False])
+    for t in range(steps):
+        ids = rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64)
+        got = {glue: sessions[glue][1].run(*feeds(glue, ids, P + t))["logits"].float().cpu().numpy()
+               for glue in (False, True)}
+        np.testing.assert_array_equal(got[True], got[False])
+    for i in range(cfg.layers):
+        for j in range(2):
+            assert torch.equal(kv[True][i][j], kv[False][i][j])
+    sd = sessions[True][1].ep.summary()
+    assert sd["claimed_nodes"] == sd["total_nodes"] and sd["partitions"] == 1
+    d = json.loads(sessions[True][1].parts[0].describe())
+    assert d["graph_replays"] >= steps - 2 and d["graph_captures"] == 1
+    assert sd["key_misses"] == 1

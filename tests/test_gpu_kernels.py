@@ -471,7 +471,10 @@ def test_matmulnbits_prepacked_vs_oracle(ops, block, M, asym):
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (1, 14336, 4096), (1, 4096, 28672), (16, 4096, 4096),
                                    (512, 4096, 1024), (1, 1168, 96), (200, 1024, 18944), (300, 4096, 20480),
-                                   (1000, 256, 28672), (16, 14336, 4096), (5, 14336, 200)])
+                                   (1000, 256, 28672), (16, 14336, 4096), (5, 14336, 200),
+                                   # Llama-3-70B shapes at 16 rows, whole and per rank of 2
+                                   (16, 8192, 10240), (16, 8192, 5120), (16, 4096, 8192), (16, 8192, 28672),
+                                   (16, 14336, 8192), (2, 8192, 28672)])
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_matmulnbits_prepacked_llama_shapes(ops, M, K, N, dt):
     rng = np.random.default_rng(M + K * 3 + N)

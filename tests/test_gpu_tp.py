@@ -12,8 +12,15 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-CFG = dict(layers=2, hidden=256, heads=8, kv_heads=4, head_dim=32, ffn=512, vocab=1000, max_seq=64)
-B, P, CAP, STEPS = 2, 16, 32, 3  # prefill: 32 rows (NCCL all-reduce); decode: 2 rows (peer mailboxes)
+CFGS = {
+    # prefill: 32 rows (NCCL all-reduce); decode: 2 rows (peer mailboxes)
+    "small": (dict(layers=2, hidden=256, heads=8, kv_heads=4, head_dim=32, ffn=512, vocab=1000, max_seq=64), 2),
+    # two Llama-3-70B-shaped layers (hidden 8192, 64 / 8 heads, FFN 28672) at batch 1: 8192-wide norm
+    # prologues over the mailbox sums, 8 query heads per local kv head
+    "70b-layers": (dict(layers=2, hidden=8192, heads=64, kv_heads=8, head_dim=128, ffn=28672, vocab=512,
+                        max_seq=64), 1),
+}
+P, CAP, STEPS = 16, 32, 3
 
 
 def _gpus():
@@ -31,7 +38,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, shape, tp_attention):
     import datetime
 
     import torch
@@ -44,14 +51,15 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
     sess_p = sess_d = None
+    CFG, B = CFGS[shape]
     try:
         obj = [E.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         cfg = DecoderConfig(**CFG)
-        ep_p = E.ExecutionProvider(device_id=rank)
+        ep_p = E.ExecutionProvider(device_id=rank, tp_attention=tp_attention)
         ep_p.set_tensor_parallel(rank, world, obj[0])
         sess_p = E.Session(build_decoder(cfg, batch=B, seq=P, cap=CAP), ep_p)
-        ep_d = E.ExecutionProvider(device_id=rank)
+        ep_d = E.ExecutionProvider(device_id=rank, tp_attention=tp_attention)
         obj2 = [E.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj2, src=0)
         ep_d.set_tensor_parallel(rank, world, obj2[0])
@@ -59,7 +67,7 @@ def _rank_main(rank, world, port, q):
         import json
 
         desc = json.loads(sess_d.parts[0].describe())
-        hk = cfg.kv_heads // world
+        hk = cfg.kv_heads // world if tp_attention == "sharded" else cfg.kv_heads
         kv = [[torch.zeros(B, hk, CAP, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
               for _ in range(cfg.layers)]
         rng = np.random.default_rng(7)
@@ -83,7 +91,8 @@ def _rank_main(rank, world, port, q):
             f, o = feeds(ids_all[t + 1], P + t)
             logits.append(sess_d.run(f, o)["logits"].float().cpu().numpy())
         torch.cuda.synchronize()
-        q.put((rank, logits, ids_all, None if desc["peer_allreduce"] == 2 * cfg.layers
+        sites = (2 if tp_attention == "sharded" else 1) * cfg.layers
+        q.put((rank, logits, ids_all, None if desc["peer_allreduce"] == sites
                else f"peer_allreduce sites {desc['peer_allreduce']}"))
     except Exception as e:  # noqa: BLE001
         q.put((rank, None, None, repr(e)))
@@ -93,7 +102,11 @@ def _rank_main(rank, world, port, q):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_decoder_matches_oracle():
+@pytest.mark.parametrize("shape,tp_attention", [("small", "sharded"), ("70b-layers", "sharded"),
+                                                ("small", "replicated")])
+def test_tp2_decoder_matches_oracle(shape, tp_attention):
+    """Two ranks against the oracle of the unsharded graph.  tp_attention = "replicated" runs attention
+    in full on every rank (one all-reduce per layer, after the FFN)."""
     import torch.multiprocessing as mp
 
     from oracle import oracle  # noqa: F401  (builds the C oracle)
@@ -103,7 +116,7 @@ def test_tp2_decoder_matches_oracle():
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, shape, tp_attention)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=600) for _ in range(world)], key=lambda x: x[0])
@@ -114,6 +127,7 @@ def test_tp2_decoder_matches_oracle():
     # every rank holds the full (all-gathered) logits
     for step in range(STEPS + 1):
         np.testing.assert_array_equal(res[0][1][step], res[1][1][step])
+    CFG, B = CFGS[shape]
     cfg = DecoderConfig(**CFG)
     ids_all = res[0][2]
     Wp, Wd = {}, {}
