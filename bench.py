@@ -578,7 +578,8 @@ def paged_prompt_timing(S, past, peaks, peak_kind, reps=10, block=16):
 
 def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
     """GroupQueryAttention over a whole prompt (32 q / 8 kv heads, head 128, fp16, past 0): the
-    rotate-and-append kernel plus the tensor-core prefill kernel, CUDA-event timed over graph
+    rotate-and-append kernel, the value transpose and the tcgen05 prompt kernel
+    (ONNXRUNTIME_EP_B200_NO_UMMA_ATTN=1: the mma.sync prompt kernel), CUDA-event timed over graph
     replays.  Algorithmic work: causal q.k and p.v, 4 * H * D * S * (S + 1) / 2 flops."""
     import torch
 
@@ -615,7 +616,9 @@ def gqa_prefill_timing(S, peaks, peak_kind, reps=10):
     flops = 4 * H * D * S * (S + 1) / 2
     peak = float(peaks.get("bf16_tflops", TENSOR_FALLBACK))
     tf = flops / launch_s / 1e12
-    return {"kernel": "gqa_append_kernel + gqa_mma_prefill_kernel", "S": S, "launch_us": round(launch_s * 1e6, 2),
+    kern = ("gqa_append_kernel + gqa_mma_prefill_kernel" if os.environ.get("ONNXRUNTIME_EP_B200_NO_UMMA_ATTN")
+            else "gqa_append_kernel + gqa_vt_kernel + gqa_umma_prefill_kernel")
+    return {"kernel": kern, "S": S, "launch_us": round(launch_s * 1e6, 2),
             "achieved": round(tf, 1), "unit": "TFLOP/s", "peak": peak, "frac": round(tf / peak, 4),
             "peak_source": f"{peak_kind} bf16_tflops (burst)"}
 
@@ -1054,9 +1057,10 @@ def main():
     ap.add_argument("--no-side-leg", action="store_true",
                     help="N > 1: skip the other parallel form's measurement reported beside the headline")
     ap.add_argument("--no-parity", action="store_true", help="N > 1 tensor parallel: skip the tp_parity check")
-    ap.add_argument("--tp-attention", default="sharded", choices=["sharded", "replicated"],
+    ap.add_argument("--tp-attention", default="auto", choices=["auto", "sharded", "replicated"],
                     help="tensor parallel: attention sharded by KV head (two all-reduces per layer) or run in "
-                         "full on every rank (one all-reduce per layer, after the FFN)")
+                         "full on every rank (one all-reduce per layer, after the FFN); auto = the faster form "
+                         "measured for the model (replicated for the 8B shape, sharded for the 70B shape)")
     ap.add_argument("--kernel-only", nargs="?", const="gemv",
                     choices=["gemv", "gemv-shapes", "gqa", "gemm", "paged", "c1"],
                     help="time one kernel alone (gemv: the roofline leg; gemv-shapes: every decode projection of "
@@ -1068,7 +1072,7 @@ def main():
     args.warmup = max(args.warmup, 3)
     global MODEL, PROMPT, LAYERS, TP_ATTENTION
     MODEL = args.model
-    TP_ATTENTION = args.tp_attention
+    TP_ATTENTION = args.tp_attention if args.tp_attention != "auto" else ("replicated" if MODEL == "8b" else "sharded")
     LAYERS = args.layers
     PROMPT = args.prompt or (2048 if MODEL == "70b" else 1024)
 
@@ -1091,7 +1095,7 @@ def main():
         if args.kernel_only == "gqa":
             for b, ctx in ((1, 1024), (1, 8192), (8, 8192)):
                 print(json.dumps(gqa_kernel_timing(b, ctx, peaks, peak_kind)), flush=True)
-            for S in (512, 1024, 4096):
+            for S in (512, 1024, 4096, 8192):
                 print(json.dumps(gqa_prefill_timing(S, peaks, peak_kind)), flush=True)
         elif args.kernel_only == "paged":
             cases = ((args.batch, args.context),) if args.context else ((1, 1024), (8, 1024), (8, 8192), (32, 2048))

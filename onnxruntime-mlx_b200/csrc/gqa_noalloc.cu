@@ -61,7 +61,7 @@ extern "C" B200EP_API int b200ep_group_query_attention_noalloc(
     B200EP_CHECK_ARG(p->batch > 0 && p->seq > 0 && p->num_heads > 0 && p->kv_heads > 0 && p->head_size > 0 &&
                          p->num_heads % p->kv_heads == 0,
                      "GroupQueryAttention (no-alloc): invalid geometry");
-    const size_t need = gqa_workspace_bytes(*p);
+    const size_t need = gqa_workspace_min_bytes(*p);
     if (need > kNoAllocScratchBytes)
       return set_error(B200EP_ERANGE, "GroupQueryAttention (no-alloc): this geometry needs " + std::to_string(need) +
                                           " bytes of scratch, above the fixed " +

@@ -1396,7 +1396,7 @@ int choose_splits(const b200ep_gqa_params& p) {
 }
 
 struct WsLayout {
-  size_t counters, partial, qrot, total;
+  size_t counters, partial, qrot, vt, base, total;  // base: without the optional V^T region
 };
 
 WsLayout ws_layout(const b200ep_gqa_params& p) {
@@ -1413,6 +1413,10 @@ WsLayout ws_layout(const b200ep_gqa_params& p) {
            ~(size_t)255;
   w.qrot = off;
   off += ((size_t)p.batch * p.seq * p.num_heads * p.head_size * 4 + 255) & ~(size_t)255;
+  w.base = off;
+  // prompts on the tensor-core kernel: the transposed value rows of every (batch, kv head)
+  w.vt = off;
+  if (p.seq > 1 && p.head_size == 128) off += (gqa_umma_vt_bytes(p.batch, p.kv_heads, p.cap) + 255) & ~(size_t)255;
   w.total = off;
   return w;
 }
@@ -1562,6 +1566,7 @@ cudaError_t launch_mma_prefill(const GqaKP& kp, cudaStream_t st) {
 }  // namespace
 
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p) { return ws_layout(p).total; }
+size_t gqa_workspace_min_bytes(const b200ep_gqa_params& p) { return ws_layout(p).base; }
 
 // PagedAttention prompt chunks on the tensor-core prefill kernel: the caller has appended the new
 // k / v rows and written the rotated q rows into `out`.
@@ -1658,7 +1663,7 @@ int launch_gqa(const GqaArgs& a, cudaStream_t st) {
   B200EP_CHECK_ARG(p.bias_batch == 0 || a.bias, "GroupQueryAttention: attention_bias pointer missing");
   const int esz = dtype_size(a.dtype);
   const WsLayout wl = ws_layout(p);
-  B200EP_CHECK_ARG(a.workspace && a.workspace_bytes >= wl.total, "GroupQueryAttention: workspace too small");
+  B200EP_CHECK_ARG(a.workspace && a.workspace_bytes >= wl.base, "GroupQueryAttention: workspace too small");
 
   GqaKP kp{};
   kp.q = a.query;
@@ -1714,6 +1719,28 @@ int launch_gqa(const GqaArgs& a, cudaStream_t st) {
     else
       e = p.head_size == 64 ? launch_mma_decode<__nv_bfloat16, 64>(kp, sp, st)
                             : launch_mma_decode<__nv_bfloat16, 128>(kp, sp, st);
+  } else if (mma_prefill_path(p, a.dtype, esz) && aligned && a.workspace_bytes >= wl.total &&
+             gqa_umma_supported(p.batch, p.kv_heads, p.head_size, p.cap, a.dtype)) {
+    // tcgen05 prompt kernel: append (rotate q into the workspace, k / v into the cache), then it
+    const int warps = 4;
+    const int items = kp.B * kp.S * (kp.H + kp.HK);
+    e = launch_k(a.dtype == kF16 ? gqa_append_kernel<__half> : gqa_append_kernel<__nv_bfloat16>,
+                 dim3(div_up(items, warps)), dim3(warps * 32), warps * kp.D * sizeof(float), st, kp);
+    if (e == cudaSuccess) {
+      UmmaAttnArgs u{};
+      u.qrot = kp.qrot;
+      u.kv_k = a.kv_key;
+      u.kv_v = a.kv_value;
+      u.vt = ws + wl.vt;
+      u.seqlens = a.seqlens_k;
+      u.out = a.out;
+      u.err = kp.err;
+      u.B = kp.B, u.S = kp.S, u.H = kp.H, u.HK = kp.HK, u.G = kp.G, u.cap = kp.cap, u.max_seq = kp.max_seq;
+      u.do_rotary = kp.do_rotary, u.local_window = kp.local_window, u.lt = (int)gqa_umma_lt(p.cap);
+      u.dtype = a.dtype;
+      u.scale_log2 = kp.scale_log2;
+      e = launch_gqa_umma_prefill(u, st);
+    }
   } else if (mma_prefill_path(p, a.dtype, esz) && aligned) {
     if (a.dtype == kF16)
       e = p.head_size == 64 ? launch_mma_prefill<__half, 64>(kp, st) : launch_mma_prefill<__half, 128>(kp, st);

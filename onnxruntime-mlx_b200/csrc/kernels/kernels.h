@@ -62,6 +62,28 @@ struct GqaArgs {
   size_t workspace_bytes;
 };
 size_t gqa_workspace_bytes(const b200ep_gqa_params& p);
+// the workspace without the optional transposed-value region of the tensor-core prompt kernel
+// (a smaller workspace runs prompts on the mma.sync kernel)
+size_t gqa_workspace_min_bytes(const b200ep_gqa_params& p);
+
+// Tensor-core (tcgen05) prompt attention for head size 128 (gqa_umma.cu), launched after the
+// append kernel: qrot = rotated query rows (fp32, rounded through the I/O type), vt = a workspace
+// of gqa_umma_vt_bytes for the transposed value rows, lt = gqa_umma_lt(cap) keys per V^T row.
+struct UmmaAttnArgs {
+  const float* qrot;
+  const void* kv_k;
+  const void* kv_v;
+  void* vt;
+  const int32_t* seqlens;
+  void* out;
+  struct DeviceErrorSlot* err;
+  int B, S, H, HK, G, cap, max_seq, do_rotary, local_window, lt, dtype;
+  float scale_log2;
+};
+int64_t gqa_umma_lt(int64_t cap);
+size_t gqa_umma_vt_bytes(int64_t batch, int64_t kv_heads, int64_t cap);
+bool gqa_umma_supported(int64_t batch, int64_t kv_heads, int64_t head_size, int64_t cap, int dtype);
+cudaError_t launch_gqa_umma_prefill(const UmmaAttnArgs& a, cudaStream_t st);
 // Validates geometry (returns a B200EP_* status and message via set_error) and launches.
 int launch_gqa(const GqaArgs& a, cudaStream_t st);
 

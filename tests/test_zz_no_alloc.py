@@ -93,3 +93,56 @@ def test_noalloc_gqa_refuses_oversize_scratch():
             ctypes.byref(p), _p(dummy), _p(dummy), _p(dummy), _p(dummy), _p(dummy), _p(dummy), None, None, None,
             None, None, _p(dummy), 10, None))
     assert ei.value.status == 2  # B200EP_ERANGE
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_noalloc_gqa_prompt_matches_oracle(dt):
+    """A prompt (S = 64 after 100 cached rows, 32 / 8 heads of 128) whose workspace fits the fixed
+    scratch: the no-alloc entry against the oracle of the GroupQueryAttention semantics, the KV
+    append bit-exact."""
+    from oracle import oracle
+
+    L, ops = _lib()
+    rng = np.random.default_rng(7 if dt == "f16" else 8)
+    B, S, H, HK, D, past = 1, 64, 32, 8, 128, 100
+    cap = past + S + 4
+    q = rng.standard_normal((B, S, H * D)).astype(np.float32)
+    k = rng.standard_normal((B, S, HK * D)).astype(np.float32)
+    v = rng.standard_normal((B, S, HK * D)).astype(np.float32)
+    kc = np.zeros((B, HK, cap, D), np.float32)
+    vc = np.zeros((B, HK, cap, D), np.float32)
+    kc[:, :, :past] = rng.standard_normal((B, HK, past, D))
+    vc[:, :, :past] = rng.standard_normal((B, HK, past, D))
+    half = D // 2
+    ang = np.arange(cap + 8)[:, None] * (1.0 / (10000.0 ** (np.arange(half) / half)))[None, :]
+    cos, sin = np.cos(ang), np.sin(ang)
+    seqlens = np.full((B,), past + S - 1, np.int32)
+    if dt == "f16":
+        args = [x.astype(np.float16) for x in (q, k, v, kc, vc, cos, sin)]
+        dev = [torch.from_numpy(x).cuda() for x in args]
+        code, tol = 10, TOL
+    else:
+        args = [oracle.f32_to_bf16_bits(x.astype(np.float32)) for x in (q, k, v, kc, vc, cos, sin)]
+        dev = [torch.from_numpy(x).cuda().view(torch.bfloat16) for x in args]
+        code, tol = 16, TOL
+    want, wk, wv = oracle.gqa(args[0], args[1], args[2], args[3].copy(), args[4].copy(), seqlens, args[5], args[6],
+                              num_heads=H, kv_heads=HK, shared_buffer=True, dtype="bf16" if dt == "bf16" else None)
+    p = ops.gqa_params(batch=B, seq=S, num_heads=H, kv_heads=HK, head_size=D, cap=cap, cos_cache=dev[5])
+    out = torch.empty(B, S, H * D, dtype=dev[0].dtype, device="cuda")
+    sl = torch.from_numpy(seqlens).cuda()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ops.check(L.b200ep_group_query_attention_noalloc(
+        ctypes.byref(p), _p(dev[0]), _p(dev[1]), _p(dev[2]), _p(dev[3]), _p(dev[4]), _p(sl), _p(dev[5]), _p(dev[6]),
+        None, None, None, _p(out), code, stream))
+    torch.cuda.synchronize()
+    if dt == "f16":
+        got = out.float().cpu().numpy()
+        np.testing.assert_allclose(got, want.astype(np.float32), **tol)
+        np.testing.assert_array_equal(dev[3].cpu().numpy(), wk)
+        np.testing.assert_array_equal(dev[4].cpu().numpy(), wv)
+    else:
+        got = out.float().cpu().numpy()
+        np.testing.assert_allclose(got, oracle.bf16_bits_to_f32(want), **tol)
+        np.testing.assert_array_equal(dev[3].view(torch.int16).cpu().numpy().view(np.uint16), wk)
+    code_e, _ = ops.device_error(clear=True)
+    assert code_e == 0
