@@ -400,15 +400,24 @@ gqa_umma_prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
         // this warp's 32 keys of the row of S_j, scaled to the base-2 exponent domain
         uint32_t v[32];
         tmem_ld32(lbase + (uint32_t)(s * 128 + c * 32), v);
-        const bool full = valid && key0 >= lo && key0 + 31 <= pos;  // no per-key mask
+        // every key of the warp's 32 x 32 block visible (all but the diagonal and window edges):
+        // raw scores, scaled inside the exponent; otherwise scaled scores with -inf where masked
+        const bool wfull = __all_sync(0xffffffffu, valid && key0 >= lo && key0 + 31 <= pos && a.scale_log2 > 0.f);
         float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (wfull) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = key0 + e;
-          const float x = __uint_as_float(v[e]) * a.scale_log2;
-          const bool vis = full || (valid && key >= lo && key <= pos);
-          v[e] = __float_as_uint(vis ? x : -INFINITY);
-          mxs[e & 3] = fmaxf(mxs[e & 3], vis ? x : -INFINITY);
+          for (int e = 0; e < 32; ++e) mxs[e & 3] = fmaxf(mxs[e & 3], __uint_as_float(v[e]));
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mxs[u] *= a.scale_log2;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = key0 + e;
+            const float x = __uint_as_float(v[e]) * a.scale_log2;
+            const bool vis = valid && key >= lo && key <= pos;
+            v[e] = __float_as_uint(vis ? x : -INFINITY);
+            mxs[e & 3] = fmaxf(mxs[e & 3], vis ? x : -INFINITY);
+          }
         }
         float part[4];
         exchange4(384u + (uint32_t)((j & 1) * 4), fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])), part);
@@ -436,12 +445,22 @@ gqa_umma_prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
         const float mr = m_ref == -INFINITY ? 0.f : m_ref;
         float pss[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[16];
+        if (wfull) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2(__uint_as_float(v[e]) - mr);  // -inf (masked) -> 0
-          const float p1 = ex2(__uint_as_float(v[e + 1]) - mr);
-          pss[(e >> 1) & 3] += p0 + p1;
-          pk[e >> 1] = pack_pair<T>(p0, p1);
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = ex2(fmaf(__uint_as_float(v[e]), a.scale_log2, -mr));
+            const float p1 = ex2(fmaf(__uint_as_float(v[e + 1]), a.scale_log2, -mr));
+            pss[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_pair<T>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = ex2(__uint_as_float(v[e]) - mr);  // -inf (masked) -> 0
+            const float p1 = ex2(__uint_as_float(v[e + 1]) - mr);
+            pss[(e >> 1) & 3] += p0 + p1;
+            pk[e >> 1] = pack_pair<T>(p0, p1);
+          }
         }
         unsigned char* pb = sm + USmem::kP + ((j & 1) * 2 + (c >> 1)) * USmem::kBox;
 #pragma unroll
