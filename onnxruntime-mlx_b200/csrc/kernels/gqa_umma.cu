@@ -160,6 +160,11 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // warp-uniform bounded wait
 __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t phase) {
   return __all_sync(0xffffffffu, mbar_wait(bar, phase));
@@ -448,8 +453,10 @@ gqa_umma_prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
         if (wfull) {
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(v[e]), a.scale_log2, -mr));
-            const float p1 = ex2(fmaf(__uint_as_float(v[e + 1]), a.scale_log2, -mr));
+            const float x0 = fmaf(__uint_as_float(v[e]), a.scale_log2, -mr);
+            const float x1 = fmaf(__uint_as_float(v[e + 1]), a.scale_log2, -mr);
+            const float p0 = ex2(x0);
+            const float p1 = ex2(x1);
             pss[(e >> 1) & 3] += p0 + p1;
             pk[e >> 1] = pack_pair<T>(p0, p1);
           }
@@ -462,11 +469,10 @@ gqa_umma_prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_c
             pk[e >> 1] = pack_pair<T>(p0, p1);
           }
         }
-        unsigned char* pb = sm + USmem::kP + ((j & 1) * 2 + (c >> 1)) * USmem::kBox;
+        const uint32_t pb = smem_u32(sm + USmem::kP + ((j & 1) * 2 + (c >> 1)) * USmem::kBox);
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(pb + sw128_off(r, (c & 1) * 32 + u * 8)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          sts128(pb + sw128_off(r, (c & 1) * 32 + u * 8), make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
         l += (pss[0] + pss[1]) + (pss[2] + pss[3]);  // this warp's keys; summed across warps at the end
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
