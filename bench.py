@@ -1060,7 +1060,7 @@ def main():
     ap.add_argument("--tp-attention", default="auto", choices=["auto", "sharded", "replicated"],
                     help="tensor parallel: attention sharded by KV head (two all-reduces per layer) or run in "
                          "full on every rank (one all-reduce per layer, after the FFN); auto = the faster form "
-                         "measured for the model (replicated for the 8B shape, sharded for the 70B shape)")
+                         "measured at 2 GPUs (replicated for both the 8B and the 70B shape)")
     ap.add_argument("--kernel-only", nargs="?", const="gemv",
                     choices=["gemv", "gemv-shapes", "gqa", "gemm", "paged", "c1"],
                     help="time one kernel alone (gemv: the roofline leg; gemv-shapes: every decode projection of "
@@ -1072,7 +1072,7 @@ def main():
     args.warmup = max(args.warmup, 3)
     global MODEL, PROMPT, LAYERS, TP_ATTENTION
     MODEL = args.model
-    TP_ATTENTION = args.tp_attention if args.tp_attention != "auto" else ("replicated" if MODEL == "8b" else "sharded")
+    TP_ATTENTION = args.tp_attention if args.tp_attention != "auto" else "replicated"
     LAYERS = args.layers
     PROMPT = args.prompt or (2048 if MODEL == "70b" else 1024)
 

@@ -103,7 +103,7 @@ def _rank_main(rank, world, port, q, shape, tp_attention):
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("shape,tp_attention", [("small", "sharded"), ("70b-layers", "sharded"),
-                                                ("small", "replicated")])
+                                                ("small", "replicated"), ("70b-layers", "replicated")])
 def test_tp2_decoder_matches_oracle(shape, tp_attention):
     """Two ranks against the oracle of the unsharded graph.  tp_attention = "replicated" runs attention
     in full on every rank (one all-reduce per layer, after the FFN)."""
