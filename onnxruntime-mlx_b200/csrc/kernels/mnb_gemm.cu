@@ -499,8 +499,22 @@ cudaError_t gemm_b(const void* A, const MnbPacked& p, void* Y, int64_t M, cudaSt
 
 }  // namespace
 
+// Rows from which the tcgen05 GEMM takes over from the GEMV (which runs 16-row chunks as grid rows,
+// each re-streaming the weights).  Measured on B200 (fp16, block 32): at 24 and 32 rows the
+// chunked GEMV is faster at every Llama-3-8B / 70B projection shape (down_proj K 14336: 58 us
+// against 174 us, whose 32 weight tiles under-fill the GEMM's grid), at 48 rows the two are mixed,
+// at 64 the GEMM wins.  ONNXRUNTIME_EP_B200_GEMM_MIN_ROWS overrides it (at least 17).
+int64_t gemm_min_rows() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("ONNXRUNTIME_EP_B200_GEMM_MIN_ROWS");
+    const long long n = e ? std::atoll(e) : 0;
+    return n > 16 ? (int64_t)n : (int64_t)33;
+  }();
+  return v;
+}
+
 bool mnb_gemm_supported(int64_t M, int64_t K, const void* A) {
-  return M > 16 && K % 16 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 && encode_fn() != nullptr;
+  return M >= gemm_min_rows() && K % 16 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 && encode_fn() != nullptr;
 }
 
 cudaError_t launch_mnb_gemm(const void* A, const MnbPacked& p, void* Y, int dtype, int64_t M, cudaStream_t st) {
