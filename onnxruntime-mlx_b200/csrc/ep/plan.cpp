@@ -517,6 +517,63 @@ void Plan::fuse_swiglu() {
   }
 }
 
+// The fused gate/up GEMV followed by SiLU(gate) * up (after tensor-parallel slicing, before the
+// upload): reorder the weight rows so that every 16-row tile holds 8 gate rows and the 8 matching up
+// rows, and let the GEMV's tile merge write h = SiLU(gate) * up itself.  The separate SiLU step
+// (or the down projection's SiLU prologue, which re-read the 2F-wide gate/up output in every CTA)
+// goes away.  Only for weights the tensor-core GEMV takes (the other paths still work through the
+// workspace and the interleaved SiLU kernel).
+void Plan::fuse_swiglu_epilogue() {
+  Uses u = uses_of(steps_, slots_.size());
+  for (int ai = 0; ai < (int)steps_.size(); ++ai) {
+    const Step a = steps_[ai];
+    if (a.kind != StepKind::kSiluMul) continue;
+    const int gu = a.in[0], pi = u.producer[gu];
+    if (pi < 0 || u.users[gu].size() != 1 || slots_[gu].kind != Slot::kTemp) continue;
+    Step& m = steps_[pi];
+    const int64_t F = a.N;
+    if (m.kind != StepKind::kMnb || m.N != 2 * F || F % 8 || m.in.empty() || m.in[0] < 0) continue;
+    if (!mnb_mma_supported(slots_[m.in[0]].dtype, m.bits, m.block, m.K)) continue;
+    bool have = true;
+    for (int w : {m.wB, m.wS, m.wZ})
+      if (w >= 0) have &= pending_consts_.count(w) && (int64_t)pending_consts_[w]->bytes.size() % m.N == 0;
+    if (!have) continue;
+    // row 16 i + r <- gate row 8 i + r, row 16 i + 8 + r <- up row 8 i + r (r < 8); up rows are F .. 2F
+    auto interleave = [&](int id, const std::string& nm) {
+      const Initializer& in = *pending_consts_[id];
+      const size_t rb = in.bytes.size() / (size_t)m.N;
+      auto out = std::make_shared<Initializer>();
+      out->name = nm;
+      out->dtype = in.dtype;
+      out->shape = in.shape;
+      out->bytes.resize(in.bytes.size());
+      for (int64_t i = 0; i < F / 8; ++i)
+        for (int r = 0; r < 16; ++r) {
+          const int64_t src = r < 8 ? 8 * i + r : F + 8 * i + (r - 8);
+          memcpy(out->bytes.data() + (size_t)(16 * i + r) * rb, in.bytes.data() + (size_t)src * rb, rb);
+        }
+      const int nid = slot_of(nm);
+      slots_[nid].kind = Slot::kConst;
+      slots_[nid].dtype = out->dtype;
+      slots_[nid].cshape = out->shape;
+      pending_consts_[nid] = out;
+      return nid;
+    };
+    m.wB = interleave(m.wB, m.name + "#B#swiglu");
+    m.wS = interleave(m.wS, m.name + "#scales#swiglu");
+    if (m.wZ >= 0) m.wZ = interleave(m.wZ, m.name + "#zp#swiglu");
+    m.swiglu = true;
+    ++stats_.swiglu_epilogue;
+    m.out = {a.out[0]};
+    const int ws = slot_of(m.name + "#gate_up_interleaved");
+    slots_[ws].dtype = slots_[gu].dtype;
+    m.ws_slot = ws;
+    steps_.erase(steps_.begin() + ai);
+    u = uses_of(steps_, slots_.size());
+    --ai;
+  }
+}
+
 int Plan::upload_constants(const Graph& g, std::string* err) {
   // fp16 / bf16 int4 MatMulNBits: upload the ORT-layout weight once, repack it on the device into
   // the tensor-core operand order, keep only the packed form
@@ -662,6 +719,8 @@ std::unique_ptr<Plan> Plan::compile_impl(const Graph& g, const std::vector<int>&
   }
   if (cfg.tp && p->shard_for_tp(err)) return nullptr;
   if (cfg.host_only) return p;
+  if (cfg.fuse && !env_on("ONNXRUNTIME_EP_B200_NO_FUSION") && !env_on("ONNXRUNTIME_EP_B200_NO_SWIGLU_EPILOGUE"))
+    p->fuse_swiglu_epilogue();
   if (p->upload_constants(g, err)) return nullptr;
   if (cfg.fuse) {
     p->fuse_prologues();
@@ -1201,8 +1260,9 @@ int Plan::infer(std::vector<Slot>& S, std::string* err) const {
         if (a.shape.empty() || a.shape.back() != st.K)
           return fail("MatMulNBits " + st.name + ": input last dim " + shape_str(a.shape) + " != K=" + std::to_string(st.K));
         auto sh = a.shape;
-        sh.back() = st.N;
+        sh.back() = st.swiglu ? st.N / 2 : st.N;
         S[st.out[0]].shape = sh;
+        if (st.swiglu && st.ws_slot >= 0) S[st.ws_slot].shape = {a.numel() / st.K * st.N};
         break;
       }
       case StepKind::kGqa: {
@@ -1360,6 +1420,7 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
             pro.gamma = s.pro_gamma >= 0 ? S[s.pro_gamma].ptr : nullptr;
             pro.residual = s.pro_res >= 0 ? S[s.pro_res].ptr : nullptr;
             pro.eps = s.pro_eps;
+            pro.swiglu = s.swiglu ? 1 : 0;
             if (s.pro_ar && ar_fused(M, s.K, s.block)) pro.ar = make_ar(*cfg_.tp);
             bool aligned = true;
             for (const void* q : {pro.x, pro.skip, pro.gamma, (const void*)pro.residual})
@@ -1377,16 +1438,25 @@ int Plan::launch_steps(const std::vector<Slot>& S, Program& prog, cudaStream_t s
             }
             if (e != cudaSuccess) break;
           }
-          if (!out_ar && mnb_gemm_supported(M, s.K, a.ptr))
-            e = launch_mnb_gemm(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st);  // prefill rows
-          else
-            e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st, nullptr, out_ar);
+          MnbPro epi;  // no prologue; the SwiGLU epilogue when the rows are interleaved
+          epi.swiglu = s.swiglu ? 1 : 0;
+          if (!out_ar && mnb_gemm_supported(M, s.K, a.ptr)) {
+            // prefill rows: the GEMM writes gate and up (interleaved) into the workspace first
+            void* y = s.swiglu ? S[s.ws_slot].ptr : S[s.out[0]].ptr;
+            e = launch_mnb_gemm(a.ptr, pk, y, a.dtype, M, st);
+            if (e == cudaSuccess && s.swiglu) e = launch_silu_mul_interleaved(y, S[s.out[0]].ptr, a.dtype, M, s.N / 2, st);
+          } else {
+            e = launch_mnb_packed(a.ptr, pk, S[s.out[0]].ptr, a.dtype, M, st, &epi, out_ar);
+          }
           break;
         }
+        void* y = s.swiglu ? S[s.ws_slot].ptr : S[s.out[0]].ptr;
         MnbArgs m{a.ptr, static_cast<const uint8_t*>(S[s.wB].ptr), S[s.wS].ptr,
                   s.wZ >= 0 ? static_cast<const uint8_t*>(S[s.wZ].ptr) : nullptr,
-                  S[s.out[0]].ptr, a.dtype, a.numel() / s.K, s.N, s.K, s.bits, s.block};
+                  y, a.dtype, a.numel() / s.K, s.N, s.K, s.bits, s.block};
         e = launch_matmulnbits(m, st);
+        if (e == cudaSuccess && s.swiglu)
+          e = launch_silu_mul_interleaved(y, S[s.out[0]].ptr, a.dtype, a.numel() / s.K, s.N / 2, st);
         break;
       }
       case StepKind::kGqa: {
@@ -2149,7 +2219,8 @@ std::string Plan::describe() const {
   std::ostringstream o;
   o << "{\"nodes\":" << stats_.nodes << ",\"steps\":" << steps_.size() << ",\"fused_qkv\":" << stats_.fused_qkv
     << ",\"fused_swiglu\":" << stats_.fused_swiglu << ",\"fused_norm\":" << stats_.fused_norm
-    << ",\"fused_act\":" << stats_.fused_act << ",\"peer_allreduce\":" << stats_.peer_allreduce
+    << ",\"fused_act\":" << stats_.fused_act << ",\"swiglu_epilogue\":" << stats_.swiglu_epilogue
+    << ",\"peer_allreduce\":" << stats_.peer_allreduce
     << ",\"weight_bytes\":" << stats_.weight_bytes
     << ",\"runs\":" << stats_.runs << ",\"graph_captures\":" << stats_.graph_captures
     << ",\"graph_replays\":" << stats_.graph_replays;

@@ -149,6 +149,10 @@ struct Step {
   int idx_rank = 0, layout = 0;
   // MatMulNBits weights prepacked for the tensor-core path (fp16/bf16, int4)
   bool prepacked = false;
+  // fused gate/up whose weight rows are interleaved 8 gate / 8 up per 16-row tile: the step writes
+  // SiLU(gate) * up (N / 2 columns); paths that cannot (the GEMM, the SIMT kernel) write both into
+  // ws_slot and a separate kernel applies it
+  bool swiglu = false;
   std::shared_ptr<DevMem> pk_w;
   // producer of in[0] folded into the GEMV's activation staging (MnbProKind); the standalone
   // producer still runs into in[0] when the rows do not fit the staging area
@@ -164,7 +168,7 @@ struct Step {
 };
 
 struct PlanStats {
-  int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0, fused_norm = 0, fused_act = 0;
+  int nodes = 0, steps = 0, fused_qkv = 0, fused_swiglu = 0, fused_norm = 0, fused_act = 0, swiglu_epilogue = 0;
   int64_t weight_bytes = 0;
   int64_t runs = 0, graph_replays = 0, graph_captures = 0;
   int peer_allreduce = 0;
@@ -200,6 +204,7 @@ class Plan {
   void fuse_swiglu();
   void fuse_prologues();
   void fuse_peer_allreduce();
+  void fuse_swiglu_epilogue();
   bool ar_fused(int64_t M, int64_t hidden, int cons_block) const;
   int shard_for_tp(std::string* err);
   int infer(std::vector<Slot>& slots, std::string* err) const;

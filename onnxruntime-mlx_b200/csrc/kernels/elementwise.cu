@@ -51,6 +51,22 @@ __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ h, int
   }
 }
 
+// gu: [rows, 2n] with the gate / up columns interleaved in groups of 8 (columns 16 g .. 16 g + 7 are
+// gate 8 g .. 8 g + 7, the next 8 the matching up values); h = gate * sigmoid(gate) * up
+template <typename T>
+__global__ void silu_mul_interleaved_kernel(const T* __restrict__ gu, T* __restrict__ h, int64_t rows, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t total = rows * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n, c = i - r * n;
+    const int64_t src = r * 2 * n + (c >> 3) * 16 + (c & 7);
+    const float g = to_f<T>(gu[src]);
+    const float u = to_f<T>(gu[src + 8]);
+    h[i] = from_f<T>(g / (1.f + __expf(-g)) * u);
+  }
+}
+
 template <typename TI, typename TO>
 __global__ void cast_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t n) {
   pdl_wait();
@@ -166,6 +182,16 @@ cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, in
     using T = decltype(tag);
     return launch_k(silu_mul_kernel<T>, dim3(grid_for(rows * n)), dim3(256), 0, st, static_cast<const T*>(gu),
                     static_cast<T*>(h), rows, n);
+  });
+}
+
+cudaError_t launch_silu_mul_interleaved(const void* gu, void* h, int dtype, int64_t rows, int64_t n,
+                                        cudaStream_t st) {
+  if (rows * n == 0) return cudaSuccess;
+  return by_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_k(silu_mul_interleaved_kernel<T>, dim3(grid_for(rows * n)), dim3(256), 0, st,
+                    static_cast<const T*>(gu), static_cast<T*>(h), rows, n);
   });
 }
 

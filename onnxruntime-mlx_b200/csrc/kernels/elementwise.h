@@ -24,6 +24,9 @@ cudaError_t launch_binary(const void* a, const void* b, void* y, int dtype, cons
 cudaError_t launch_sigmoid(const void* x, void* y, int dtype, int64_t n, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* gu, void* h, int dtype, int64_t rows, int64_t n, cudaStream_t st);
 cudaError_t launch_cast(const void* x, int in_dt, void* y, int out_dt, int64_t n, cudaStream_t st);
+// SiLU(gate) * up over gate / up columns interleaved in groups of 8 ([rows, 2n] -> [rows, n])
+cudaError_t launch_silu_mul_interleaved(const void* gu, void* h, int dtype, int64_t rows, int64_t n,
+                                        cudaStream_t st);
 
 // Integer glue (index_ops.cu): exact int32 / int64 arithmetic for the attention-mask and
 // shape-vector chains of exported decoders.

@@ -854,14 +854,25 @@ mnb_tma_kernel(const T* __restrict__ A, const uint8_t* __restrict__ recs, T* __r
       for (int tid = threadIdx.x; tid < 256; tid += NC * 32) {
         const int row = tid & 15, col = tid >> 4;
         const int m = m0 + col, n = t * 16 + row;
-        if (col < 8 * NT && m < M && n < N) {
+        const bool ok = col < 8 * NT && m < M && n < N;
+        float v = 0.f;
+        if (ok) {
           const int nt = col >> 3, cc = col & 7;
           const int e = (row >= 8 ? 2 : 0) + (cc & 1);
           const int ln = (row & 7) * 4 + (cc >> 1);
-          float v = 0.f;
 #pragma unroll
           for (int w = 0; w < NC; ++w) v += rb[((w * NT + nt) * 4 + e) * 32 + ln];
-          Y[(size_t)m * N + n] = from_f<T>(v);
+        }
+        if (!pro.swiglu) {
+          if (ok) Y[(size_t)m * N + n] = from_f<T>(v);
+        } else {
+          // rows 8..15 of the tile are the up projections of rows 0..7 (lane + 8 of this warp);
+          // both rounded to T first, as the separate SiLU * up kernel reads them
+          const float u = __shfl_down_sync(0xffffffffu, v, 8);
+          if (ok && row < 8) {
+            const float gf = round_through<T>(v), uf = round_through<T>(u);
+            Y[(size_t)m * (N / 2) + t * 8 + row] = from_f<T>(gf / (1.f + __expf(-gf)) * uf);
+          }
         }
       }
       ++tp;

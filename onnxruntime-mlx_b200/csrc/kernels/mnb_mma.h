@@ -51,6 +51,9 @@ struct MnbPro {
   void* residual = nullptr;
   float eps = 0.f;
   MnbAr ar;  // world > 0: x is the sum of the mailbox slots (kProSkipRms only)
+  // epilogue: the weight rows are interleaved 8 gate / 8 up per 16-row tile (N = 2 F); the GEMV
+  // writes h = SiLU(gate) * up, F outputs per row, instead of the 2 F projections
+  int swiglu = 0;
 };
 
 int mnb_record_bytes(int block);

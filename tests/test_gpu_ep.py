@@ -217,8 +217,9 @@ def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
     sess_d = ep_mod.Session(build_decoder(cfg, batch=B, seq=1, cap=cap, weights_out=Wd))
     d = json.loads(sess_d.parts[0].describe())
     assert d["fused_qkv"] == cfg.layers and d["fused_swiglu"] == cfg.layers
-    # every norm and SiLU*up folds into the staging of the GEMV that consumes it
-    assert d["fused_norm"] == 2 * cfg.layers + 1 and d["fused_act"] == cfg.layers
+    # every norm folds into the staging of the GEMV that consumes it; SiLU(gate) * up is written by
+    # the gate/up GEMV's epilogue (its weight rows interleaved), so the down projection stages plainly
+    assert d["fused_norm"] == 2 * cfg.layers + 1 and d["swiglu_epilogue"] == cfg.layers and d["fused_act"] == 0
     rng = np.random.default_rng(7)
     kv_dev = [[torch.zeros(B, cfg.kv_heads, cap, cfg.head_dim, dtype=torch.float16, device="cuda") for _ in range(2)]
               for _ in range(cfg.layers)]
@@ -249,16 +250,13 @@ def test_small_decoder_prefill_and_decode_match_oracle(ep_mod, shape):
     f, o = feeds_for(ids, 0)
     got = sess_p.run(f, o)["logits"].float().cpu().numpy()
     want = oracle_decoder_step(cfg, Wp, ids, kv_ref, np.full(B, P - 1, np.int32)).astype(np.float32)
-    scale = np.abs(want).max()
-    np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2 * scale)
+    _compare_logits(got, want, "prefill")
     for t in range(steps):
         ids = rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64)
         f, o = feeds_for(ids, P + t)
         got = sess_d.run(f, o)["logits"].float().cpu().numpy()
         want = oracle_decoder_step(cfg, Wd, ids, kv_ref, np.full(B, P + t, np.int32)).astype(np.float32)
-        np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2 * np.abs(want).max())
-        # greedy next token agrees (top-1 of the logits)
-        assert (got.argmax(-1) == want.argmax(-1)).mean() >= 0.5
+        _compare_logits(got, want, f"decode step {t}")
     for i in range(cfg.layers):
         np.testing.assert_allclose(kv_dev[i][0].float().cpu().numpy()[:, :, :P + steps],
                                    kv_ref[i][0].astype(np.float32)[:, :, :P + steps], rtol=2e-2, atol=2e-2)
