@@ -19,10 +19,11 @@ full decode step per timed step (the reference implementation — Rust over MLX/
 on Linux, and ORT's CPU EP is not installed on this image).
 
 Multi-GPU (N > 1, one process per GPU under torchrun): by default one model sharded over the ranks
-(tensor parallel, strong scaling): q/k/v, gate/up and the vocabulary projection split by output rows
-(attention by KV head), o_proj / down_proj split by K blocks and followed by an all-reduce (peer
-memory for decode rows, NCCL for prompts), the logits all-gathered; every rank decodes the same
-tokens; value = tokens / max rank time.  The line also carries `tp_parity` (the sharded decoder's
+(tensor parallel, strong scaling): gate/up and the vocabulary projection split by output rows,
+down_proj split by K blocks and followed by one all-reduce per layer (peer memory for decode rows,
+NCCL for prompts), attention (q/k/v, GroupQueryAttention, o_proj) run in full on every rank
+(`--tp-attention sharded` splits it by KV head instead, with a second all-reduce after o_proj), the
+logits all-gathered; every rank decodes the same tokens; value = tokens / max rank time.  The line also carries `tp_parity` (the sharded decoder's
 logits against a one-GPU plan of the same graph, prompt + decode steps, compared on rank 0) and
 `replicas` (the same N GPUs as independent data-parallel replicas, weak scaling).  Every rank reads
 the library's device error word after the warm-up and after the timed region; a non-zero code fails
